@@ -1,0 +1,392 @@
+#!/usr/bin/env python3
+"""Benchmark of the COVE SpMV hot path on B200 (one process per GPU).
+
+Workload (default): the FEM-like 27-point stencil, 64^3 nodes x 3 DOF
+(n = 786,432, nnz = 61,731,000, fp64 values), x ~ U[-1,1] seed 1, planned with
+the joint value codec `auto` (-> BFP8 blocks + bf16 residual, gated at 1e-2
+on the canonical x).  One step = one SpMV y = A x on the dispatched route.
+
+With --gpus N > 1 (torchrun, one rank per GPU) the FEM grid grows to
+64 x 64 x 64N nodes, partitioned into z-slabs of 64 planes: every rank owns
+the same row count as the 1-GPU run (weak scaling), and a step is the NCCL
+x-halo exchange (one node plane to each neighbour) followed by the local
+SpMV.  `value` is the whole-job GFLOP/s (2 nnz_total / t).
+
+--workload lapl3d_cg runs the 3D 7-point Laplacian CG (strong scaling).
+
+Timing: W warm-up steps, then K steps bracketed by barrier + synchronize;
+each step's SpMV is timed with CUDA events on the launching stream and the
+L2 is flushed (a 256 MiB write) between steps, outside the event pair.
+`--impl reference` times the reference's own CPU SpMV (spmv_csr, OpenMP)
+on the same workload instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "cove-spmv_b200"))
+
+import numpy as np  # noqa: E402
+
+FEM = dict(nx=64, ny=64, nz=64, dof=3, seed=1)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def fem_partition(rank, world):
+    """Rows, window and generator arguments of one z-slab of the FEM grid."""
+    nx, ny, nzl, dof = FEM["nx"], FEM["ny"], FEM["nz"], FEM["dof"]
+    nz = nzl * world
+    plane = nx * ny * dof
+    row_begin = rank * nzl * plane
+    row_end = row_begin + nzl * plane
+    wb = max(0, row_begin - plane)
+    we = min(nz * plane, row_end + plane)
+    return dict(nx=nx, ny=ny, nz=nz, dof=dof, row_begin=row_begin, row_end=row_end,
+                window_begin=wb, window_len=we - wb)
+
+
+def cpu_reference_time(rows, cols, rp, ci, v, x, reps):
+    """The reference's spmv_csr (OpenMP) on this host; (best ms, threads, kind)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    if O.ref_available():
+        t = O.RefCsrTimer(rows, cols, rp, ci, v, x)
+        t.run(1)
+        _, ms = t.run(reps)
+        t.close()
+        return ms, O.ref_threads(), "reference"
+    best = 1e300
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.spmv_csr(rows, rp, ci, v, x)
+        best = min(best, (time.perf_counter() - t0) * 1e3)
+    return best, 1, "port"
+
+
+def run_reference_arm(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    part = fem_partition(0, 1)
+    import cove_b200 as cb
+
+    rows, n, rp, ci, v = cb.synth_fem27_rows(part["nx"], part["ny"], part["nz"], part["dof"],
+                                             FEM["seed"], part["row_begin"], part["row_end"], 0)
+    x = cb.synth_vector("uniform_pm1", n, seed=FEM["seed"])
+    nnz = int(ci.size)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    kind = "reference" if O.ref_available() else "port"
+    times = []
+    if kind == "reference":
+        t = O.RefCsrTimer(rows, n, rp, ci, v, x)
+        for _ in range(args.warmup):
+            t.run(1)
+        for _ in range(args.steps):
+            _, ms = t.run(1)
+            times.append(ms)
+        t.close()
+        cores = O.ref_threads()
+    else:
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            O.spmv_csr(rows, rp, ci, v, x)
+            if i >= args.warmup:
+                times.append((time.perf_counter() - t0) * 1e3)
+        cores = 1
+    ms = sum(times) / len(times)
+    gflops = 2.0 * nnz / (ms * 1e-3) / 1e9
+    line = {
+        "impl": "reference", "metric": "spmv_gflops", "value": round(gflops, 3),
+        "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "fem27_64^3x3 (n=786432, nnz=61731000)",
+                   "sample": "one full SpMV of the 1-GPU slab per step"},
+        "cpu_baseline": {"value": round(gflops, 3), "unit": "GFLOP/s", "cores": cores,
+                         "kind": kind,
+                         "sample": "structural::spmv_csr on the fem27 64^3x3 matrix, one SpMV per step"},
+        "e2e": {"value": round(gflops, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_fem(args):
+    import torch
+    import torch.distributed as dist
+
+    import cove_b200 as cb
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    part = fem_partition(rank, world)
+    rows, n, rp, ci, v = cb.synth_fem27_rows(part["nx"], part["ny"], part["nz"], part["dof"],
+                                             FEM["seed"], part["row_begin"], part["row_end"],
+                                             part["window_begin"])
+    wl = part["window_len"]
+    xg = cb.synth_vector("uniform_pm1", n, seed=FEM["seed"])
+    x_window = xg[part["window_begin"]: part["window_begin"] + wl].copy()
+    csr = cb.DeviceCsr.from_numpy(rows, wl, rp, ci, v, device=dev)
+    t0 = time.perf_counter()
+    plan = cb.Plan(csr, value_codec=args.codec, long_row_split=256)
+    build_s = time.perf_counter() - t0
+    del csr
+    info = plan.info
+    route = info.dispatched_route
+    nnz_local = int(info.nnz)
+
+    stream = torch.cuda.current_stream()
+    xw = torch.from_numpy(x_window).to(dev)
+    y = torch.empty(rows, dtype=torch.float64, device=dev)
+    D = None
+    if world > 1:
+        import ctypes as C
+
+        idb = cb.lib().cove_dist_id_bytes()
+        idbuf = np.zeros(idb, np.uint8)
+        if rank == 0:
+            cb.check(cb.lib().cove_dist_make_id(idbuf.ctypes.data_as(C.c_void_p)))
+        obj = [idbuf.tobytes()]
+        dist.broadcast_object_list(obj, src=0)
+        idbuf = np.frombuffer(obj[0], np.uint8).copy()
+        D = C.c_void_p()
+        arr = (C.c_void_p * 1)(plan.handle.value)
+        cb.check(cb.lib().cove_dist_create(rank, world, idbuf.ctypes.data_as(C.c_void_p), arr, 1,
+                                           n, part["row_begin"], part["row_end"],
+                                           part["window_begin"], wl, 120000, C.byref(D)))
+
+    def step(xbuf, ybuf):
+        if D is not None:
+            cb.check(cb.lib().cove_dist_spmv(D, C.c_void_p(xbuf.data_ptr()),
+                                             C.c_void_p(ybuf.data_ptr()),
+                                             C.c_void_p(stream.cuda_stream)))
+        else:
+            plan.spmv(xbuf, ybuf, stream=stream)
+
+    # parity check of this very plan against a CPU SpMV of the same rows
+    step(xw, y)
+    torch.cuda.synchronize()
+    import scipy.sparse as sp
+
+    A = sp.csr_matrix((v, ci, rp), shape=(rows, wl))
+    y_ref = A @ x_window
+    yh = y.cpu().numpy()
+    rel = float(np.abs(yh - y_ref).max() / max(np.abs(y_ref).max(), 1e-300))
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        step(xw, y)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    clk = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk.start()
+    time.sleep(0.3)
+    w0 = time.perf_counter()
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step(xw, y)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    if world > 1:
+        dist.barrier()
+    clocks = clk.stop()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    ms = sum(step_ms) / len(step_ms)
+    launches = plan.launches()
+
+    # end to end through the public C ABI with host buffers (pinned)
+    xh = torch.from_numpy(x_window).pin_memory()
+    yh_t = torch.empty(rows, dtype=torch.float64).pin_memory()
+    xd2 = torch.empty(wl, dtype=torch.float64, device=dev)
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        if D is None:
+            plan.spmv_host(xh.numpy(), yh_t.numpy(), stream=stream)
+        else:
+            xd2.copy_(xh, non_blocking=True)
+            step(xd2, y)
+            yh_t.copy_(y, non_blocking=True)
+            torch.cuda.synchronize()
+        if i >= args.warmup:
+            e2e_ms.append((time.perf_counter() - t0) * 1e3)
+
+    tot = torch.tensor([ms, float(np.mean(e2e_ms)), float(nnz_local), rel, wall],
+                       dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = tot.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = tot.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms_all, e2e_all, rel_all = float(mx[0]), float(mx[1]), float(mx[3])
+        nnz_total = float(sm[2])
+    else:
+        ms_all, e2e_all, rel_all, nnz_total = ms, float(np.mean(e2e_ms)), rel, float(nnz_local)
+
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        alg_bytes = int(info.algorithmic_bytes[route])
+        achieved = alg_bytes / (ms * 1e-3) / 1e9
+        gflops = 2.0 * nnz_total / (ms_all * 1e-3) / 1e9
+        e2e_gflops = 2.0 * nnz_total / (e2e_all * 1e-3) / 1e9
+        traffic = None
+        prof = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(prof):
+            try:
+                with open(prof) as f:
+                    t = json.load(f)
+                traffic = t.get("fem27_64", {}).get(cb.ROUTE_NAMES[route])
+            except Exception:
+                traffic = None
+        # the reference's CPU SpMV on the same matrix, bounded sample
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cms, cores, kind = cpu_reference_time(rows, wl, rp, ci, v, x_window, 5)
+            cpu = {"value": round(2.0 * nnz_local / (cms * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
+                   "cores": cores, "kind": kind,
+                   "sample": "best of 5 full SpMVs (structural::spmv_csr, OpenMP) of the same matrix"}
+        line = {
+            "metric": "spmv_gflops", "value": round(gflops, 3), "unit": "GFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_all, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64" if route in (0, 1, 2) else "f32 accumulate, f64 in/out",
+            "data": "synthetic",
+            "config": {"workload": f"fem27 {FEM['nx']}x{FEM['ny']}x{FEM['nz'] * world} nodes x3 dof"
+                                   f" ({'z-slab per rank, ' if world > 1 else ''}nnz={int(nnz_total)})",
+                       "route": cb.ROUTE_NAMES[route], "requested_codec": args.codec,
+                       "gate_rel_err": info.joint_rel_err, "gate_pass": bool(info.gate_pass),
+                       "l2": "flushed between steps (256 MiB write, outside the timed events)",
+                       "parallelism": f"row-block z-slabs x{world}, NCCL halo" if world > 1 else "1 GPU",
+                       "plan_build_s": round(build_s, 3), "kernel_slots": info.kernel_slots,
+                       "parity_rel_vs_cpu": rel_all},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
+                         "algorithmic_bytes": alg_bytes, "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_gflops, 3), "unit": "GFLOP/s",
+                    "h2d_bytes_per_step": wl * 8, "d2h_bytes_per_step": rows * 8},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if D is not None:
+        cb.lib().cove_dist_destroy(D)
+    plan.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="fem27", choices=["fem27"])
+    ap.add_argument("--codec", default="auto")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_fem(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,428 @@
+// cg.cu -- textbook CG over the fused SpMV, on one GPU or a row-block
+// partition across GPUs (one process per GPU, NCCL over NVLink).
+//
+// Recurrence of the reference's timed CG (structural/src/bench_cg_solve.cu:
+// 165-197): x0 = 0, r = p = b, rs = r.r; per iteration Ap = A p,
+// alpha = rs / (p.Ap) (0 if p.Ap == 0), x += alpha p, r -= alpha Ap,
+// rs' = r.r, beta = rs'/rs (0 if rs == 0), p = r + beta p.
+//
+// B200 layout: alpha and beta never leave the device (the reference reads
+// every dot product back to the host, two syncs per iteration).  Dots are
+// two-stage deterministic reductions (fixed grid, per-CTA partials, one
+// final CTA).  On a partition each dot's partial sum is allreduced with
+// ncclAllReduce on the compute stream, and the SpMV's x window gets its halo
+// with ncclSend/ncclRecv from the neighbouring ranks first.
+#include "cove_plan.cuh"
+
+#include <nccl.h>
+
+#include <chrono>
+#include <thread>
+#include <vector>
+
+namespace cove {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kDotCtas = 148 * 4;
+
+// partial sums of a . b over a fixed grid; partial[blockIdx.x]
+__global__ void dot_partial_kernel(int64_t n, const double* __restrict__ a,
+                                   const double* __restrict__ b, double* __restrict__ partial) {
+    double s = 0.0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        s += a[i] * b[i];
+    __shared__ double sh[kThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < kThreads / 32; ++w) t += sh[w];
+        partial[blockIdx.x] = t;
+    }
+}
+
+__global__ void dot_final_kernel(const double* __restrict__ partial, int m,
+                                 double* __restrict__ out) {
+    __shared__ double sh[kThreads];
+    double s = 0.0;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) s += partial[i];
+    sh[threadIdx.x] = s;
+    __syncthreads();
+    for (int o = kThreads / 2; o > 0; o >>= 1) {
+        if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *out = sh[0];
+}
+
+// x += alpha p; r -= alpha Ap; partial of r.r   (alpha = rs / pAp on device)
+__global__ void cg_update_kernel(int64_t n, const double* __restrict__ scal, int rs_slot,
+                                 const double* __restrict__ p, const double* __restrict__ ap,
+                                 double* __restrict__ x, double* __restrict__ r,
+                                 double* __restrict__ partial) {
+    const double rs = scal[rs_slot];
+    const double pap = scal[2];
+    const double alpha = pap != 0.0 ? rs / pap : 0.0;
+    double s = 0.0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        x[i] += alpha * p[i];
+        const double ri = r[i] - alpha * ap[i];
+        r[i] = ri;
+        s += ri * ri;
+    }
+    __shared__ double sh[kThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < kThreads / 32; ++w) t += sh[w];
+        partial[blockIdx.x] = t;
+    }
+}
+
+// p = r + beta p, beta = rs_new / rs
+__global__ void cg_p_kernel(int64_t n, const double* __restrict__ scal, int rs_slot, int new_slot,
+                            const double* __restrict__ r, double* __restrict__ p) {
+    const double rs = scal[rs_slot];
+    const double beta = rs != 0.0 ? scal[new_slot] / rs : 0.0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        p[i] = r[i] + beta * p[i];
+}
+
+inline void nccl_ok(ncclResult_t r, const char* what) {
+    if (r != ncclSuccess && r != ncclInProgress) {
+        COVE_THROW(COVE_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+    }
+}
+
+void wait_comm_ready(ncclComm_t comm, int timeout_ms);
+
+}  // namespace
+}  // namespace cove
+
+using namespace cove;
+
+struct cove_dist {
+    int rank = 0, world = 1;
+    ncclComm_t comm = nullptr;
+    std::vector<cove_plan*> plans;
+    int64_t global_rows = 0, row_begin = 0, row_end = 0, wb = 0, wl = 0;
+    int timeout_ms = 60000;
+    struct Xfer {
+        int peer;
+        int64_t send_off, send_n, recv_off, recv_n;  // offsets into this rank's window
+    };
+    std::vector<Xfer> xfers;
+};
+
+namespace cove {
+namespace {
+
+void wait_comm_ready(ncclComm_t comm, int timeout_ms) {
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        ncclResult_t st = ncclSuccess;
+        nccl_ok(ncclCommGetAsyncError(comm, &st), "ncclCommGetAsyncError");
+        if (st == ncclSuccess) return;
+        if (st != ncclInProgress) {
+            ncclCommAbort(comm);
+            COVE_THROW(COVE_ERR_NCCL, std::string("NCCL communicator error: ") + ncclGetErrorString(st));
+        }
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                            std::chrono::steady_clock::now() - t0).count();
+        if (ms > timeout_ms) {
+            ncclCommAbort(comm);
+            COVE_THROW(COVE_ERR_TIMEOUT, "NCCL communicator did not become ready in time");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+// Wait for the stream with a host deadline; on timeout or an asynchronous
+// NCCL error the communicator is aborted so no rank waits forever.
+void wait_stream(cove_dist* d, cudaStream_t s) {
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        const cudaError_t q = cudaStreamQuery(s);
+        if (q == cudaSuccess) return;
+        if (q != cudaErrorNotReady) CUDA_OK(q);
+        if (d && d->comm) {
+            ncclResult_t st = ncclSuccess;
+            ncclCommGetAsyncError(d->comm, &st);
+            if (st != ncclSuccess && st != ncclInProgress) {
+                ncclCommAbort(d->comm);
+                d->comm = nullptr;
+                COVE_THROW(COVE_ERR_NCCL, std::string("NCCL async error: ") + ncclGetErrorString(st));
+            }
+        }
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                            std::chrono::steady_clock::now() - t0).count();
+        if (d && ms > d->timeout_ms) {
+            if (d->comm) ncclCommAbort(d->comm);
+            d->comm = nullptr;
+            COVE_THROW(COVE_ERR_TIMEOUT, "stream did not finish before the deadline");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+void halo(cove_dist* d, double* xw, cudaStream_t s) {
+    if (!d || d->world == 1 || d->xfers.empty()) return;
+    nccl_ok(ncclGroupStart(), "ncclGroupStart");
+    for (const auto& x : d->xfers) {
+        if (x.send_n > 0)
+            nccl_ok(ncclSend(xw + x.send_off, static_cast<size_t>(x.send_n), ncclFloat64, x.peer,
+                             d->comm, s), "ncclSend");
+        if (x.recv_n > 0)
+            nccl_ok(ncclRecv(xw + x.recv_off, static_cast<size_t>(x.recv_n), ncclFloat64, x.peer,
+                             d->comm, s), "ncclRecv");
+    }
+    const ncclResult_t r = ncclGroupEnd();
+    nccl_ok(r, "ncclGroupEnd");
+    if (r == ncclInProgress) wait_comm_ready(d->comm, d->timeout_ms);
+}
+
+void allreduce_scalar(cove_dist* d, double* v, cudaStream_t s) {
+    if (!d || d->world == 1) return;
+    const ncclResult_t r = ncclAllReduce(v, v, 1, ncclFloat64, ncclSum, d->comm, s);
+    nccl_ok(r, "ncclAllReduce");
+    if (r == ncclInProgress) wait_comm_ready(d->comm, d->timeout_ms);
+}
+
+// y_local = A_local x_window over the rank's plans (consecutive row blocks)
+float spmv_plans(const std::vector<cove_plan*>& plans, const double* xw, double* y,
+                 cudaStream_t s) {
+    int64_t off = 0;
+    for (const cove_plan* P : plans) {
+        launch_hybrid_spmv(P->shape(), P->route_values(P->dispatched_route), xw, y + off, s);
+        off += P->rows;
+    }
+    return 0.0f;
+}
+
+void dot(int64_t n, const double* a, const double* b, double* partial, double* out,
+         cudaStream_t s) {
+    dot_partial_kernel<<<kDotCtas, kThreads, 0, s>>>(n, a, b, partial);
+    dot_final_kernel<<<1, kThreads, 0, s>>>(partial, kDotCtas, out);
+}
+
+void cg_run(cove_dist* d, const std::vector<cove_plan*>& plans, int64_t n_local,
+            int64_t p_off, int64_t wl, const double* b, double* x, int iters,
+            cove_cg_result* res, cudaStream_t s) {
+    for (const cove_plan* P : plans) {
+        if (P->dtype != COVE_F64) COVE_THROW(COVE_ERR_UNSUPPORTED, "CG runs in fp64");
+    }
+    DevBuf r, pw, ap, partial, scal;
+    alloc_n<double>(r, n_local);
+    alloc_n<double>(pw, wl);
+    alloc_n<double>(ap, n_local);
+    alloc_n<double>(partial, kDotCtas);
+    alloc_n<double>(scal, 8);
+    double* p = pw.as<double>() + p_off;
+    CUDA_OK(cudaMemsetAsync(pw.p, 0, static_cast<size_t>(wl) * 8, s));
+    CUDA_OK(cudaMemsetAsync(x, 0, static_cast<size_t>(n_local) * 8, s));
+    CUDA_OK(cudaMemcpyAsync(r.p, b, static_cast<size_t>(n_local) * 8, cudaMemcpyDeviceToDevice, s));
+    CUDA_OK(cudaMemcpyAsync(p, b, static_cast<size_t>(n_local) * 8, cudaMemcpyDeviceToDevice, s));
+    double* S = scal.as<double>();
+    dot(n_local, r.as<double>(), r.as<double>(), partial.as<double>(), S + 0, s);
+    allreduce_scalar(d, S + 0, s);
+    CUDA_LAUNCH_OK();
+    wait_stream(d, s);
+    double rs0 = 0.0;
+    CUDA_OK(cudaMemcpy(&rs0, S, 8, cudaMemcpyDeviceToHost));
+
+    cudaEvent_t e0, e1;
+    CUDA_OK(cudaEventCreate(&e0));
+    CUDA_OK(cudaEventCreate(&e1));
+    std::vector<cudaEvent_t> ev(2 * static_cast<size_t>(iters));
+    for (auto& e : ev) CUDA_OK(cudaEventCreate(&e));
+    const int ug = static_cast<int>(std::min<int64_t>(grid_for(n_local, kThreads), kDotCtas));
+    double spmv_ms = 0.0;
+    CUDA_OK(cudaEventRecord(e0, s));
+    for (int k = 0; k < iters; ++k) {
+        const int cur = k & 1, nxt = cur ^ 1;
+        halo(d, pw.as<double>(), s);
+        CUDA_OK(cudaEventRecord(ev[2 * k], s));
+        spmv_plans(plans, pw.as<double>(), ap.as<double>(), s);
+        CUDA_OK(cudaEventRecord(ev[2 * k + 1], s));
+        dot(n_local, p, ap.as<double>(), partial.as<double>(), S + 2, s);
+        allreduce_scalar(d, S + 2, s);
+        cg_update_kernel<<<kDotCtas, kThreads, 0, s>>>(n_local, S, cur, p, ap.as<double>(), x,
+                                                      r.as<double>(), partial.as<double>());
+        dot_final_kernel<<<1, kThreads, 0, s>>>(partial.as<double>(), kDotCtas, S + nxt);
+        allreduce_scalar(d, S + nxt, s);
+        cg_p_kernel<<<ug, kThreads, 0, s>>>(n_local, S, cur, nxt, r.as<double>(), p);
+        CUDA_LAUNCH_OK();
+    }
+    CUDA_OK(cudaEventRecord(e1, s));
+    wait_stream(d, s);
+    float total = 0.0f;
+    CUDA_OK(cudaEventElapsedTime(&total, e0, e1));
+    for (int k = 0; k < iters; ++k) {
+        float ms = 0.0f;
+        CUDA_OK(cudaEventElapsedTime(&ms, ev[2 * k], ev[2 * k + 1]));
+        spmv_ms += ms;
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    double rsf = 0.0;
+    CUDA_OK(cudaMemcpy(&rsf, S + (iters & 1), 8, cudaMemcpyDeviceToHost));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (res) {
+        res->iterations = iters;
+        res->rs_initial = rs0;
+        res->rs_final = rsf;
+        res->ms_total = total;
+        res->ms_spmv = spmv_ms;
+    }
+}
+
+}  // namespace
+}  // namespace cove
+
+extern "C" {
+
+cove_status cove_cg_solve(const cove_plan* P, const void* b, void* x, int32_t iters,
+                          cove_cg_result* result, void* stream) {
+    return guarded([&] {
+        if (!P || !b || !x) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        if (P->rows != P->cols) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "CG needs a square matrix");
+        if (iters < 0) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "iterations must be non-negative");
+        std::vector<cove_plan*> plans{const_cast<cove_plan*>(P)};
+        cg_run(nullptr, plans, P->rows, 0, P->cols, static_cast<const double*>(b),
+               static_cast<double*>(x), iters, result, static_cast<cudaStream_t>(stream));
+    });
+}
+
+size_t cove_dist_id_bytes(void) { return sizeof(ncclUniqueId); }
+
+cove_status cove_dist_make_id(void* id_out) {
+    return guarded([&] {
+        if (!id_out) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null id");
+        ncclUniqueId id;
+        nccl_ok(ncclGetUniqueId(&id), "ncclGetUniqueId");
+        std::memcpy(id_out, &id, sizeof(id));
+    });
+}
+
+cove_status cove_dist_create(int32_t rank, int32_t world, const void* nccl_id,
+                             cove_plan* const* plans, int32_t num_plans, int64_t global_rows,
+                             int64_t row_begin, int64_t row_end, int64_t window_begin,
+                             int64_t window_len, int32_t timeout_ms, cove_dist** out) {
+    return guarded([&] {
+        if (!out || !nccl_id || (num_plans > 0 && !plans)) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        if (world < 1 || rank < 0 || rank >= world) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "bad rank/world");
+        if (row_begin < window_begin || row_end > window_begin + window_len || row_end < row_begin) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "row block must lie inside the window");
+        }
+        int64_t rows = 0;
+        for (int i = 0; i < num_plans; ++i) {
+            if (plans[i]->cols != window_len) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "plan columns must equal the window length");
+            rows += plans[i]->rows;
+        }
+        if (rows != row_end - row_begin) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "plans must cover the row block");
+        auto* d = new cove_dist();
+        d->rank = rank;
+        d->world = world;
+        d->plans.assign(plans, plans + num_plans);
+        d->global_rows = global_rows;
+        d->row_begin = row_begin;
+        d->row_end = row_end;
+        d->wb = window_begin;
+        d->wl = window_len;
+        d->timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+        try {
+            ncclUniqueId id;
+            std::memcpy(&id, nccl_id, sizeof(id));
+            ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+            cfg.blocking = 0;
+            nccl_ok(ncclCommInitRankConfig(&d->comm, world, id, rank, &cfg), "ncclCommInitRankConfig");
+            wait_comm_ready(d->comm, d->timeout_ms);
+            // share every rank's (row_begin, row_end, window_begin, window_len)
+            DevBuf all;
+            alloc_n<int64_t>(all, 4 * world);
+            int64_t mine[4] = {row_begin, row_end, window_begin, window_len};
+            cudaStream_t s = nullptr;
+            CUDA_OK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+            CUDA_OK(cudaMemcpyAsync(all.as<int64_t>() + 4 * rank, mine, sizeof(mine),
+                                    cudaMemcpyHostToDevice, s));
+            const ncclResult_t ag =
+                ncclAllGather(all.as<int64_t>() + 4 * rank, all.p, 4, ncclInt64, d->comm, s);
+            nccl_ok(ag, "ncclAllGather");
+            if (ag == ncclInProgress) wait_comm_ready(d->comm, d->timeout_ms);
+            wait_stream(d, s);
+            std::vector<int64_t> h(4 * world);
+            CUDA_OK(cudaMemcpy(h.data(), all.p, h.size() * 8, cudaMemcpyDeviceToHost));
+            cudaStreamDestroy(s);
+            for (int q = 0; q < world; ++q) {
+                if (q == rank) continue;
+                const int64_t qb = h[4 * q], qe = h[4 * q + 1], qwb = h[4 * q + 2], qwl = h[4 * q + 3];
+                // my rows inside q's window go to q; q's rows inside my window come from q
+                const int64_t sb = std::max(row_begin, qwb), se = std::min(row_end, qwb + qwl);
+                const int64_t rb = std::max(qb, window_begin), re = std::min(qe, window_begin + window_len);
+                cove_dist::Xfer x{q, sb - window_begin, std::max<int64_t>(0, se - sb), rb - window_begin,
+                                  std::max<int64_t>(0, re - rb)};
+                if (x.send_n > 0 || x.recv_n > 0) d->xfers.push_back(x);
+            }
+            // the window outside the row block must be covered by received ranges
+            int64_t covered = row_end - row_begin;
+            for (const auto& x : d->xfers) covered += x.recv_n;
+            if (covered != window_len) {
+                COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "halo is not covered by other ranks' row blocks");
+            }
+        } catch (...) {
+            if (d->comm) ncclCommAbort(d->comm);
+            delete d;
+            throw;
+        }
+        *out = d;
+    });
+}
+
+cove_status cove_dist_destroy(cove_dist* d) {
+    return guarded([&] {
+        if (!d) return;
+        if (d->comm) {
+            ncclCommFinalize(d->comm);
+            wait_comm_ready(d->comm, d->timeout_ms);
+            ncclCommDestroy(d->comm);
+        }
+        delete d;
+    });
+}
+
+cove_status cove_dist_halo(cove_dist* d, void* x_window, void* stream) {
+    return guarded([&] {
+        if (!d || !x_window) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        halo(d, static_cast<double*>(x_window), static_cast<cudaStream_t>(stream));
+    });
+}
+
+cove_status cove_dist_spmv(cove_dist* d, void* x_window, void* y_local, void* stream) {
+    return guarded([&] {
+        if (!d || !x_window || !y_local) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        halo(d, static_cast<double*>(x_window), s);
+        spmv_plans(d->plans, static_cast<const double*>(x_window), static_cast<double*>(y_local), s);
+    });
+}
+
+cove_status cove_dist_cg_solve(cove_dist* d, const void* b_local, void* x_local, int32_t iters,
+                               cove_cg_result* result, void* stream) {
+    return guarded([&] {
+        if (!d || !b_local || !x_local) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        cg_run(d, d->plans, d->row_end - d->row_begin, d->row_begin - d->wb, d->wl,
+               static_cast<const double*>(b_local), static_cast<double*>(x_local), iters, result,
+               static_cast<cudaStream_t>(stream));
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,723 @@
+// convert.cu -- the 8x4 position converter on sm_100a.
+//
+// CSR -> full BitBSR 8x4 -> cost-gated CSR+BitBSR split -> packed block words,
+// work items and long residual-row chunks.  Each stage is bit-exact with the
+// reference's host pipeline:
+//   convert_to_bitbsr                 structural/include/structural/convert.hpp:13-165
+//   warp-direct GPU converter         structural/include/structural/gpu_convert.cuh:126-243
+//   split (cost gate)                 structural/include/structural/csr_bitbsr_split.hpp:405-490
+//   work items + packed words         structural/src/main_gpu_csr_bitbsr_spmv.cu:387-475
+//                                     structural/include/structural/operators/bitbsr_spmv_8x4_common.cuh:95-117,199-267
+//   long-row chunks                   structural/src/main_gpu_csr_bitbsr_spmv.cu:1155-1184
+//
+// Layout of the kernels: the converter runs one 8-lane group per block row
+// (lane = row of the block row, four block rows per warp) and merges the
+// eight sorted rows with __reduce_min_sync over the group, so all 32 lanes
+// work.  The split runs one warp per block row with one lane per block; the
+// eight per-row residual counts of a block are packed as 8-bit fields of a
+// 64-bit word so one warp scan covers all eight rows.
+#include "cove_convert.cuh"
+
+#include <climits>
+
+namespace cove {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ bool is_zero(T v) { return v == T(0); }
+
+__device__ __forceinline__ unsigned group_mask(int lane) { return 0xFFu << (lane & 24); }
+
+// ---------------------------------------------------------------------------
+// validation: monotonic row_ptr, columns in range, strictly increasing
+// columns among the nonzero entries of each row
+// ---------------------------------------------------------------------------
+
+template <typename T, typename RP>
+__global__ void validate_csr_kernel(int32_t rows, int32_t cols, const RP* __restrict__ rp,
+                                    const int32_t* __restrict__ ci, const T* __restrict__ v,
+                                    int* __restrict__ err) {
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const int64_t b = static_cast<int64_t>(rp[r]);
+    const int64_t e = static_cast<int64_t>(rp[r + 1]);
+    if (b > e) {
+        atomicOr(err, 1);
+        return;
+    }
+    int prev = -1;
+    for (int64_t p = b; p < e; ++p) {
+        const int c = ci[p];
+        if (c < 0 || c >= cols) {
+            atomicOr(err, 2);
+            return;
+        }
+        if (is_zero(v[p])) continue;
+        if (c <= prev) {
+            atomicOr(err, 4);
+            return;
+        }
+        prev = c;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// full BitBSR: count and fill (one 8-lane group per block row)
+// ---------------------------------------------------------------------------
+
+template <typename T, typename RP>
+struct RowCursor {
+    int64_t pos, end;
+    __device__ __forceinline__ void skip_zeros(const T* __restrict__ v) {
+        while (pos < end && is_zero(v[pos])) ++pos;
+    }
+};
+
+template <typename T, typename RP>
+__global__ void full_count_kernel(int32_t rows, int32_t nbr, const RP* __restrict__ rp,
+                                  const int32_t* __restrict__ ci, const T* __restrict__ v,
+                                  int32_t* __restrict__ block_counts,
+                                  int32_t* __restrict__ nnz_counts) {
+    const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t br = gt >> 3;
+    const int lane = threadIdx.x & 31;
+    const int l8 = lane & 7;
+    const unsigned gm = group_mask(lane);
+    if (br >= nbr) return;  // whole group leaves together
+    const int64_t row = br * kBlockRows + l8;
+    const bool active = row < rows;
+    RowCursor<T, RP> cur{active ? static_cast<int64_t>(rp[row]) : 0,
+                         active ? static_cast<int64_t>(rp[row + 1]) : 0};
+    cur.skip_zeros(v);
+    int nblocks = 0;
+    int nnz = 0;
+    while (true) {
+        const int cand = cur.pos < cur.end ? (ci[cur.pos] >> 2) : INT_MAX;
+        const int bc = __reduce_min_sync(gm, cand);
+        if (bc == INT_MAX) break;
+        ++nblocks;
+        while (cur.pos < cur.end && (ci[cur.pos] >> 2) == bc) {
+            ++nnz;
+            ++cur.pos;
+            cur.skip_zeros(v);
+        }
+    }
+    const int total = __reduce_add_sync(gm, nnz);
+    if (l8 == 0) {
+        block_counts[br] = nblocks;
+        nnz_counts[br] = total;
+    }
+}
+
+template <typename T, typename RP>
+__global__ void full_fill_kernel(int32_t rows, int32_t nbr, const RP* __restrict__ rp,
+                                 const int32_t* __restrict__ ci, const T* __restrict__ v,
+                                 const int32_t* __restrict__ block_row_ptr,
+                                 const int32_t* __restrict__ block_row_val_ptr,
+                                 int32_t* __restrict__ block_col_idx,
+                                 uint32_t* __restrict__ bitmap, T* __restrict__ values) {
+    const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t br = gt >> 3;
+    const int lane = threadIdx.x & 31;
+    const int l8 = lane & 7;
+    const unsigned gm = group_mask(lane);
+    if (br >= nbr) return;
+    const int64_t row = br * kBlockRows + l8;
+    const bool active = row < rows;
+    RowCursor<T, RP> cur{active ? static_cast<int64_t>(rp[row]) : 0,
+                         active ? static_cast<int64_t>(rp[row + 1]) : 0};
+    cur.skip_zeros(v);
+    int64_t block_id = block_row_ptr[br];
+    int64_t value_pos = block_row_val_ptr[br];
+    while (true) {
+        const int cand = cur.pos < cur.end ? (ci[cur.pos] >> 2) : INT_MAX;
+        const int bc = __reduce_min_sync(gm, cand);
+        if (bc == INT_MAX) break;
+        // this row's entries of block bc, in CSR order = bit order
+        unsigned bits = 0;
+        int cnt = 0;
+        const int64_t start = cur.pos;
+        while (cur.pos < cur.end && (ci[cur.pos] >> 2) == bc) {
+            bits |= 1u << (l8 * kBlockCols + (ci[cur.pos] & 3));
+            ++cnt;
+            ++cur.pos;
+            cur.skip_zeros(v);
+        }
+        // exclusive prefix of cnt over the 8 lanes of the group
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            const int t = __shfl_up_sync(gm, incl, o, 8);
+            if (l8 >= o) incl += t;
+        }
+        const int total = __shfl_sync(gm, incl, 7, 8);
+        const unsigned bm = __reduce_or_sync(gm, bits);
+        // copy values, skipping stored zeros
+        int64_t dst = value_pos + (incl - cnt);
+        for (int64_t p = start; p < cur.pos; ++p) {
+            const T val = v[p];
+            if (is_zero(val)) continue;
+            values[dst++] = val;
+        }
+        if (l8 == 0) {
+            block_col_idx[block_id] = bc;
+            bitmap[block_id] = bm;
+        }
+        ++block_id;
+        value_pos += total;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// split: count and fill (one warp per block row, one lane per block)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint64_t nibble_counts(uint32_t bm) {
+    uint64_t packed = 0;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        packed |= static_cast<uint64_t>(__popc((bm >> (4 * r)) & 0xFu)) << (8 * r);
+    }
+    return packed;
+}
+
+__device__ __forceinline__ uint64_t warp_incl_scan_u64(uint64_t v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    return v;
+}
+
+__device__ __forceinline__ int warp_incl_scan_i32(int v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    return v;
+}
+
+__global__ void split_count_kernel(int32_t rows, int32_t nbr, int32_t threshold,
+                                   unsigned long long move_mask,
+                                   const int32_t* __restrict__ brp,
+                                   const uint32_t* __restrict__ bitmap,
+                                   int32_t* __restrict__ kept_count,
+                                   int32_t* __restrict__ kept_nnz,
+                                   int32_t* __restrict__ res_count,
+                                   int32_t* __restrict__ res_blocks,
+                                   int32_t* __restrict__ skipped_blocks,
+                                   int32_t* __restrict__ skipped_nnz) {
+    const int64_t br = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (br >= nbr) return;
+    const int b0 = brp[br], b1 = brp[br + 1];
+    int kc = 0, kn = 0, rb = 0, sb = 0, sn = 0;
+    int run = 0;  // lane r < 8: residual entries of row r
+    for (int base = b0; base < b1; base += 32) {
+        const int b = base + lane;
+        const bool valid = b < b1;
+        const uint32_t bm = valid ? bitmap[b] : 0u;
+        const int bn = __popc(bm);
+        const bool small = valid && bn <= threshold;
+        const bool moved = small && ((move_mask >> bn) & 1ULL);
+        const bool kept = valid && !moved;
+        kc += __popc(__ballot_sync(0xffffffffu, kept));
+        kn += __reduce_add_sync(0xffffffffu, kept ? bn : 0);
+        rb += __popc(__ballot_sync(0xffffffffu, moved));
+        sb += __popc(__ballot_sync(0xffffffffu, small && !moved));
+        sn += __reduce_add_sync(0xffffffffu, (small && !moved) ? bn : 0);
+        uint64_t packed = moved ? nibble_counts(bm) : 0ULL;
+        packed = warp_incl_scan_u64(packed, lane);
+        const uint64_t tot = __shfl_sync(0xffffffffu, packed, 31);
+        run += static_cast<int>((tot >> (8 * (lane & 7))) & 0xFFu);
+    }
+    if (lane == 0) {
+        kept_count[br] = kc;
+        kept_nnz[br] = kn;
+        res_blocks[br] = rb;
+        skipped_blocks[br] = sb;
+        skipped_nnz[br] = sn;
+    }
+    if (lane < 8) {
+        const int64_t row = br * kBlockRows + lane;
+        if (row < rows) res_count[row] = run;
+    }
+}
+
+template <typename T>
+__global__ void split_fill_kernel(int32_t rows, int32_t nbr, int32_t threshold,
+                                  unsigned long long move_mask,
+                                  const int32_t* __restrict__ brp,
+                                  const int32_t* __restrict__ brvp,
+                                  const int32_t* __restrict__ full_col,
+                                  const uint32_t* __restrict__ bitmap,
+                                  const T* __restrict__ full_values,
+                                  const int32_t* __restrict__ kept_brp,
+                                  const int32_t* __restrict__ kept_brvp,
+                                  const int32_t* __restrict__ res_rp,
+                                  int32_t* __restrict__ kept_col,
+                                  uint32_t* __restrict__ kept_bitmap,
+                                  T* __restrict__ kept_values,
+                                  int32_t* __restrict__ res_col,
+                                  T* __restrict__ res_values) {
+    __shared__ int s_base[kThreads / 32][8];
+    const int64_t br = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int w = threadIdx.x >> 5;
+    if (br >= nbr) return;
+    if (lane < 8) {
+        const int64_t row = br * kBlockRows + lane;
+        s_base[w][lane] = row < rows ? res_rp[row] : 0;
+    }
+    __syncwarp();
+    const int b0 = brp[br], b1 = brp[br + 1];
+    int kb = kept_brp[br];
+    int kv = kept_brvp[br];
+    int fv = brvp[br];
+    const unsigned lt = (1u << lane) - 1u;
+    for (int base = b0; base < b1; base += 32) {
+        const int b = base + lane;
+        const bool valid = b < b1;
+        const uint32_t bm = valid ? bitmap[b] : 0u;
+        const int bn = __popc(bm);
+        const bool moved = valid && bn <= threshold && ((move_mask >> bn) & 1ULL);
+        const bool kept = valid && !moved;
+        const unsigned kballot = __ballot_sync(0xffffffffu, kept);
+        const int fv_incl = warp_incl_scan_i32(bn, lane);
+        const int kv_incl = warp_incl_scan_i32(kept ? bn : 0, lane);
+        const uint64_t packed = moved ? nibble_counts(bm) : 0ULL;
+        const uint64_t p_incl = warp_incl_scan_u64(packed, lane);
+        const uint64_t p_excl = p_incl - packed;
+        const int my_fv = fv + fv_incl - bn;
+        if (kept) {
+            const int dst = kb + __popc(kballot & lt);
+            kept_col[dst] = full_col[b];
+            kept_bitmap[dst] = bm;
+            const int vdst = kv + kv_incl - bn;
+            for (int k = 0; k < bn; ++k) kept_values[vdst + k] = full_values[my_fv + k];
+        } else if (moved) {
+            const int bc = full_col[b];
+            uint32_t rest = bm;
+            int rank = 0;
+            while (rest) {
+                const int bit = __ffs(rest) - 1;
+                const int r = bit >> 2;
+                const int c = bit & 3;
+                const uint32_t nib = (bm >> (4 * r)) & 0xFu;
+                const int within = __popc(nib & ((1u << c) - 1u));
+                const int dst = s_base[w][r] + static_cast<int>((p_excl >> (8 * r)) & 0xFFu) + within;
+                res_col[dst] = bc * kBlockCols + c;
+                res_values[dst] = full_values[my_fv + rank];
+                ++rank;
+                rest &= rest - 1u;
+            }
+        }
+        const uint64_t tot = __shfl_sync(0xffffffffu, p_incl, 31);
+        kb += __popc(kballot);
+        kv += __shfl_sync(0xffffffffu, kv_incl, 31);
+        fv += __shfl_sync(0xffffffffu, fv_incl, 31);
+        __syncwarp();
+        if (lane < 8) s_base[w][lane] += static_cast<int>((tot >> (8 * lane)) & 0xFFu);
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// block popcounts (block_val_ptr), packed words, work items, long chunks
+// ---------------------------------------------------------------------------
+
+__global__ void popc_kernel(int64_t n, const uint32_t* __restrict__ bitmap,
+                            int32_t* __restrict__ out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __popc(bitmap[i]);
+}
+
+__global__ void pack_words_kernel(int64_t n, const int32_t* __restrict__ col,
+                                  const uint32_t* __restrict__ bitmap,
+                                  uint64_t* __restrict__ words) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) words[i] = pack_word(static_cast<uint32_t>(col[i]), bitmap[i], false);
+}
+
+__device__ __forceinline__ void lb_shape(int count, int chunk, int split, int style,
+                                         int* pieces, bool* atomic, int* eff) {
+    if (count == 0) {
+        *pieces = style == COVE_LB_HYBRID ? 1 : 0;
+        *atomic = false;
+        *eff = 0;
+        return;
+    }
+    if (style == COVE_LB_HYBRID) {
+        *atomic = count > split;
+        *eff = *atomic ? chunk : count;
+        *pieces = (count + *eff - 1) / *eff;
+    } else {
+        *pieces = count <= split ? 1 : (count + chunk - 1) / chunk;
+        *atomic = *pieces > 1;
+        *eff = *atomic ? chunk : count;
+    }
+}
+
+__global__ void lb_count_kernel(int32_t nbr, const int32_t* __restrict__ kbrp, int chunk,
+                                int split, int style, int32_t* __restrict__ out) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (br >= nbr) return;
+    int pieces, eff;
+    bool atomic;
+    lb_shape(kbrp[br + 1] - kbrp[br], chunk, split, style, &pieces, &atomic, &eff);
+    out[br] = pieces;
+}
+
+__global__ void lb_fill_kernel(int32_t nbr, const int32_t* __restrict__ kbrp,
+                               const int32_t* __restrict__ kbvp,
+                               const uint32_t* __restrict__ kbitmap,
+                               const int32_t* __restrict__ item_rp, int chunk, int split,
+                               int style, uint64_t* __restrict__ words,
+                               WorkItem* __restrict__ items) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (br >= nbr) return;
+    const int rs = kbrp[br], re = kbrp[br + 1];
+    int pieces, eff;
+    bool atomic;
+    lb_shape(re - rs, chunk, split, style, &pieces, &atomic, &eff);
+    int out = item_rp[br];
+    if (re == rs) {
+        if (pieces == 1) items[out] = WorkItem{static_cast<uint32_t>(br), static_cast<uint32_t>(rs), 0u,
+                                               static_cast<uint32_t>(kbvp[rs])};
+        return;
+    }
+    int blk = rs;
+    int vp = kbvp[rs];
+    while (blk < re) {
+        const int c = min(eff, re - blk);
+        items[out++] = WorkItem{static_cast<uint32_t>(br), static_cast<uint32_t>(blk),
+                                static_cast<uint32_t>(c), static_cast<uint32_t>(vp)};
+        if (atomic) words[blk] |= kFlagBit;
+        for (int i = 0; i < c; ++i) vp += __popc(kbitmap[blk + i]);
+        blk += c;
+    }
+}
+
+__global__ void chunk_count_kernel(int32_t rows, const int32_t* __restrict__ rp, int tau,
+                                   int chunk_nnz, int32_t* __restrict__ out,
+                                   int32_t* __restrict__ long_flag) {
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const int len = rp[r + 1] - rp[r];
+    const bool lg = tau > 0 && len > tau;
+    out[r] = lg ? (len + chunk_nnz - 1) / chunk_nnz : 0;
+    long_flag[r] = lg ? 1 : 0;
+}
+
+__global__ void chunk_fill_kernel(int32_t rows, const int32_t* __restrict__ rp, int tau,
+                                  int chunk_nnz, const int64_t* __restrict__ crp,
+                                  int32_t* __restrict__ crow, int32_t* __restrict__ cbegin,
+                                  int32_t* __restrict__ ccount) {
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const int b = rp[r];
+    const int len = rp[r + 1] - b;
+    if (!(tau > 0 && len > tau)) return;
+    int64_t o = crp[r];
+    for (int off = 0; off < len; off += chunk_nnz) {
+        crow[o] = static_cast<int32_t>(r);
+        cbegin[o] = b + off;
+        ccount[o] = min(chunk_nnz, len - off);
+        ++o;
+    }
+}
+
+__global__ void block_row_val_ptr_kernel(int32_t nbr, const int32_t* __restrict__ brp,
+                                         const int32_t* __restrict__ bvp,
+                                         int32_t* __restrict__ out) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (br > nbr) return;
+    out[br] = bvp[brp[br]];
+}
+
+int32_t checked_i32(int64_t v, const char* what) {
+    if (v > INT32_MAX) {
+        COVE_THROW(COVE_ERR_OVERFLOW, std::string(what) + " exceeds int32 offsets (" +
+                                          std::to_string(v) + ")");
+    }
+    return static_cast<int32_t>(v);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// host drivers
+// ---------------------------------------------------------------------------
+
+template <typename T>
+void validate_csr(const cove_csr_desc& d, cudaStream_t s) {
+    if (d.rows < 0 || d.cols < 0 || d.nnz < 0) {
+        COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "CSR dimensions must be non-negative");
+    }
+    if (d.rows > 0 && d.row_ptr == nullptr) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "CSR row_ptr is null");
+    if (d.nnz > 0 && (d.col_idx == nullptr || d.values == nullptr)) {
+        COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "CSR col_idx/values are null");
+    }
+    // endpoints
+    int64_t first = 0, last = 0;
+    if (d.row_ptr_i32) {
+        int32_t a = 0, b = 0;
+        CUDA_OK(cudaMemcpyAsync(&a, d.row_ptr, 4, cudaMemcpyDeviceToHost, s));
+        CUDA_OK(cudaMemcpyAsync(&b, static_cast<const int32_t*>(d.row_ptr) + d.rows, 4,
+                                cudaMemcpyDeviceToHost, s));
+        CUDA_OK(cudaStreamSynchronize(s));
+        first = a;
+        last = b;
+    } else {
+        CUDA_OK(cudaMemcpyAsync(&first, d.row_ptr, 8, cudaMemcpyDeviceToHost, s));
+        CUDA_OK(cudaMemcpyAsync(&last, static_cast<const int64_t*>(d.row_ptr) + d.rows, 8,
+                                cudaMemcpyDeviceToHost, s));
+        CUDA_OK(cudaStreamSynchronize(s));
+    }
+    if (first != 0) COVE_THROW(COVE_ERR_INVALID_INPUT, "CSR row_ptr must start at zero");
+    if (last != d.nnz) COVE_THROW(COVE_ERR_INVALID_INPUT, "CSR row_ptr.back must equal nnz");
+    if (d.rows == 0) return;
+    DevBuf err;
+    err.alloc(sizeof(int));
+    CUDA_OK(cudaMemsetAsync(err.p, 0, sizeof(int), s));
+    const T* v = static_cast<const T*>(d.values);
+    if (d.row_ptr_i32) {
+        validate_csr_kernel<T, int32_t><<<grid_for(d.rows, kThreads), kThreads, 0, s>>>(
+            d.rows, d.cols, static_cast<const int32_t*>(d.row_ptr), d.col_idx, v, err.as<int>());
+    } else {
+        validate_csr_kernel<T, int64_t><<<grid_for(d.rows, kThreads), kThreads, 0, s>>>(
+            d.rows, d.cols, static_cast<const int64_t*>(d.row_ptr), d.col_idx, v, err.as<int>());
+    }
+    CUDA_LAUNCH_OK();
+    int h = 0;
+    CUDA_OK(cudaMemcpyAsync(&h, err.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUDA_OK(cudaStreamSynchronize(s));
+    if (h & 1) COVE_THROW(COVE_ERR_INVALID_INPUT, "CSR row_ptr must be monotonic");
+    if (h & 2) COVE_THROW(COVE_ERR_INVALID_INPUT, "CSR column index out of range");
+    if (h & 4) {
+        COVE_THROW(COVE_ERR_INVALID_INPUT,
+                   "CSR columns must be strictly increasing within a row "
+                   "(duplicate CSR entry maps to the same BitBSR bit)");
+    }
+}
+
+template <typename T>
+void build_full_bitbsr(const cove_csr_desc& d, FullBitBsr& out, cudaStream_t s) {
+    out.rows = d.rows;
+    out.cols = d.cols;
+    out.nbr = (d.rows + kBlockRows - 1) / kBlockRows;
+    const int32_t nbr = out.nbr;
+    DevBuf counts, nnzc;
+    alloc_n<int32_t>(counts, nbr);
+    alloc_n<int32_t>(nnzc, nbr);
+    alloc_n<int32_t>(out.block_row_ptr, nbr + 1);
+    alloc_n<int32_t>(out.block_row_val_ptr, nbr + 1);
+    const T* v = static_cast<const T*>(d.values);
+    const int grid = grid_for(static_cast<int64_t>(nbr) * 8, kThreads);
+    if (nbr > 0) {
+        if (d.row_ptr_i32) {
+            full_count_kernel<T, int32_t><<<grid, kThreads, 0, s>>>(
+                d.rows, nbr, static_cast<const int32_t*>(d.row_ptr), d.col_idx, v,
+                counts.as<int32_t>(), nnzc.as<int32_t>());
+        } else {
+            full_count_kernel<T, int64_t><<<grid, kThreads, 0, s>>>(
+                d.rows, nbr, static_cast<const int64_t*>(d.row_ptr), d.col_idx, v,
+                counts.as<int32_t>(), nnzc.as<int32_t>());
+        }
+        CUDA_LAUNCH_OK();
+    }
+    // scans into int64 first so an overflow is detected, then narrowed
+    out.num_blocks = checked_i32(
+        exclusive_scan_total<int32_t, int32_t>(counts.as<int32_t>(), out.block_row_ptr.as<int32_t>(), nbr, s),
+        "BitBSR block count");
+    out.nnz = checked_i32(
+        exclusive_scan_total<int32_t, int32_t>(nnzc.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(), nbr, s),
+        "BitBSR nnz");
+    alloc_n<int32_t>(out.block_col_idx, out.num_blocks);
+    alloc_n<uint32_t>(out.bitmap, out.num_blocks);
+    alloc_n<T>(out.values, out.nnz);
+    if (nbr > 0 && out.num_blocks > 0) {
+        if (d.row_ptr_i32) {
+            full_fill_kernel<T, int32_t><<<grid, kThreads, 0, s>>>(
+                d.rows, nbr, static_cast<const int32_t*>(d.row_ptr), d.col_idx, v,
+                out.block_row_ptr.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(),
+                out.block_col_idx.as<int32_t>(), out.bitmap.as<uint32_t>(), out.values.as<T>());
+        } else {
+            full_fill_kernel<T, int64_t><<<grid, kThreads, 0, s>>>(
+                d.rows, nbr, static_cast<const int64_t*>(d.row_ptr), d.col_idx, v,
+                out.block_row_ptr.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(),
+                out.block_col_idx.as<int32_t>(), out.bitmap.as<uint32_t>(), out.values.as<T>());
+        }
+        CUDA_LAUNCH_OK();
+    }
+}
+
+// CsrBitBsrSplitCostModel::should_move_to_residual (csr_bitbsr_split.hpp:66-73)
+// tabulated for every block population 0..32 on the host, with plain double
+// arithmetic, so the device applies exactly the reference's decisions.
+unsigned long long move_mask_for(const cove_plan_opts& o) {
+    unsigned long long m = 0;
+    for (int bn = 0; bn <= 32; ++bn) {
+        bool move = true;
+        if (o.split_policy == COVE_SPLIT_COST_GATED) {
+            volatile double nnz = static_cast<double>(bn);
+            volatile double bitmap_cost = o.cost_bitmap_block + o.cost_bitmap_nnz * nnz;
+            volatile double csr_cost = o.cost_csr_block + o.cost_csr_nnz * nnz;
+            move = csr_cost < bitmap_cost;
+        } else if (o.split_policy == COVE_SPLIT_NONE) {
+            move = false;
+        }
+        if (move) m |= 1ULL << bn;
+    }
+    return m;
+}
+
+template <typename T>
+void build_split(const FullBitBsr& f, const cove_plan_opts& o, SplitParts& out, cudaStream_t s) {
+    const int32_t nbr = f.nbr;
+    const int32_t rows = f.rows;
+    const unsigned long long mm = move_mask_for(o);
+    const int32_t thr = o.split_policy == COVE_SPLIT_NONE ? -1 : o.residual_threshold;
+    DevBuf kc, kn, rc, rb, sb, sn;
+    alloc_n<int32_t>(kc, nbr);
+    alloc_n<int32_t>(kn, nbr);
+    alloc_n<int32_t>(rb, nbr);
+    alloc_n<int32_t>(sb, nbr);
+    alloc_n<int32_t>(sn, nbr);
+    alloc_n<int32_t>(rc, rows);
+    CUDA_OK(cudaMemsetAsync(rc.p, 0, static_cast<size_t>(rows) * 4 + 4, s));
+    const int grid = grid_for(static_cast<int64_t>(nbr) * 32, kThreads);
+    if (nbr > 0) {
+        split_count_kernel<<<grid, kThreads, 0, s>>>(
+            rows, nbr, thr, mm, f.block_row_ptr.as<int32_t>(), f.bitmap.as<uint32_t>(),
+            kc.as<int32_t>(), kn.as<int32_t>(), rc.as<int32_t>(), rb.as<int32_t>(),
+            sb.as<int32_t>(), sn.as<int32_t>());
+        CUDA_LAUNCH_OK();
+    }
+    alloc_n<int32_t>(out.kept_block_row_ptr, nbr + 1);
+    alloc_n<int32_t>(out.kept_block_row_val_ptr, nbr + 1);
+    alloc_n<int32_t>(out.res_row_ptr, rows + 1);
+    out.kept_blocks = exclusive_scan_total<int32_t, int32_t>(kc.as<int32_t>(),
+                                                             out.kept_block_row_ptr.as<int32_t>(), nbr, s);
+    out.kept_nnz = exclusive_scan_total<int32_t, int32_t>(kn.as<int32_t>(),
+                                                          out.kept_block_row_val_ptr.as<int32_t>(), nbr, s);
+    out.residual_nnz = checked_i32(
+        exclusive_scan_total<int32_t, int32_t>(rc.as<int32_t>(), out.res_row_ptr.as<int32_t>(), rows, s),
+        "residual nnz");
+    {
+        DevBuf tmp;
+        alloc_n<int32_t>(tmp, nbr + 1);
+        out.residual_blocks = exclusive_scan_total<int32_t, int32_t>(rb.as<int32_t>(), tmp.as<int32_t>(), nbr, s);
+        out.cost_skipped_blocks = exclusive_scan_total<int32_t, int32_t>(sb.as<int32_t>(), tmp.as<int32_t>(), nbr, s);
+        out.cost_skipped_nnz = exclusive_scan_total<int32_t, int32_t>(sn.as<int32_t>(), tmp.as<int32_t>(), nbr, s);
+    }
+    alloc_n<int32_t>(out.kept_col, out.kept_blocks);
+    alloc_n<uint32_t>(out.kept_bitmap, out.kept_blocks);
+    alloc_n<T>(out.kept_values, out.kept_nnz);
+    alloc_n<int32_t>(out.res_col, out.residual_nnz);
+    alloc_n<T>(out.res_values, out.residual_nnz);
+    if (nbr > 0 && f.num_blocks > 0) {
+        split_fill_kernel<T><<<grid, kThreads, 0, s>>>(
+            rows, nbr, thr, mm, f.block_row_ptr.as<int32_t>(), f.block_row_val_ptr.as<int32_t>(),
+            f.block_col_idx.as<int32_t>(), f.bitmap.as<uint32_t>(), f.values.as<T>(),
+            out.kept_block_row_ptr.as<int32_t>(), out.kept_block_row_val_ptr.as<int32_t>(),
+            out.res_row_ptr.as<int32_t>(), out.kept_col.as<int32_t>(),
+            out.kept_bitmap.as<uint32_t>(), out.kept_values.as<T>(), out.res_col.as<int32_t>(),
+            out.res_values.as<T>());
+        CUDA_LAUNCH_OK();
+    }
+    // BitBsrMatrix::block_val_ptr of the kept part
+    alloc_n<int32_t>(out.kept_block_val_ptr, out.kept_blocks + 1);
+    {
+        DevBuf pc;
+        alloc_n<int32_t>(pc, out.kept_blocks);
+        if (out.kept_blocks > 0) {
+            popc_kernel<<<grid_for(out.kept_blocks, kThreads), kThreads, 0, s>>>(
+                out.kept_blocks, out.kept_bitmap.as<uint32_t>(), pc.as<int32_t>());
+            CUDA_LAUNCH_OK();
+        }
+        exclusive_scan_total<int32_t, int32_t>(pc.as<int32_t>(), out.kept_block_val_ptr.as<int32_t>(),
+                                               out.kept_blocks, s);
+    }
+}
+
+void build_layout(const SplitParts& sp, int32_t nbr, const cove_plan_opts& o, Layout& out,
+                  cudaStream_t s) {
+    const int chunk = o.lb_chunk_blocks;
+    const int split = o.lb_split_threshold_blocks < 0 ? chunk : o.lb_split_threshold_blocks;
+    if (chunk <= 0 || split <= 0) {
+        COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "fused CSR+BitBSR load-balance parameters must be positive");
+    }
+    out.chunk_blocks = chunk;
+    out.split_threshold_blocks = split;
+    alloc_n<uint64_t>(out.words, sp.kept_blocks);
+    if (sp.kept_blocks > 0) {
+        pack_words_kernel<<<grid_for(sp.kept_blocks, kThreads), kThreads, 0, s>>>(
+            sp.kept_blocks, sp.kept_col.as<int32_t>(), sp.kept_bitmap.as<uint32_t>(),
+            out.words.as<uint64_t>());
+        CUDA_LAUNCH_OK();
+    }
+    DevBuf cnt;
+    alloc_n<int32_t>(cnt, nbr);
+    alloc_n<int32_t>(out.item_row_ptr, nbr + 1);
+    if (nbr > 0) {
+        lb_count_kernel<<<grid_for(nbr, kThreads), kThreads, 0, s>>>(
+            nbr, sp.kept_block_row_ptr.as<int32_t>(), chunk, split, o.lb_style, cnt.as<int32_t>());
+        CUDA_LAUNCH_OK();
+    }
+    out.num_items = checked_i32(
+        exclusive_scan_total<int32_t, int32_t>(cnt.as<int32_t>(), out.item_row_ptr.as<int32_t>(), nbr, s),
+        "work items");
+    alloc_n<WorkItem>(out.items, out.num_items);
+    if (nbr > 0 && out.num_items > 0) {
+        lb_fill_kernel<<<grid_for(nbr, kThreads), kThreads, 0, s>>>(
+            nbr, sp.kept_block_row_ptr.as<int32_t>(), sp.kept_block_val_ptr.as<int32_t>(),
+            sp.kept_bitmap.as<uint32_t>(), out.item_row_ptr.as<int32_t>(), chunk, split,
+            o.lb_style, out.words.as<uint64_t>(), out.items.as<WorkItem>());
+        CUDA_LAUNCH_OK();
+    }
+}
+
+void build_chunks(const int32_t* res_rp, int32_t rows, int tau, int chunk_nnz, Chunks& out,
+                  cudaStream_t s) {
+    out.tau = tau;
+    out.num_chunks = 0;
+    out.long_rows = 0;
+    if (tau <= 0 || rows == 0) return;
+    DevBuf cnt, flag, crp;
+    alloc_n<int32_t>(cnt, rows);
+    alloc_n<int32_t>(flag, rows);
+    alloc_n<int64_t>(crp, rows + 1);
+    chunk_count_kernel<<<grid_for(rows, kThreads), kThreads, 0, s>>>(
+        rows, res_rp, tau, chunk_nnz, cnt.as<int32_t>(), flag.as<int32_t>());
+    CUDA_LAUNCH_OK();
+    out.num_chunks = exclusive_scan_total<int32_t, int64_t>(cnt.as<int32_t>(), crp.as<int64_t>(), rows, s);
+    {
+        DevBuf tmp;
+        alloc_n<int64_t>(tmp, rows + 1);
+        out.long_rows = exclusive_scan_total<int32_t, int64_t>(flag.as<int32_t>(), tmp.as<int64_t>(), rows, s);
+    }
+    checked_i32(out.num_chunks, "long-row chunks");
+    alloc_n<int32_t>(out.row, out.num_chunks);
+    alloc_n<int32_t>(out.pbegin, out.num_chunks);
+    alloc_n<int32_t>(out.pcount, out.num_chunks);
+    if (out.num_chunks > 0) {
+        chunk_fill_kernel<<<grid_for(rows, kThreads), kThreads, 0, s>>>(
+            rows, res_rp, tau, chunk_nnz, crp.as<int64_t>(), out.row.as<int32_t>(),
+            out.pbegin.as<int32_t>(), out.pcount.as<int32_t>());
+        CUDA_LAUNCH_OK();
+    }
+}
+
+template void validate_csr<double>(const cove_csr_desc&, cudaStream_t);
+template void validate_csr<float>(const cove_csr_desc&, cudaStream_t);
+template void build_full_bitbsr<double>(const cove_csr_desc&, FullBitBsr&, cudaStream_t);
+template void build_full_bitbsr<float>(const cove_csr_desc&, FullBitBsr&, cudaStream_t);
+template void build_split<double>(const FullBitBsr&, const cove_plan_opts&, SplitParts&, cudaStream_t);
+template void build_split<float>(const FullBitBsr&, const cove_plan_opts&, SplitParts&, cudaStream_t);
+
+}  // namespace cove

@@ -1,0 +1,62 @@
+// cove_convert.cuh -- device-resident streams of a plan and the builders.
+#pragma once
+
+#include "cove_internal.cuh"
+
+namespace cove {
+
+// Un-split BitBSR 8x4 (DeviceBitBsrMatrix, gpu_convert.cuh:251-351).
+struct FullBitBsr {
+    int32_t rows = 0, cols = 0, nbr = 0;
+    int64_t num_blocks = 0, nnz = 0;
+    DevBuf block_row_ptr;      // int32 nbr+1
+    DevBuf block_row_val_ptr;  // int32 nbr+1
+    DevBuf block_col_idx;      // int32 blocks
+    DevBuf bitmap;             // uint32 blocks
+    DevBuf values;             // T nnz
+};
+
+// CSR + BitBSR split (CsrBitBsrSplitMatrix, csr_bitbsr_split.hpp:15-51).
+struct SplitParts {
+    int64_t kept_blocks = 0, kept_nnz = 0, residual_blocks = 0, residual_nnz = 0;
+    int64_t cost_skipped_blocks = 0, cost_skipped_nnz = 0;
+    DevBuf kept_block_row_ptr;      // int32 nbr+1
+    DevBuf kept_block_row_val_ptr;  // int32 nbr+1
+    DevBuf kept_block_val_ptr;      // int32 kept_blocks+1
+    DevBuf kept_col;                // int32
+    DevBuf kept_bitmap;             // uint32
+    DevBuf kept_values;             // T
+    DevBuf res_row_ptr;             // int32 rows+1
+    DevBuf res_col;                 // int32
+    DevBuf res_values;              // T
+};
+
+// Packed words + work items (BitBsrLoadBalanceLayout8x4, common.cuh:24-29).
+struct Layout {
+    int chunk_blocks = 0, split_threshold_blocks = 0;
+    int64_t num_items = 0;
+    DevBuf words;         // uint64 kept_blocks
+    DevBuf items;         // WorkItem
+    DevBuf item_row_ptr;  // int32 nbr+1
+};
+
+// Long residual-row chunks (main_gpu_csr_bitbsr_spmv.cu:1155-1184).
+struct Chunks {
+    int tau = 0;
+    int64_t num_chunks = 0, long_rows = 0;
+    DevBuf row, pbegin, pcount;  // int32 each
+};
+
+template <typename T>
+void validate_csr(const cove_csr_desc& d, cudaStream_t s);
+template <typename T>
+void build_full_bitbsr(const cove_csr_desc& d, FullBitBsr& out, cudaStream_t s);
+unsigned long long move_mask_for(const cove_plan_opts& o);
+template <typename T>
+void build_split(const FullBitBsr& f, const cove_plan_opts& o, SplitParts& out, cudaStream_t s);
+void build_layout(const SplitParts& sp, int32_t nbr, const cove_plan_opts& o, Layout& out,
+                  cudaStream_t s);
+void build_chunks(const int32_t* res_rp, int32_t rows, int tau, int chunk_nnz, Chunks& out,
+                  cudaStream_t s);
+
+}  // namespace cove

@@ -1,0 +1,335 @@
+// spmv.cu -- fused load-balanced CSR+BitBSR SpMV for sm_100a.
+//
+// One launch computes y = A x over the kept 8x4 bit blocks and the CSR
+// residual.  It replaces the reference's unified kernels
+// (structural/src/main_gpu_csr_bitbsr_spmv.cu:517-634 lossless,
+// :755-860 joint/quantized) and the outlier correction (:967-979).
+//
+// Work split: one group of 8*SLOTS lanes owns one block row.  Lane (s, r)
+// of a group handles local row r of every SLOTS-th kept block, starting at
+// block s, so each lane covers one 4-cell row segment of a block per step:
+// the segment's values are contiguous (bit order is row-major), the four x
+// values are contiguous, and the value base of each block comes from a
+// two-step shuffle scan of the blocks' popcounts over the slots.  The same
+// lanes then stride the eight residual rows (SLOTS lanes per row), reduce
+// over the slots with two xor-shuffles, and store y once per row: no
+// atomics, no zero-fill, deterministic.
+//
+// Block rows with more than `heavy_limit` kept blocks and residual rows
+// longer than `long_tau` are finished by a second launch (one warp per
+// piece / 1024-nnz chunk, atomicAdd into y), which also applies the exact
+// BFP8 outlier side list.  Matrices without such rows need one launch.
+//
+// Accumulation: raw and dict routes accumulate in T (exact decode); the
+// BFP8 route accumulates in fp32 with x cast to float, as the reference's
+// joint kernel does (:795, :811).
+#include "cove_spmv.cuh"
+
+#include <algorithm>
+
+namespace cove {
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float bf16_to_float(uint16_t b) {
+    return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+// ---- value decoders --------------------------------------------------------
+
+template <typename T>
+struct RawDec {
+    using Acc = T;
+    const T* __restrict__ kept;
+    const T* __restrict__ res;
+    __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
+    __device__ __forceinline__ Acc kept_val(Acc, int64_t k) const { return kept[k]; }
+    __device__ __forceinline__ Acc res_val(int64_t p) const { return res[p]; }
+    __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return x[c]; }
+};
+
+template <typename T, typename IdxT, bool Smem>
+struct DictDec {
+    using Acc = T;
+    const IdxT* __restrict__ kept;
+    const IdxT* __restrict__ res;
+    const T* __restrict__ codebook;
+    int64_t size;
+    const T* cb;  // shared copy when Smem
+    __device__ __forceinline__ void prepare(void* smem) {
+        if constexpr (Smem) {
+            T* s = static_cast<T*>(smem);
+            for (int64_t i = threadIdx.x; i < size; i += blockDim.x) s[i] = codebook[i];
+            cb = s;
+        } else {
+            cb = codebook;
+        }
+    }
+    __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
+    __device__ __forceinline__ Acc kept_val(Acc, int64_t k) const { return cb[kept[k]]; }
+    __device__ __forceinline__ Acc res_val(int64_t p) const { return cb[res[p]]; }
+    __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return x[c]; }
+};
+
+template <typename T>
+struct Bfp8Dec {
+    using Acc = float;
+    const int8_t* __restrict__ kept;
+    const uint16_t* __restrict__ res;
+    const uint16_t* __restrict__ scale;
+    __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ float block_ctx(int64_t b) const { return bf16_to_float(scale[b]); }
+    __device__ __forceinline__ float kept_val(float sc, int64_t k) const {
+        return static_cast<float>(kept[k]) * sc;
+    }
+    __device__ __forceinline__ float res_val(int64_t p) const { return bf16_to_float(res[p]); }
+    __device__ __forceinline__ float xv(const T* __restrict__ x, int64_t c) const {
+        return static_cast<float>(x[c]);
+    }
+};
+
+// ---- main pass -----------------------------------------------------------------
+
+template <typename T, typename Dec, int SLOTS>
+__global__ void __launch_bounds__(kThreads)
+hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    dec.prepare(smem);
+    if constexpr (sizeof(Dec) > 0) {
+        // the shared codebook is complete before any lane reads it
+        __syncthreads();
+    }
+    using Acc = typename Dec::Acc;
+    constexpr int G = 8 * SLOTS;
+    const int lane = threadIdx.x & 31;
+    const int gl = lane & (G - 1);
+    const int s = gl >> 3;
+    const int r = gl & 7;
+    const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
+    const int64_t br = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
+    if (br >= k.nbr) return;  // the whole group leaves together
+
+    const int b0 = k.kept_brp[br];
+    int b1 = k.kept_brp[br + 1];
+    if (b1 - b0 > k.heavy_limit) b1 = b0 + k.heavy_limit;
+    int vb = k.kept_brvp[br];
+    const uint64_t* __restrict__ words = k.words;
+    Acc sum = Acc(0);
+
+#pragma unroll 2
+    for (int base = b0; base < b1; base += SLOTS) {
+        const int b = base + s;
+        const bool valid = b < b1;
+        const uint64_t w = valid ? __ldg(words + b) : 0ULL;
+        const uint32_t bm = static_cast<uint32_t>(w >> 32);
+        const int bc = static_cast<int>(w & 0x7fffffffULL);
+        const int pc = __popc(bm);
+        int incl = pc;
+        if constexpr (SLOTS > 1) {
+            const int t = __shfl_up_sync(gmask, incl, 8, G);
+            if (s >= 1) incl += t;
+        }
+        if constexpr (SLOTS > 2) {
+            const int t = __shfl_up_sync(gmask, incl, 16, G);
+            if (s >= 2) incl += t;
+        }
+        const int total = SLOTS > 1 ? __shfl_sync(gmask, incl, G - 1, G) : pc;
+        const int vblk = vb + incl - pc;
+        vb += total;
+        const uint32_t nib = (bm >> (4 * r)) & 0xFu;
+        if (nib) {
+            const Acc ctx = dec.block_ctx(b);
+            int v0 = vblk + __popc(bm & ((1u << (4 * r)) - 1u));
+            const int64_t c4 = static_cast<int64_t>(bc) * 4;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (nib & (1u << c)) {
+                    sum += dec.kept_val(ctx, v0) * dec.xv(x, c4 + c);
+                    ++v0;
+                }
+            }
+        }
+    }
+
+    const int64_t row = br * kBlockRows + r;
+    if (row < k.rows) {
+        const int rs = k.res_rp[row];
+        const int re = k.res_rp[row + 1];
+        if (!(k.long_tau > 0 && re - rs > k.long_tau)) {
+            const int32_t* __restrict__ rc = k.res_col;
+            for (int q = rs + s; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
+        }
+    }
+    if constexpr (SLOTS > 1) sum += __shfl_xor_sync(gmask, sum, 8, G);
+    if constexpr (SLOTS > 2) sum += __shfl_xor_sync(gmask, sum, 16, G);
+    if (s == 0 && row < k.rows) y[row] = static_cast<T>(sum);
+}
+
+// ---- overflow pass: heavy block-row pieces, long residual chunks, outliers ----
+
+template <typename T, typename Dec>
+__global__ void __launch_bounds__(kThreads)
+hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y,
+                       int heavy_ctas, int chunk_ctas, int64_t num_out,
+                       const int32_t* __restrict__ orow, const int32_t* __restrict__ ocol,
+                       const T* __restrict__ oval) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    dec.prepare(smem);
+    __syncthreads();
+    using Acc = typename Dec::Acc;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int cta = static_cast<int>(blockIdx.x);
+    if (cta < heavy_ctas) {
+        const int64_t t = static_cast<int64_t>(cta) * (kThreads / 32) + warp;
+        if (t >= k.num_heavy) return;
+        const int64_t br = k.heavy_br[t];
+        const int b0 = k.heavy_b0[t], b1 = k.heavy_b1[t];
+        const int s = lane >> 3, r = lane & 7;
+        int vb = k.kept_bvp[b0];
+        Acc sum = Acc(0);
+        for (int base = b0; base < b1; base += 4) {
+            const int b = base + s;
+            const bool valid = b < b1;
+            const uint64_t w = valid ? __ldg(k.words + b) : 0ULL;
+            const uint32_t bm = static_cast<uint32_t>(w >> 32);
+            const int bc = static_cast<int>(w & 0x7fffffffULL);
+            const int pc = __popc(bm);
+            int incl = pc;
+            int tt = __shfl_up_sync(0xffffffffu, incl, 8);
+            if (s >= 1) incl += tt;
+            tt = __shfl_up_sync(0xffffffffu, incl, 16);
+            if (s >= 2) incl += tt;
+            const int total = __shfl_sync(0xffffffffu, incl, 31);
+            const int vblk = vb + incl - pc;
+            vb += total;
+            const uint32_t nib = (bm >> (4 * r)) & 0xFu;
+            if (nib) {
+                const Acc ctx = dec.block_ctx(b);
+                int v0 = vblk + __popc(bm & ((1u << (4 * r)) - 1u));
+                const int64_t c4 = static_cast<int64_t>(bc) * 4;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if (nib & (1u << c)) {
+                        sum += dec.kept_val(ctx, v0) * dec.xv(x, c4 + c);
+                        ++v0;
+                    }
+                }
+            }
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        const int64_t row = br * kBlockRows + r;
+        if (s == 0 && row < k.rows) atomicAdd(&y[row], static_cast<T>(sum));
+        return;
+    }
+    if (cta < heavy_ctas + chunk_ctas) {
+        const int64_t c = static_cast<int64_t>(cta - heavy_ctas) * (kThreads / 32) + warp;
+        if (c >= k.num_chunks) return;
+        const int row = k.chunk_row[c];
+        const int pb = k.chunk_pbegin[c];
+        const int pn = k.chunk_pcount[c];
+        Acc sum = Acc(0);
+        for (int q = lane; q < pn; q += 32) sum += dec.res_val(pb + q) * dec.xv(x, k.res_col[pb + q]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) atomicAdd(&y[row], static_cast<T>(sum));
+        return;
+    }
+    // exact outlier correction in T (main_gpu_csr_bitbsr_spmv.cu:967-979)
+    const int64_t i = static_cast<int64_t>(cta - heavy_ctas - chunk_ctas) * kThreads + threadIdx.x;
+    if (i < num_out) atomicAdd(&y[orow[i]], oval[i] * x[ocol[i]]);
+}
+
+template <typename T, typename Dec>
+int launch_with(const KernelShape& k, Dec dec, size_t smem, const RouteValues& v, const void* xv,
+                void* yv, cudaStream_t s) {
+    const T* x = static_cast<const T*>(xv);
+    T* y = static_cast<T*>(yv);
+    int launches = 0;
+    if (k.nbr > 0) {
+        const int64_t groups_per_cta = kThreads / (8 * k.slots);
+        const int grid = grid_for(k.nbr, static_cast<int>(groups_per_cta));
+        switch (k.slots) {
+            case 1:
+                hybrid_main_kernel<T, Dec, 1><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+                break;
+            case 2:
+                hybrid_main_kernel<T, Dec, 2><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+                break;
+            default:
+                hybrid_main_kernel<T, Dec, 4><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+                break;
+        }
+        CUDA_LAUNCH_OK();
+        ++launches;
+    }
+    const int heavy_ctas = grid_for(k.num_heavy, kThreads / 32);
+    const int chunk_ctas = grid_for(k.num_chunks, kThreads / 32);
+    const int out_ctas = grid_for(v.num_outliers, kThreads);
+    if (heavy_ctas + chunk_ctas + out_ctas > 0) {
+        hybrid_overflow_kernel<T, Dec><<<heavy_ctas + chunk_ctas + out_ctas, kThreads, smem, s>>>(
+            k, dec, x, y, heavy_ctas, chunk_ctas, v.num_outliers, v.out_rows, v.out_cols,
+            static_cast<const T*>(v.out_vals));
+        CUDA_LAUNCH_OK();
+        ++launches;
+    }
+    return launches;
+}
+
+template <typename T>
+int launch_typed(const KernelShape& k, const RouteValues& v, const void* x, void* y,
+                 cudaStream_t s) {
+    switch (v.route) {
+        case COVE_ROUTE_HYBRID: {
+            RawDec<T> d{static_cast<const T*>(v.kept), static_cast<const T*>(v.res)};
+            return launch_with<T>(k, d, 0, v, x, y, s);
+        }
+        case COVE_ROUTE_DICT_U8: {
+            DictDec<T, uint8_t, true> d{static_cast<const uint8_t*>(v.kept),
+                                        static_cast<const uint8_t*>(v.res),
+                                        static_cast<const T*>(v.codebook), v.codebook_size, nullptr};
+            return launch_with<T>(k, d, static_cast<size_t>(v.codebook_size) * sizeof(T), v, x, y, s);
+        }
+        case COVE_ROUTE_DICT_U16: {
+            DictDec<T, uint16_t, false> d{static_cast<const uint16_t*>(v.kept),
+                                          static_cast<const uint16_t*>(v.res),
+                                          static_cast<const T*>(v.codebook), v.codebook_size, nullptr};
+            return launch_with<T>(k, d, 0, v, x, y, s);
+        }
+        case COVE_ROUTE_BFP8:
+        case COVE_ROUTE_BFP8_OUTLIER: {
+            Bfp8Dec<T> d{static_cast<const int8_t*>(v.kept), static_cast<const uint16_t*>(v.res),
+                         v.scale};
+            return launch_with<T>(k, d, 0, v, x, y, s);
+        }
+        default:
+            COVE_THROW(COVE_ERR_UNSUPPORTED, "unknown route");
+    }
+}
+
+}  // namespace
+
+int launch_hybrid_spmv(const KernelShape& k, const RouteValues& v, const void* x, void* y,
+                       cudaStream_t s) {
+    if (k.dtype == COVE_F64) return launch_typed<double>(k, v, x, y, s);
+    return launch_typed<float>(k, v, x, y, s);
+}
+
+int hybrid_spmv_launch_count(const KernelShape& k, const RouteValues& v) {
+    int n = k.nbr > 0 ? 1 : 0;
+    if (k.num_heavy + k.num_chunks + v.num_outliers > 0) ++n;
+    return n;
+}
+
+int choose_slots(int64_t nbr, int64_t kept_blocks, int64_t rows, int64_t residual_nnz) {
+    const double kb = nbr > 0 ? static_cast<double>(kept_blocks) / static_cast<double>(nbr) : 0.0;
+    const double rr = rows > 0 ? static_cast<double>(residual_nnz) / static_cast<double>(rows) : 0.0;
+    if (kb >= 8.0 || rr >= 8.0) return 4;
+    if (kb >= 1.5 || rr >= 2.5) return 2;
+    return 1;
+}
+
+}  // namespace cove

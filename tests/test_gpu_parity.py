@@ -1,0 +1,367 @@
+"""CUDA path vs the oracle / the reference's own outputs (needs a B200).
+
+Position and value streams are compared bit for bit; SpMV outputs are
+compared normwise with the reference's global_rel metric
+(max|y - y0| / max|y0|, structural/include/structural/spmv.hpp:73-89):
+lossless routes within 1e-12 (fp64) / 1e-6 (fp32), lossy routes within the
+reference's joint gate (1e-2) and within fp32-summation noise of the
+oracle's emulation of the same decoded values.
+"""
+import numpy as np
+import pytest
+
+import cove_b200 as cb
+import oracle as O
+from conftest import case_names
+
+pytestmark = pytest.mark.gpu
+
+LOSSLESS_TOL = {np.float64: 1e-12, np.float32: 1e-6}
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    import torch
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    yield
+
+
+def plan_for(rows, cols, rp, ci, v, **opts):
+    csr = cb.DeviceCsr.from_numpy(rows, cols, rp, ci, v)
+    return cb.Plan(csr, **opts)
+
+
+def gpu_spmv(plan, x, route=None):
+    import torch
+
+    xd = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    yd = torch.full((plan.info.rows,), float("nan"), dtype=xd.dtype, device="cuda")
+    plan.spmv(xd, yd, route=route)
+    torch.cuda.synchronize()
+    return yd.cpu().numpy()
+
+
+def assert_streams_equal_split(p, s, dtype):
+    assert np.array_equal(p.stream("kept_block_row_ptr"), s.kept.block_row_ptr)
+    assert np.array_equal(p.stream("kept_block_col_idx"), s.kept.block_col_idx)
+    assert np.array_equal(p.stream("kept_bitmap"), s.kept.bitmap_words)
+    assert np.array_equal(p.stream("kept_values"), s.kept.values.astype(dtype))
+    assert np.array_equal(p.stream("kept_block_val_ptr"), s.kept.block_val_ptr)
+    assert np.array_equal(p.stream("res_row_ptr"), s.res_row_ptr)
+    assert np.array_equal(p.stream("res_col_idx"), s.res_col_idx)
+    assert np.array_equal(p.stream("res_values"), s.res_values.astype(dtype))
+    i = p.info
+    assert (i.kept_blocks, i.residual_blocks, i.cost_skipped_blocks) == (
+        s.kept_blocks, s.residual_blocks, s.cost_skipped_blocks)
+    assert (i.kept_nnz, i.residual_nnz, i.cost_skipped_nnz) == (
+        s.kept_nnz, s.residual_nnz, s.cost_skipped_nnz)
+
+
+def _kat_csr(k):
+    return (k["rows"], k["cols"], np.array(k["row_ptr"], np.int64),
+            np.array(k["col_idx"], np.int32), np.array(k["values"], np.float64))
+
+
+@pytest.mark.parametrize("name", ["gpu_warp_direct_9x10", "gpu_warp_direct_empty_block_row",
+                                  "gpu_workspace_second", "gpu_wide_block_span",
+                                  "gpu_flag_lb_chunk2"])
+def test_kat_full_bitbsr_matches_cpu_converter(kats, name):
+    """test_gpu_convert.cu:124-296: GPU converter == convert_to_bitbsr(8x4)."""
+    rows, cols, rp, ci, v = _kat_csr(kats[name])
+    p = plan_for(rows, cols, rp, ci, v, keep_full_bitbsr=1)
+    b = O.convert_to_bitbsr(rows, cols, rp, ci, v)
+    assert np.array_equal(p.stream("full_block_row_ptr"), b.block_row_ptr)
+    assert np.array_equal(p.stream("full_block_col_idx"), b.block_col_idx)
+    assert np.array_equal(p.stream("full_bitmap"), b.bitmap_words)
+    assert np.array_equal(p.stream("full_values"), b.values)
+    assert np.array_equal(p.stream("full_block_row_val_ptr"), b.block_val_ptr[b.block_row_ptr])
+    if name == "gpu_warp_direct_9x10":
+        assert p.stream("full_block_row_val_ptr").tolist() == kats[name]["expect"]["block_row_val_ptr"]
+
+
+@pytest.mark.parametrize("name,style", [("gpu_flag_lb_chunk2", "device"),
+                                        ("gpu_split_threshold_chunking", "device"),
+                                        ("gpu_flag_lb_chunk2", "hybrid")])
+def test_kat_work_items(kats, name, style):
+    k = kats[name]
+    rows, cols, rp, ci, v = _kat_csr(k)
+    p = plan_for(rows, cols, rp, ci, v, split_policy="none", lb_chunk_blocks=k["chunk"],
+                 lb_split_threshold_blocks=k["split"], lb_style=style)
+    b = O.convert_to_bitbsr(rows, cols, rp, ci, v)
+    words, items, irp = O.lb_layout(b, k["chunk"], k["split"], style=style)
+    assert np.array_equal(p.stream("words"), words)
+    assert np.array_equal(p.stream("work_items"), items)
+    assert np.array_equal(p.stream("work_item_row_ptr"), irp)
+    if style == "device":
+        assert p.stream("work_items").tolist() == k["expect"]["items"]
+    y = gpu_spmv(p, np.arange(cols) % 13 * 0.25 - 1.5)
+    y0 = O.spmv_csr(rows, rp, ci, v, np.arange(cols) % 13 * 0.25 - 1.5)
+    assert O.compare_vectors(y0, y)[2] <= 1e-12
+
+
+@pytest.mark.parametrize("name", ["cli_hybrid_4x8_thr2", "cli_hybrid_4x8_cost_b2"])
+def test_kat_cli_counts(kats, name):
+    k = kats[name]
+    rows, cols, rp, ci, v = _kat_csr(k)
+    c = k["cost"]
+    p = plan_for(rows, cols, rp, ci, v, residual_threshold=k["threshold"], cost_bitmap_block=c[0],
+                 cost_bitmap_nnz=c[1], cost_csr_block=c[2], cost_csr_nnz=c[3])
+    for key, val in k["expect"].items():
+        assert getattr(p.info, key) == val, key
+    x = O.canonical_x(cols)
+    assert O.compare_vectors(O.spmv_csr(rows, rp, ci, v, x), gpu_spmv(p, x))[2] <= 1e-12
+
+
+SPLIT_OPTS = {"cost32": dict(residual_threshold=32),
+              "thr2": dict(residual_threshold=2, split_policy="threshold"),
+              "cost_b2": dict(residual_threshold=3, cost_bitmap_block=2.0)}
+
+
+@pytest.mark.parametrize("split_key", sorted(SPLIT_OPTS))
+def test_reference_cases_position_streams(ref_cases, split_key):
+    d = ref_cases
+    for name in case_names(d):
+        rows, cols = (int(v) for v in d[f"{name}/shape"])
+        rp, ci, v = d[f"{name}/row_ptr"], d[f"{name}/col_idx"], d[f"{name}/values"]
+        p = plan_for(rows, cols, rp, ci, v, keep_full_bitbsr=1, long_row_split=16,
+                     **SPLIT_OPTS[split_key])
+        q = f"{name}/{split_key}/"
+        assert np.array_equal(p.stream("kept_block_row_ptr"), d[q + "kept/block_row_ptr"]), name
+        assert np.array_equal(p.stream("kept_block_col_idx"), d[q + "kept/block_col_idx"]), name
+        assert np.array_equal(p.stream("kept_bitmap"), d[q + "kept/bitmap"]), name
+        assert np.array_equal(p.stream("kept_block_val_ptr"), d[q + "kept/block_val_ptr"]), name
+        assert np.array_equal(p.stream("kept_values"), d[q + "kept/values"]), name
+        assert np.array_equal(p.stream("res_row_ptr"), d[q + "res/row_ptr"]), name
+        assert np.array_equal(p.stream("res_col_idx"), d[q + "res/col_idx"]), name
+        assert np.array_equal(p.stream("res_values"), d[q + "res/values"]), name
+        if split_key == "cost32":
+            assert np.array_equal(p.stream("full_block_row_ptr"), d[f"{name}/full/block_row_ptr"])
+            assert np.array_equal(p.stream("full_block_col_idx"), d[f"{name}/full/block_col_idx"])
+            assert np.array_equal(p.stream("full_bitmap"), d[f"{name}/full/bitmap"])
+            assert np.array_equal(p.stream("full_values"), d[f"{name}/full/values"])
+        # packed words, work items and long chunks against the oracle
+        s = O.split(rows, cols, rp, ci, v, threshold=p.opts.residual_threshold,
+                    use_cost=p.opts.split_policy == 0,
+                    cost=(p.opts.cost_bitmap_block, 0.0, 0.0, 1.0))
+        words, items, irp = O.lb_layout(s.kept, 32, 32, style="hybrid")
+        assert np.array_equal(p.stream("words"), words), name
+        assert np.array_equal(p.stream("work_items"), items), name
+        assert np.array_equal(p.stream("work_item_row_ptr"), irp), name
+        cr, cpb, cpc, nl = O.long_chunks(s.res_row_ptr, 16)
+        assert np.array_equal(p.stream("chunk_row"), cr), name
+        assert np.array_equal(p.stream("chunk_pbegin"), cpb), name
+        assert np.array_equal(p.stream("chunk_pcount"), cpc), name
+        assert p.info.long_rows == nl
+        # lossless SpMV on the canonical x vs the reference's spmv_csr output
+        x = d[f"{name}/canonical_x"]
+        y = gpu_spmv(p, x)
+        tol = LOSSLESS_TOL[v.dtype.type]
+        assert O.compare_vectors(d[f"{name}/y_canonical"], y)[2] <= tol, name
+
+
+def test_reference_cases_value_codecs(ref_cases):
+    d = ref_cases
+    for name in case_names(d):
+        rows, cols = (int(v) for v in d[f"{name}/shape"])
+        rp, ci, v = d[f"{name}/row_ptr"], d[f"{name}/col_idx"], d[f"{name}/values"]
+        q = f"{name}/cost32/"
+        p8 = plan_for(rows, cols, rp, ci, v, value_codec="bfp8")
+        assert np.array_equal(p8.stream("bfp8_int8"), d[q + "bfp8/q"]), name
+        assert np.array_equal(p8.stream("bfp8_scale"), d[q + "bfp8/scale"]), name
+        assert np.array_equal(p8.stream("res_bf16"), O.bf16_half_up(d[q + "res/values"])), name
+        po = plan_for(rows, cols, rp, ci, v, value_codec="bfp8_outlier")
+        assert np.array_equal(po.stream("bfp8_int8"), d[q + "bfp8o/q"]), name
+        assert np.array_equal(po.stream("bfp8_scale"), d[q + "bfp8o/scale"]), name
+        assert np.array_equal(po.stream("outlier_rows"), d[q + "bfp8o/rows"]), name
+        assert np.array_equal(po.stream("outlier_cols"), d[q + "bfp8o/cols"]), name
+        assert np.array_equal(po.stream("outlier_vals"), d[q + "bfp8o/vals"]), name
+        po5 = plan_for(rows, cols, rp, ci, v, value_codec="bfp8_outlier", outlier_fraction=0.05)
+        assert np.array_equal(po5.stream("bfp8_int8"), d[q + "bfp8o5/q"]), name
+        assert np.array_equal(po5.stream("outlier_rows"), d[q + "bfp8o5/rows"]), name
+        pd = plan_for(rows, cols, rp, ci, v, value_codec="dict")
+        uniq, cbk, kc, rc = O.dict_intern(d[q + "kept/values"], d[q + "res/values"])
+        assert pd.info.value_cardinality == uniq
+        if uniq <= 65536:
+            assert np.array_equal(pd.stream("dict_codebook"), cbk), name
+            assert np.array_equal(pd.stream("dict_kept_idx").astype(np.int32), kc), name
+            assert np.array_equal(pd.stream("dict_res_idx").astype(np.int32), rc), name
+
+
+def _joint_oracle(rows, cols, rp, ci, v, x, fraction=None):
+    s = O.split(rows, cols, rp, ci, v)
+    if fraction is None:
+        q, sc = O.bfp8_encode(s.kept)
+        orow = ocol = np.zeros(0, np.int32)
+        oval = np.zeros(0, v.dtype)
+    else:
+        q, sc, orow, ocol, oval, _ = O.bfp8_outlier_encode(s.kept, fraction)
+    rb = O.bf16_half_up(s.res_values)
+    return O.joint_bfp8_spmv(s.kept, q, sc, s.res_row_ptr, s.res_col_idx, rb, orow, ocol, oval, x)
+
+
+@pytest.mark.parametrize("codec", ["bfp8", "bfp8_outlier", "dict", "auto"])
+def test_routes_spmv_and_gate(ref_cases, codec):
+    d = ref_cases
+    for name in case_names(d):
+        rows, cols = (int(v) for v in d[f"{name}/shape"])
+        rp, ci, v = d[f"{name}/row_ptr"], d[f"{name}/col_idx"], d[f"{name}/values"]
+        p = plan_for(rows, cols, rp, ci, v, value_codec=codec, long_row_split=16)
+        x = d[f"{name}/canonical_x"]
+        y0 = d[f"{name}/y_canonical"]
+        jr = p.info.joint_route
+        y = gpu_spmv(p, x, route=jr)
+        rel = O.compare_vectors(y0, y)[2]
+        if jr in (cb.ROUTE_DICT_U8, cb.ROUTE_DICT_U16):
+            assert rel <= LOSSLESS_TOL[v.dtype.type], name
+        else:
+            frac = 0.005 if jr == cb.ROUTE_BFP8_OUTLIER else None
+            ye = _joint_oracle(rows, cols, rp, ci, v, x, frac)
+            scale = max(np.abs(ye).max(), 1e-30)
+            assert np.abs(ye - y).max() / scale <= 2e-6, name
+            # the plan's gate value is this same global_rel (up to fp32 summation order)
+            assert abs(p.info.joint_rel_err - rel) <= 1e-5 + 1e-3 * rel, name
+            assert p.info.gate_pass == (rel <= 1e-2), name
+            want = jr if p.info.gate_pass else cb.ROUTE_HYBRID
+            assert p.info.dispatched_route == want
+
+
+def test_auto_route_choice_matches_reference_rule():
+    # uniq <= 256 -> dict_u8; > 256 -> bfp8 (main_gpu_csr_bitbsr_spmv.cu:1244-1245)
+    rows, cols, rp, ci, v = cb.synth_lapl2d(64, 64)
+    p = plan_for(rows, cols, rp, ci, v, value_codec="auto")
+    assert p.info.value_cardinality == 2 and p.info.joint_route == cb.ROUTE_DICT_U8
+    assert p.info.dispatched_route == cb.ROUTE_DICT_U8
+    assert p.stream("dict_codebook").tolist() == [4.0, -1.0]
+    v2 = v.copy()
+    v2[::3] = np.arange(v2[::3].size) + 5.0  # many distinct values
+    p2 = plan_for(rows, cols, rp, ci, v2, value_codec="auto")
+    assert p2.info.value_cardinality > 256 and p2.info.joint_route == cb.ROUTE_BFP8
+    p3 = plan_for(rows, cols, rp, ci, v2, value_codec="dict")
+    assert p3.info.joint_route == cb.ROUTE_DICT_U16
+    x = O.canonical_x(cols)
+    assert O.compare_vectors(O.spmv_csr(rows, rp, ci, v2, x), gpu_spmv(p3, x))[2] <= 1e-12
+
+
+def test_gate_failure_falls_back_to_lossless():
+    # values spanning many orders of magnitude inside each block: bfp8 fails the gate
+    rng = np.random.default_rng(3)
+    rows, cols, rp, ci, v = cb.synth_lapl2d(64, 64)
+    v = v * np.exp(rng.uniform(-20, 20, v.size))
+    p = plan_for(rows, cols, rp, ci, v, value_codec="bfp8")
+    assert p.info.gate_evaluated == 1 and p.info.joint_rel_err > 1e-2
+    assert p.info.gate_pass == 0 and p.info.dispatched_route == cb.ROUTE_HYBRID
+    x = O.canonical_x(cols)
+    y = np.empty(rows)
+    p.spmv_host(x, y)
+    assert O.compare_vectors(O.spmv_csr(rows, rp, ci, v, x), y)[2] <= 1e-12
+
+
+def test_edge_cases():
+    import torch
+
+    # empty matrix
+    p = plan_for(3, 4, np.zeros(4, np.int64), np.zeros(0, np.int32), np.zeros(0))
+    y = gpu_spmv(p, np.ones(4))
+    assert np.all(y == 0)
+    # stored zeros only
+    p = plan_for(2, 4, np.array([0, 2, 3]), np.array([0, 1, 2], np.int32), np.zeros(3))
+    assert p.info.nnz == 0 and np.all(gpu_spmv(p, np.ones(4)) == 0)
+    # int32 row_ptr input
+    rows, cols, rp, ci, v = cb.synth_lapl2d(16, 16)
+    csr = cb.DeviceCsr(rows, cols, torch.from_numpy(rp.astype(np.int32)).cuda(),
+                       torch.from_numpy(ci).cuda(), torch.from_numpy(v).cuda())
+    p = cb.Plan(csr)
+    x = O.canonical_x(cols)
+    assert O.compare_vectors(O.spmv_csr(rows, rp, ci, v, x), gpu_spmv(p, x))[2] <= 1e-12
+    # invalid inputs return status codes (validation on the device)
+    bad = [
+        (np.array([0, 2, 1, 3]), np.array([0, 1, 2], np.int32), "monotonic"),
+        (np.array([0, 2, 2, 3]), np.array([1, 0, 2], np.int32), "strictly increasing"),
+        (np.array([0, 2, 2, 3]), np.array([1, 1, 2], np.int32), "strictly increasing"),
+        (np.array([0, 2, 2, 3]), np.array([0, 9, 2], np.int32), "out of range"),
+    ]
+    for rp_b, ci_b, msg in bad:
+        with pytest.raises(cb.CoveError, match=msg):
+            plan_for(3, 4, rp_b, ci_b, np.ones(3))
+
+
+def test_long_rows_and_heavy_block_rows_overflow_path():
+    """Residual rows beyond the kernel's row split and block rows beyond the
+    heavy limit go through the second launch; results stay exact."""
+    rng = np.random.default_rng(11)
+    rows, cols = 4096, 40000
+    rp = [0]
+    ci = []
+    for r in range(rows):
+        if r == 5:
+            cs = np.arange(0, cols, 3)  # very long residual-ish row
+        elif 64 <= r < 72:
+            cs = np.arange(0, cols, 1)[: 20000]  # one block row with 5000 dense blocks
+        else:
+            cs = np.unique(rng.integers(0, cols, 6))
+        ci.extend(cs.tolist())
+        rp.append(len(ci))
+    rp = np.array(rp, np.int64)
+    ci = np.array(ci, np.int32)
+    v = rng.standard_normal(ci.size)
+    for codec in ("original", "bfp8_outlier"):
+        p = plan_for(rows, cols, rp, ci, v, value_codec=codec, gate_enable=0)
+        assert p.info.kernel_overflow_tasks > 0
+        assert p.launches() == 2
+        x = O.canonical_x(cols)
+        y0 = O.spmv_csr(rows, rp, ci, v, x)
+        y = gpu_spmv(p, x, route=p.info.joint_route)
+        if codec == "original":
+            assert O.compare_vectors(y0, y)[2] <= 1e-12
+        else:
+            assert O.compare_vectors(y0, y)[2] <= 1e-2
+
+
+def test_spmv_host_matches_device():
+    rows, cols, rp, ci, v = cb.synth_fem27(12, 10, 9, 3, seed=5)
+    p = plan_for(rows, cols, rp, ci, v, value_codec="auto")
+    x = cb.synth_vector("uniform_pm1", cols, seed=1)
+    yh = p.spmv_host(x)
+    yd = gpu_spmv(p, x)
+    assert np.array_equal(yh, yd)  # same kernel, deterministic stores
+
+
+@pytest.mark.parametrize("cfg", ["lapl2d_512", "fem27_64", "rmat_22"])
+def test_full_size_configs(cfg):
+    """BASELINE configs 1-3 at full size: streams bit-exact, routes, SpMV."""
+    rows, cols, rp, ci, v, x = cb.workload(cfg)
+    opts = dict(value_codec="auto", long_row_split=256)
+    p = plan_for(rows, cols, rp, ci, v, **opts)
+    s = O.split(rows, cols, rp, ci, v)
+    assert_streams_equal_split(p, s, v.dtype)
+    words, items, irp = O.lb_layout(s.kept, 32, 32, style="hybrid")
+    assert np.array_equal(p.stream("words"), words)
+    assert np.array_equal(p.stream("work_items"), items)
+    cr, cpb, cpc, nl = O.long_chunks(s.res_row_ptr, 256)
+    assert np.array_equal(p.stream("chunk_row"), cr) and np.array_equal(p.stream("chunk_pbegin"), cpb)
+    want_route = {"lapl2d_512": cb.ROUTE_DICT_U8, "fem27_64": cb.ROUTE_BFP8,
+                  "rmat_22": cb.ROUTE_BFP8}[cfg]
+    assert p.info.joint_route == want_route
+    y0 = O.spmv_csr(rows, rp, ci, v, x)
+    yl = gpu_spmv(p, x, route=cb.ROUTE_HYBRID)
+    assert O.compare_vectors(y0, yl)[2] <= LOSSLESS_TOL[v.dtype.type]
+    yj = gpu_spmv(p, x, route=want_route)
+    if want_route == cb.ROUTE_DICT_U8:
+        assert O.compare_vectors(y0, yj)[2] <= LOSSLESS_TOL[v.dtype.type]
+    else:
+        q, sc = O.bfp8_encode(s.kept)
+        assert np.array_equal(p.stream("bfp8_int8"), q) and np.array_equal(p.stream("bfp8_scale"), sc)
+        ye = O.joint_bfp8_spmv(s.kept, q, sc, s.res_row_ptr, s.res_col_idx,
+                               O.bf16_half_up(s.res_values), np.zeros(0, np.int32),
+                               np.zeros(0, np.int32), np.zeros(0, v.dtype), x)
+        assert np.abs(ye - yj).max() / np.abs(ye).max() <= 1e-5
+        # gate decision = the oracle's on the canonical x
+        xc = O.canonical_x(cols, v.dtype)
+        yc0 = O.spmv_csr(rows, rp, ci, v, xc)
+        yce = O.joint_bfp8_spmv(s.kept, q, sc, s.res_row_ptr, s.res_col_idx,
+                                O.bf16_half_up(s.res_values), np.zeros(0, np.int32),
+                                np.zeros(0, np.int32), np.zeros(0, v.dtype), xc)
+        rel = O.compare_vectors(yc0, yce)[2]
+        assert p.info.gate_pass == (rel <= 1e-2)
+        assert abs(p.info.joint_rel_err - rel) <= 1e-4 * max(rel, 1e-6) + 1e-6
