@@ -217,7 +217,7 @@ def run_fem(args):
     build_s = time.perf_counter() - t0
     del csr
     info = plan.info
-    route = info.dispatched_route
+    route = info.dispatched_route if args.route is None else cb.ROUTE_NAMES_INV[args.route]
     nnz_local = int(info.nnz)
 
     stream = torch.cuda.current_stream()
@@ -246,7 +246,7 @@ def run_fem(args):
                                              C.c_void_p(ybuf.data_ptr()),
                                              C.c_void_p(stream.cuda_stream)))
         else:
-            plan.spmv(xbuf, ybuf, stream=stream)
+            plan.spmv(xbuf, ybuf, route=route, stream=stream)
 
     # parity check of this very plan against a CPU SpMV of the same rows
     step(xw, y)
@@ -282,7 +282,7 @@ def run_fem(args):
     clocks = clk.stop()
     step_ms = [a.elapsed_time(b) for a, b in ev]
     ms = sum(step_ms) / len(step_ms)
-    launches = plan.launches()
+    launches = plan.launches(route)
 
     # end to end through the public C ABI with host buffers (pinned)
     xh = torch.from_numpy(x_window).pin_memory()
@@ -347,6 +347,8 @@ def run_fem(args):
             "config": {"workload": f"fem27 {FEM['nx']}x{FEM['ny']}x{FEM['nz'] * world} nodes x3 dof"
                                    f" ({'z-slab per rank, ' if world > 1 else ''}nnz={int(nnz_total)})",
                        "route": cb.ROUTE_NAMES[route], "requested_codec": args.codec,
+                       "dispatched_route": cb.ROUTE_NAMES[info.dispatched_route],
+                       "joint_route": cb.ROUTE_NAMES[info.joint_route],
                        "gate_rel_err": info.joint_rel_err, "gate_pass": bool(info.gate_pass),
                        "l2": "flushed between steps (256 MiB write, outside the timed events)",
                        "parallelism": f"row-block z-slabs x{world}, NCCL halo" if world > 1 else "1 GPU",
@@ -379,6 +381,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="fem27", choices=["fem27"])
     ap.add_argument("--codec", default="auto")
+    ap.add_argument("--route", default=None,
+                    help="time this route instead of the dispatched one (analysis only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

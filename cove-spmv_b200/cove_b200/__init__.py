@@ -22,6 +22,8 @@ CODEC = {"original": 0, "auto": 1, "dict": 2, "bfp8": 3, "bfp8_outlier": 4}
 ROUTE_HYBRID, ROUTE_DICT_U8, ROUTE_DICT_U16, ROUTE_BFP8, ROUTE_BFP8_OUTLIER = range(5)
 ROUTE_NAMES = {0: "original", 1: "dict_u8_lossless", 2: "dict_u16_lossless",
                3: "bfp8_blocks+bf16_residual", 4: "bfp8_outlier_blocks+bf16_residual"}
+ROUTE_NAMES_INV = {v: k for k, v in ROUTE_NAMES.items()}
+ROUTE_NAMES_INV.update({"hybrid": 0, "dict_u8": 1, "dict_u16": 2, "bfp8": 3, "bfp8_outlier": 4})
 SPLIT = {"cost_gated": 0, "threshold": 1, "none": 2}
 LB_STYLE = {"hybrid": 0, "device": 1}
 
@@ -85,6 +87,24 @@ class PlanInfo(C.Structure):
                 ("kernel_slots", C.c_int32), ("kernel_overflow_tasks", C.c_int32)]
 
 
+class HybridDesc(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("num_block_rows", C.c_int32),
+                ("dtype", C.c_int32), ("kept_blocks", C.c_int64), ("kept_nnz", C.c_int64),
+                ("residual_nnz", C.c_int64), ("block_row_ptr", C.c_void_p),
+                ("block_row_val_ptr", C.c_void_p), ("words", C.c_void_p),
+                ("res_row_ptr", C.c_void_p), ("res_col_idx", C.c_void_p),
+                ("long_row_tau", C.c_int32), ("num_chunks", C.c_int64), ("chunk_row", C.c_void_p),
+                ("chunk_pbegin", C.c_void_p), ("chunk_pcount", C.c_void_p)]
+
+
+class ValuesDesc(C.Structure):
+    _fields_ = [("route", C.c_int32), ("kept", C.c_void_p), ("res", C.c_void_p),
+                ("block_scale", C.c_void_p), ("codebook", C.c_void_p),
+                ("codebook_size", C.c_int64), ("num_outliers", C.c_int64),
+                ("outlier_rows", C.c_void_p), ("outlier_cols", C.c_void_p),
+                ("outlier_vals", C.c_void_p)]
+
+
 class CgResult(C.Structure):
     _fields_ = [("iterations", C.c_int32), ("rs_initial", C.c_double),
                 ("rs_final", C.c_double), ("ms_total", C.c_double), ("ms_spmv", C.c_double)]
@@ -94,9 +114,9 @@ class CgResult(C.Structure):
 EXPORTED = [
     "cove_last_error", "cove_status_string", "cove_version", "cove_plan_opts_default",
     "cove_plan_build", "cove_plan_destroy", "cove_plan_get_info", "cove_route_name",
-    "cove_plan_stream", "cove_spmv", "cove_spmv_route", "cove_spmv_host",
+    "cove_plan_stream", "cove_hybrid_spmv", "cove_spmv", "cove_spmv_route", "cove_spmv_host",
     "cove_spmv_launches", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
-    "cove_dist_id_bytes", "cove_dist_make_id", "cove_dist_create", "cove_dist_destroy",
+    "cove_dist_halo_plan", "cove_dist_id_bytes", "cove_dist_make_id", "cove_dist_create", "cove_dist_destroy",
     "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv",
     "cove_rng_u64", "cove_rng_uniform01", "cove_synth_lapl2d", "cove_synth_lapl3d",
     "cove_synth_fem27", "cove_synth_fem27_rows", "cove_synth_rmat", "cove_synth_blocksparse", "cove_synth_vector",
@@ -131,6 +151,7 @@ def _setup(L):
     L.cove_route_name.restype = C.c_char_p
     L.cove_route_name.argtypes = [i32]
     L.cove_plan_stream.argtypes = [vp, i32, vp, C.c_size_t, C.POINTER(C.c_size_t), vp]
+    L.cove_hybrid_spmv.argtypes = [C.POINTER(HybridDesc), C.POINTER(ValuesDesc), vp, vp, vp]
     L.cove_spmv.argtypes = [vp, vp, vp, vp]
     L.cove_spmv_route.argtypes = [vp, i32, vp, vp, vp]
     L.cove_spmv_host.argtypes = [vp, vp, vp, vp]
@@ -139,6 +160,8 @@ def _setup(L):
     L.cove_compare_vectors.argtypes = [vp, vp, i64, i32, vp, vp]
     L.cove_canonical_x.argtypes = [vp, i64, i32, vp]
     L.cove_cg_solve.argtypes = [vp, vp, vp, i32, C.POINTER(CgResult), vp]
+    L.cove_dist_halo_plan.restype = i32
+    L.cove_dist_halo_plan.argtypes = [i32, i32, vp, vp, i32]
     L.cove_dist_id_bytes.restype = C.c_size_t
     L.cove_dist_make_id.argtypes = [vp]
     L.cove_dist_create.argtypes = [i32, i32, vp, vp, i32, i64, i64, i64, i64, i64, i32,
@@ -170,6 +193,7 @@ def _setup(L):
     L.cove_synth_vector_device.restype = C.c_int
     L.cove_synth_vector_device.argtypes = [i32, u64, u64, i64, i64, vp, vp]
     for fn in ("cove_plan_build", "cove_plan_destroy", "cove_plan_get_info", "cove_plan_stream",
+               "cove_hybrid_spmv",
                "cove_spmv", "cove_spmv_route", "cove_spmv_host", "cove_compare_vectors",
                "cove_canonical_x", "cove_cg_solve", "cove_dist_make_id", "cove_dist_create",
                "cove_dist_destroy", "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv"):
@@ -334,6 +358,18 @@ class Plan:
         check(lib().cove_cg_solve(self._h, _dptr(b), _dptr(x), iters, C.byref(res),
                                   _stream_handle(stream)))
         return res
+
+
+def halo_plan(rank, blocks):
+    """Transfer plan of `rank` given every rank's (row_begin, row_end,
+    window_begin, window_len); list of (peer, send_off, send_n, recv_off, recv_n)."""
+    b = np.ascontiguousarray(np.array(blocks, np.int64).reshape(-1))
+    world = b.size // 4
+    out = np.zeros(5 * max(world, 1), np.int64)
+    n = lib().cove_dist_halo_plan(rank, world, _np_ptr(b), _np_ptr(out), world)
+    if n < 0:
+        raise CoveError(1, "halo is not covered by other ranks' row blocks")
+    return [tuple(int(v) for v in out[5 * i: 5 * i + 5]) for i in range(n)]
 
 
 def compare_vectors(ref, got, stream=None):

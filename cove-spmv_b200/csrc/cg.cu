@@ -14,6 +14,7 @@
 // with ncclSend/ncclRecv from the neighbouring ranks first.
 #include "cove_plan.cuh"
 
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <chrono>
@@ -97,9 +98,60 @@ __global__ void cg_p_kernel(int64_t n, const double* __restrict__ scal, int rs_s
         p[i] = r[i] + beta * p[i];
 }
 
+
+// NCCL is resolved at run time: a process that already holds libnccl.so.2
+// (PyTorch loads its own) keeps using that copy, and the library itself
+// never forces a second NCCL version into the process.
+struct NcclApi {
+    bool loaded = false;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl() {
+    static NcclApi api;
+    if (api.loaded) return api;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) COVE_THROW(COVE_ERR_NCCL, std::string("cannot load libnccl.so.2: ") + dlerror());
+    auto sym = [&](const char* name) {
+        void* f = dlsym(h, name);
+        if (!f) COVE_THROW(COVE_ERR_NCCL, std::string("libnccl.so.2 lacks ") + name);
+        return f;
+    };
+    api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(sym("ncclGetUniqueId"));
+    api.CommInitRankConfig = reinterpret_cast<decltype(api.CommInitRankConfig)>(sym("ncclCommInitRankConfig"));
+    api.CommGetAsyncError = reinterpret_cast<decltype(api.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
+    api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(sym("ncclCommAbort"));
+    api.CommFinalize = reinterpret_cast<decltype(api.CommFinalize)>(sym("ncclCommFinalize"));
+    api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym("ncclCommDestroy"));
+    api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(sym("ncclGroupStart"));
+    api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
+    api.Send = reinterpret_cast<decltype(api.Send)>(sym("ncclSend"));
+    api.Recv = reinterpret_cast<decltype(api.Recv)>(sym("ncclRecv"));
+    api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(sym("ncclAllReduce"));
+    api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
+    api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
+    api.loaded = true;
+    return api;
+}
+
 inline void nccl_ok(ncclResult_t r, const char* what) {
     if (r != ncclSuccess && r != ncclInProgress) {
-        COVE_THROW(COVE_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+        COVE_THROW(COVE_ERR_NCCL, std::string(what) + ": " + nccl().GetErrorString(r));
     }
 }
 
@@ -130,16 +182,16 @@ void wait_comm_ready(ncclComm_t comm, int timeout_ms) {
     const auto t0 = std::chrono::steady_clock::now();
     while (true) {
         ncclResult_t st = ncclSuccess;
-        nccl_ok(ncclCommGetAsyncError(comm, &st), "ncclCommGetAsyncError");
+        nccl_ok(nccl().CommGetAsyncError(comm, &st), "ncclCommGetAsyncError");
         if (st == ncclSuccess) return;
         if (st != ncclInProgress) {
-            ncclCommAbort(comm);
-            COVE_THROW(COVE_ERR_NCCL, std::string("NCCL communicator error: ") + ncclGetErrorString(st));
+            nccl().CommAbort(comm);
+            COVE_THROW(COVE_ERR_NCCL, std::string("NCCL communicator error: ") + nccl().GetErrorString(st));
         }
         const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
                             std::chrono::steady_clock::now() - t0).count();
         if (ms > timeout_ms) {
-            ncclCommAbort(comm);
+            nccl().CommAbort(comm);
             COVE_THROW(COVE_ERR_TIMEOUT, "NCCL communicator did not become ready in time");
         }
         std::this_thread::sleep_for(std::chrono::microseconds(200));
@@ -156,17 +208,17 @@ void wait_stream(cove_dist* d, cudaStream_t s) {
         if (q != cudaErrorNotReady) CUDA_OK(q);
         if (d && d->comm) {
             ncclResult_t st = ncclSuccess;
-            ncclCommGetAsyncError(d->comm, &st);
+            nccl().CommGetAsyncError(d->comm, &st);
             if (st != ncclSuccess && st != ncclInProgress) {
-                ncclCommAbort(d->comm);
+                nccl().CommAbort(d->comm);
                 d->comm = nullptr;
-                COVE_THROW(COVE_ERR_NCCL, std::string("NCCL async error: ") + ncclGetErrorString(st));
+                COVE_THROW(COVE_ERR_NCCL, std::string("NCCL async error: ") + nccl().GetErrorString(st));
             }
         }
         const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
                             std::chrono::steady_clock::now() - t0).count();
         if (d && ms > d->timeout_ms) {
-            if (d->comm) ncclCommAbort(d->comm);
+            if (d->comm) nccl().CommAbort(d->comm);
             d->comm = nullptr;
             COVE_THROW(COVE_ERR_TIMEOUT, "stream did not finish before the deadline");
         }
@@ -176,23 +228,23 @@ void wait_stream(cove_dist* d, cudaStream_t s) {
 
 void halo(cove_dist* d, double* xw, cudaStream_t s) {
     if (!d || d->world == 1 || d->xfers.empty()) return;
-    nccl_ok(ncclGroupStart(), "ncclGroupStart");
+    nccl_ok(nccl().GroupStart(), "ncclGroupStart");
     for (const auto& x : d->xfers) {
         if (x.send_n > 0)
-            nccl_ok(ncclSend(xw + x.send_off, static_cast<size_t>(x.send_n), ncclFloat64, x.peer,
+            nccl_ok(nccl().Send(xw + x.send_off, static_cast<size_t>(x.send_n), ncclFloat64, x.peer,
                              d->comm, s), "ncclSend");
         if (x.recv_n > 0)
-            nccl_ok(ncclRecv(xw + x.recv_off, static_cast<size_t>(x.recv_n), ncclFloat64, x.peer,
+            nccl_ok(nccl().Recv(xw + x.recv_off, static_cast<size_t>(x.recv_n), ncclFloat64, x.peer,
                              d->comm, s), "ncclRecv");
     }
-    const ncclResult_t r = ncclGroupEnd();
+    const ncclResult_t r = nccl().GroupEnd();
     nccl_ok(r, "ncclGroupEnd");
     if (r == ncclInProgress) wait_comm_ready(d->comm, d->timeout_ms);
 }
 
 void allreduce_scalar(cove_dist* d, double* v, cudaStream_t s) {
     if (!d || d->world == 1) return;
-    const ncclResult_t r = ncclAllReduce(v, v, 1, ncclFloat64, ncclSum, d->comm, s);
+    const ncclResult_t r = nccl().AllReduce(v, v, 1, ncclFloat64, ncclSum, d->comm, s);
     nccl_ok(r, "ncclAllReduce");
     if (r == ncclInProgress) wait_comm_ready(d->comm, d->timeout_ms);
 }
@@ -302,13 +354,41 @@ cove_status cove_cg_solve(const cove_plan* P, const void* b, void* x, int32_t it
     });
 }
 
+int32_t cove_dist_halo_plan(int32_t rank, int32_t world, const int64_t* blocks4, int64_t* xfers5,
+                            int32_t cap) {
+    if (!blocks4 || !xfers5 || rank < 0 || rank >= world) return -1;
+    const int64_t row_begin = blocks4[4 * rank], row_end = blocks4[4 * rank + 1];
+    const int64_t wb = blocks4[4 * rank + 2], wl = blocks4[4 * rank + 3];
+    int n = 0;
+    int64_t covered = row_end - row_begin;
+    for (int q = 0; q < world; ++q) {
+        if (q == rank) continue;
+        const int64_t qb = blocks4[4 * q], qe = blocks4[4 * q + 1];
+        const int64_t qwb = blocks4[4 * q + 2], qwl = blocks4[4 * q + 3];
+        // my rows inside q's window go to q; q's rows inside my window come from q
+        const int64_t sb = std::max(row_begin, qwb), se = std::min(row_end, qwb + qwl);
+        const int64_t rb = std::max(qb, wb), re = std::min(qe, wb + wl);
+        const int64_t sn = std::max<int64_t>(0, se - sb), rn = std::max<int64_t>(0, re - rb);
+        if (sn == 0 && rn == 0) continue;
+        if (n >= cap) return -1;
+        xfers5[5 * n + 0] = q;
+        xfers5[5 * n + 1] = sn > 0 ? sb - wb : 0;
+        xfers5[5 * n + 2] = sn;
+        xfers5[5 * n + 3] = rn > 0 ? rb - wb : 0;
+        xfers5[5 * n + 4] = rn;
+        covered += rn;
+        ++n;
+    }
+    return covered == wl ? n : -1;
+}
+
 size_t cove_dist_id_bytes(void) { return sizeof(ncclUniqueId); }
 
 cove_status cove_dist_make_id(void* id_out) {
     return guarded([&] {
         if (!id_out) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null id");
         ncclUniqueId id;
-        nccl_ok(ncclGetUniqueId(&id), "ncclGetUniqueId");
+        nccl_ok(nccl().GetUniqueId(&id), "ncclGetUniqueId");
         std::memcpy(id_out, &id, sizeof(id));
     });
 }
@@ -344,7 +424,7 @@ cove_status cove_dist_create(int32_t rank, int32_t world, const void* nccl_id,
             std::memcpy(&id, nccl_id, sizeof(id));
             ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
             cfg.blocking = 0;
-            nccl_ok(ncclCommInitRankConfig(&d->comm, world, id, rank, &cfg), "ncclCommInitRankConfig");
+            nccl_ok(nccl().CommInitRankConfig(&d->comm, world, id, rank, &cfg), "ncclCommInitRankConfig");
             wait_comm_ready(d->comm, d->timeout_ms);
             // share every rank's (row_begin, row_end, window_begin, window_len)
             DevBuf all;
@@ -355,31 +435,24 @@ cove_status cove_dist_create(int32_t rank, int32_t world, const void* nccl_id,
             CUDA_OK(cudaMemcpyAsync(all.as<int64_t>() + 4 * rank, mine, sizeof(mine),
                                     cudaMemcpyHostToDevice, s));
             const ncclResult_t ag =
-                ncclAllGather(all.as<int64_t>() + 4 * rank, all.p, 4, ncclInt64, d->comm, s);
+                nccl().AllGather(all.as<int64_t>() + 4 * rank, all.p, 4, ncclInt64, d->comm, s);
             nccl_ok(ag, "ncclAllGather");
             if (ag == ncclInProgress) wait_comm_ready(d->comm, d->timeout_ms);
             wait_stream(d, s);
             std::vector<int64_t> h(4 * world);
             CUDA_OK(cudaMemcpy(h.data(), all.p, h.size() * 8, cudaMemcpyDeviceToHost));
             cudaStreamDestroy(s);
-            for (int q = 0; q < world; ++q) {
-                if (q == rank) continue;
-                const int64_t qb = h[4 * q], qe = h[4 * q + 1], qwb = h[4 * q + 2], qwl = h[4 * q + 3];
-                // my rows inside q's window go to q; q's rows inside my window come from q
-                const int64_t sb = std::max(row_begin, qwb), se = std::min(row_end, qwb + qwl);
-                const int64_t rb = std::max(qb, window_begin), re = std::min(qe, window_begin + window_len);
-                cove_dist::Xfer x{q, sb - window_begin, std::max<int64_t>(0, se - sb), rb - window_begin,
-                                  std::max<int64_t>(0, re - rb)};
-                if (x.send_n > 0 || x.recv_n > 0) d->xfers.push_back(x);
-            }
-            // the window outside the row block must be covered by received ranges
-            int64_t covered = row_end - row_begin;
-            for (const auto& x : d->xfers) covered += x.recv_n;
-            if (covered != window_len) {
+            std::vector<int64_t> xf(5 * static_cast<size_t>(world));
+            const int nx = cove_dist_halo_plan(rank, world, h.data(), xf.data(), world);
+            if (nx < 0) {
                 COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "halo is not covered by other ranks' row blocks");
             }
+            for (int i = 0; i < nx; ++i) {
+                d->xfers.push_back(cove_dist::Xfer{static_cast<int>(xf[5 * i]), xf[5 * i + 1], xf[5 * i + 2],
+                                                   xf[5 * i + 3], xf[5 * i + 4]});
+            }
         } catch (...) {
-            if (d->comm) ncclCommAbort(d->comm);
+            if (d->comm) nccl().CommAbort(d->comm);
             delete d;
             throw;
         }
@@ -391,9 +464,9 @@ cove_status cove_dist_destroy(cove_dist* d) {
     return guarded([&] {
         if (!d) return;
         if (d->comm) {
-            ncclCommFinalize(d->comm);
+            nccl().CommFinalize(d->comm);
             wait_comm_ready(d->comm, d->timeout_ms);
-            ncclCommDestroy(d->comm);
+            nccl().CommDestroy(d->comm);
         }
         delete d;
     });

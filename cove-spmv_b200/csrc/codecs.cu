@@ -289,7 +289,7 @@ void encode_bfp8_outlier(const SplitParts& sp, int32_t nbr, double fraction, Dev
     const int64_t nnz = sp.kept_nnz;
     DevBuf flag;
     alloc_n<uint8_t>(flag, nnz);
-    CUDA_OK(cudaMemsetAsync(flag.p, 0, static_cast<size_t>(nnz) + 1, s));
+    CUDA_OK(cudaMemsetAsync(flag.p, 0, flag.bytes, s));
     double thr = 0.0;
     if (fraction > 0.0 && nnz > 0) {
         // size_t((1.0 - P) * nnz), clamped (gpu_value_codecs.cuh:384-388)

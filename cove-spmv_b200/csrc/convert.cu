@@ -589,7 +589,7 @@ void build_split(const FullBitBsr& f, const cove_plan_opts& o, SplitParts& out, 
     alloc_n<int32_t>(sb, nbr);
     alloc_n<int32_t>(sn, nbr);
     alloc_n<int32_t>(rc, rows);
-    CUDA_OK(cudaMemsetAsync(rc.p, 0, static_cast<size_t>(rows) * 4 + 4, s));
+    CUDA_OK(cudaMemsetAsync(rc.p, 0, rc.bytes, s));
     const int grid = grid_for(static_cast<int64_t>(nbr) * 32, kThreads);
     if (nbr > 0) {
         split_count_kernel<<<grid, kThreads, 0, s>>>(

@@ -532,6 +532,59 @@ cove_status cove_spmv_route(const cove_plan* P, int32_t route, const void* x, vo
     });
 }
 
+cove_status cove_hybrid_spmv(const cove_hybrid_desc* a, const cove_values_desc* v, const void* x,
+                             void* y, void* stream) {
+    return guarded([&] {
+        if (!a || !v) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null descriptor");
+        if (a->rows < 0 || a->cols < 0 || a->num_block_rows != (a->rows + kBlockRows - 1) / kBlockRows) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "fused CSR+BitBSR shape mismatch");
+        }
+        if (a->dtype != COVE_F64 && a->dtype != COVE_F32) COVE_THROW(COVE_ERR_UNSUPPORTED, "dtype");
+        if (v->route < COVE_ROUTE_HYBRID || v->route > COVE_ROUTE_BFP8_OUTLIER) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "unknown route");
+        }
+        if (a->rows > 0 && (!a->block_row_ptr || !a->block_row_val_ptr || !a->res_row_ptr || !y)) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null stream");
+        }
+        if (a->num_chunks > 0 && (!a->chunk_row || !a->chunk_pbegin || !a->chunk_pcount)) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null long-row chunk stream");
+        }
+        KernelShape k;
+        k.dtype = a->dtype;
+        k.rows = a->rows;
+        k.cols = a->cols;
+        k.nbr = a->num_block_rows;
+        k.kept_brp = a->block_row_ptr;
+        k.kept_brvp = a->block_row_val_ptr;
+        k.words = a->words;
+        k.res_rp = a->res_row_ptr;
+        k.res_col = a->res_col_idx;
+        k.slots = choose_slots(a->num_block_rows, a->kept_blocks, a->rows, a->residual_nnz);
+        k.long_tau = a->num_chunks > 0 ? a->long_row_tau : 0;
+        k.num_chunks = a->num_chunks > 0 ? a->num_chunks : 0;
+        k.chunk_row = a->chunk_row;
+        k.chunk_pbegin = a->chunk_pbegin;
+        k.chunk_pcount = a->chunk_pcount;
+        RouteValues rv;
+        rv.route = v->route;
+        rv.kept = v->kept;
+        rv.res = v->res;
+        rv.scale = v->block_scale;
+        rv.codebook = v->codebook;
+        rv.codebook_size = v->codebook_size;
+        if (v->route == COVE_ROUTE_BFP8_OUTLIER) {
+            rv.num_outliers = v->num_outliers;
+            rv.out_rows = v->outlier_rows;
+            rv.out_cols = v->outlier_cols;
+            rv.out_vals = v->outlier_vals;
+        }
+        if (v->route == COVE_ROUTE_DICT_U8 && v->codebook_size > 256) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "u8 dictionary holds at most 256 values");
+        }
+        launch_hybrid_spmv(k, rv, x, y, static_cast<cudaStream_t>(stream));
+    });
+}
+
 cove_status cove_spmv(const cove_plan* P, const void* x, void* y, void* stream) {
     if (!P) {
         cove::set_last_error("null plan");

@@ -222,6 +222,48 @@ COVE_API cove_status cove_plan_stream(const cove_plan* plan, int32_t which, void
  */
 COVE_API cove_status cove_spmv(const cove_plan* plan, const void* x, void* y, void* stream);
 
+/*
+ * Caller-owned streams of the fused hybrid operator (the argument lists of
+ * run_csr_bitbsr_fused_8x4_lb / _bfp8 / _dict / _bfp8_outlier,
+ * main_gpu_csr_bitbsr_spmv.cu:636-650, :899-915, :932-948, :984-1003).
+ * All pointers are device pointers; the flag bit of the words is ignored.
+ */
+typedef struct {
+    int32_t rows, cols, num_block_rows, dtype;
+    int64_t kept_blocks, kept_nnz, residual_nnz;
+    const int32_t* block_row_ptr;      /* kept BitBSR, nbr+1 (DeviceBitBsrMatrix::block_row_ptr) */
+    const int32_t* block_row_val_ptr;  /* nbr+1 (DeviceBitBsrMatrix::block_row_val_ptr) */
+    const uint64_t* words;             /* packed col/flag/bitmap per kept block */
+    const int32_t* res_row_ptr;        /* rows+1 */
+    const int32_t* res_col_idx;        /* residual nnz */
+    int32_t long_row_tau;              /* residual rows longer than this use the chunks */
+    int64_t num_chunks;
+    const int32_t* chunk_row;
+    const int32_t* chunk_pbegin;
+    const int32_t* chunk_pcount;
+} cove_hybrid_desc;
+
+typedef struct {
+    int32_t route;                 /* cove_route */
+    const void* kept;              /* T / uint8 / uint16 codes / int8, per kept nnz */
+    const void* res;               /* T / codes / uint16 bf16, per residual nnz */
+    const uint16_t* block_scale;   /* bfp8: bf16 bits per kept block */
+    const void* codebook;          /* dict: T values */
+    int64_t codebook_size;
+    int64_t num_outliers;          /* bfp8_outlier side list */
+    const int32_t* outlier_rows;
+    const int32_t* outlier_cols;
+    const void* outlier_vals;
+} cove_values_desc;
+
+/*
+ * y = A x over caller-owned streams.  Replaces the four launchers of
+ * main_gpu_csr_bitbsr_spmv.cu:636-1029; the caller need not zero y.
+ * Asynchronous on `stream`.
+ */
+COVE_API cove_status cove_hybrid_spmv(const cove_hybrid_desc* a, const cove_values_desc* v,
+                                      const void* x, void* y, void* stream);
+
 /* Same on an explicit route (the plan must hold that route's streams). */
 COVE_API cove_status cove_spmv_route(const cove_plan* plan, int32_t route, const void* x, void* y,
                             void* stream);
@@ -288,6 +330,17 @@ COVE_API cove_status cove_dist_create(int32_t rank, int32_t world, const void* n
                              int64_t window_begin, int64_t window_len,
                              int32_t timeout_ms, cove_dist** out);
 COVE_API cove_status cove_dist_destroy(cove_dist* d);
+
+/*
+ * Halo transfer plan of `rank` (host only, no communicator): blocks4 holds
+ * every rank's {row_begin, row_end, window_begin, window_len}; writes up to
+ * `cap` records {peer, send_offset, send_count, recv_offset, recv_count}
+ * (offsets into this rank's window) and returns their number, or -1 when
+ * the window outside the rank's rows is not covered exactly by other ranks'
+ * rows.  cove_dist_create uses it after an allgather of the blocks.
+ */
+COVE_API int32_t cove_dist_halo_plan(int32_t rank, int32_t world, const int64_t* blocks4,
+                                     int64_t* xfers5, int32_t cap);
 
 /* Halo exchange of a window vector (device, window_len T) over NCCL. */
 COVE_API cove_status cove_dist_halo(cove_dist* d, void* x_window, void* stream);

@@ -244,10 +244,13 @@ def test_auto_route_choice_matches_reference_rule():
 
 
 def test_gate_failure_falls_back_to_lossless():
-    # values spanning many orders of magnitude inside each block: bfp8 fails the gate
-    rng = np.random.default_rng(3)
-    rows, cols, rp, ci, v = cb.synth_lapl2d(64, 64)
-    v = v * np.exp(rng.uniform(-20, 20, v.size))
+    # each row holds a cancelling pair 1000 + d, -1000 in two sparse blocks whose x
+    # entries are equal (columns 136 = 8 * 17 apart): bf16 cannot hold d, so the
+    # joint output loses the whole row value and the gate must reject it
+    rows, cols = 256, 400
+    rp = np.arange(0, 2 * rows + 1, 2, dtype=np.int64)
+    ci = np.stack([np.arange(rows), np.arange(rows) + 136], 1).reshape(-1).astype(np.int32)
+    v = np.stack([1000.0 + 0.123 + 1e-3 * np.arange(rows), -1000.0 * np.ones(rows)], 1).reshape(-1)
     p = plan_for(rows, cols, rp, ci, v, value_codec="bfp8")
     assert p.info.gate_evaluated == 1 and p.info.joint_rel_err > 1e-2
     assert p.info.gate_pass == 0 and p.info.dispatched_route == cb.ROUTE_HYBRID
