@@ -32,6 +32,7 @@ struct KernelShape {
     int slots = 4;                        // lanes per block row = 8 * slots
     int heavy_limit = 0x7fffffff;         // blocks a block row handles in the main pass
     int long_tau = 0;                     // residual rows longer than this go to chunks
+    bool x_vec_ok = false;                // set per launch: x 16-byte aligned, cols % 4 == 0
     // overflow tasks (second launch)
     int64_t num_heavy = 0;
     const int32_t* heavy_br = nullptr;

@@ -31,28 +31,67 @@ namespace cove {
 namespace {
 
 constexpr int kThreads = 256;
+#ifndef COVE_MAIN_MIN_CTAS
+#define COVE_MAIN_MIN_CTAS 8  // resident CTAs per SM the main kernel is register-budgeted for
+#endif
 
 __device__ __forceinline__ float bf16_to_float(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }
 
+// The four x values of a block column, as the accumulator type.  With
+// `vec` (x 16-byte aligned, cols a multiple of 4) they come from 16-byte
+// read-only vector loads; otherwise only the cells present in `nib`.
+template <typename Acc, typename T>
+__device__ __forceinline__ void load_x4(const T* __restrict__ x, int64_t c4, bool vec,
+                                        uint32_t nib, Acc* out) {
+    if constexpr (sizeof(T) == 8) {
+        if (vec) {
+            const double2 a = __ldg(reinterpret_cast<const double2*>(x + c4));
+            const double2 b = __ldg(reinterpret_cast<const double2*>(x + c4 + 2));
+            out[0] = static_cast<Acc>(a.x);
+            out[1] = static_cast<Acc>(a.y);
+            out[2] = static_cast<Acc>(b.x);
+            out[3] = static_cast<Acc>(b.y);
+            return;
+        }
+    } else {
+        if (vec) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(x + c4));
+            out[0] = static_cast<Acc>(a.x);
+            out[1] = static_cast<Acc>(a.y);
+            out[2] = static_cast<Acc>(a.z);
+            out[3] = static_cast<Acc>(a.w);
+            return;
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) out[c] = (nib & (1u << c)) ? static_cast<Acc>(__ldg(x + c4 + c)) : Acc(0);
+}
+
 // ---- value decoders --------------------------------------------------------
 
+// Lossless routes accumulate in double (fp32 matrices too: a long fp32 row
+// summed in fp32 drifts by ~sqrt(len) ulps, above a 1e-6 normwise bound).
 template <typename T>
 struct RawDec {
-    using Acc = T;
+    using Acc = double;
     const T* __restrict__ kept;
     const T* __restrict__ res;
     __device__ __forceinline__ void prepare(void*) {}
     __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
-    __device__ __forceinline__ Acc kept_val(Acc, int64_t k) const { return kept[k]; }
-    __device__ __forceinline__ Acc res_val(int64_t p) const { return res[p]; }
-    __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return x[c]; }
+    __device__ __forceinline__ Acc kept_val(Acc, int64_t k) const { return static_cast<Acc>(kept[k]); }
+    __device__ __forceinline__ Acc res_val(int64_t p) const { return static_cast<Acc>(res[p]); }
+    __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return static_cast<Acc>(x[c]); }
+    __device__ __forceinline__ void x4(const T* __restrict__ x, int64_t c4, bool vec, uint32_t nib,
+                                       Acc* out) const {
+        load_x4<Acc, T>(x, c4, vec, nib, out);
+    }
 };
 
 template <typename T, typename IdxT, bool Smem>
 struct DictDec {
-    using Acc = T;
+    using Acc = double;
     const IdxT* __restrict__ kept;
     const IdxT* __restrict__ res;
     const T* __restrict__ codebook;
@@ -68,9 +107,13 @@ struct DictDec {
         }
     }
     __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
-    __device__ __forceinline__ Acc kept_val(Acc, int64_t k) const { return cb[kept[k]]; }
-    __device__ __forceinline__ Acc res_val(int64_t p) const { return cb[res[p]]; }
-    __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return x[c]; }
+    __device__ __forceinline__ Acc kept_val(Acc, int64_t k) const { return static_cast<Acc>(cb[kept[k]]); }
+    __device__ __forceinline__ Acc res_val(int64_t p) const { return static_cast<Acc>(cb[res[p]]); }
+    __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return static_cast<Acc>(x[c]); }
+    __device__ __forceinline__ void x4(const T* __restrict__ x, int64_t c4, bool vec, uint32_t nib,
+                                       Acc* out) const {
+        load_x4<Acc, T>(x, c4, vec, nib, out);
+    }
 };
 
 template <typename T>
@@ -88,12 +131,16 @@ struct Bfp8Dec {
     __device__ __forceinline__ float xv(const T* __restrict__ x, int64_t c) const {
         return static_cast<float>(x[c]);
     }
+    __device__ __forceinline__ void x4(const T* __restrict__ x, int64_t c4, bool vec, uint32_t nib,
+                                       float* out) const {
+        load_x4<float, T>(x, c4, vec, nib, out);
+    }
 };
 
 // ---- main pass -----------------------------------------------------------------
 
 template <typename T, typename Dec, int SLOTS>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, COVE_MAIN_MIN_CTAS)
 hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y) {
     extern __shared__ __align__(16) unsigned char smem[];
     dec.prepare(smem);
@@ -116,41 +163,48 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
     if (b1 - b0 > k.heavy_limit) b1 = b0 + k.heavy_limit;
     int vb = k.kept_brvp[br];
     const uint64_t* __restrict__ words = k.words;
+    const bool vec_x = k.x_vec_ok;
     Acc sum = Acc(0);
 
-#pragma unroll 2
-    for (int base = b0; base < b1; base += SLOTS) {
-        const int b = base + s;
-        const bool valid = b < b1;
-        const uint64_t w = valid ? __ldg(words + b) : 0ULL;
-        const uint32_t bm = static_cast<uint32_t>(w >> 32);
-        const int bc = static_cast<int>(w & 0x7fffffffULL);
-        const int pc = __popc(bm);
-        int incl = pc;
-        if constexpr (SLOTS > 1) {
-            const int t = __shfl_up_sync(gmask, incl, 8, G);
-            if (s >= 1) incl += t;
-        }
-        if constexpr (SLOTS > 2) {
-            const int t = __shfl_up_sync(gmask, incl, 16, G);
-            if (s >= 2) incl += t;
-        }
-        const int total = SLOTS > 1 ? __shfl_sync(gmask, incl, G - 1, G) : pc;
-        const int vblk = vb + incl - pc;
-        vb += total;
-        const uint32_t nib = (bm >> (4 * r)) & 0xFu;
-        if (nib) {
-            const Acc ctx = dec.block_ctx(b);
-            int v0 = vblk + __popc(bm & ((1u << (4 * r)) - 1u));
-            const int64_t c4 = static_cast<int64_t>(bc) * 4;
+    // One coalesced load brings G block words into the group; a group scan of
+    // their popcounts gives every block's value base; the blocks are then
+    // handed to the slots by shuffle, so consecutive steps are independent.
+    for (int batch = b0; batch < b1; batch += G) {
+        const int nblk = min(G, b1 - batch);
+        const uint64_t wl = gl < nblk ? __ldg(words + batch + gl) : 0ULL;
+        const int pcl = __popc(static_cast<uint32_t>(wl >> 32));
+        int incl = pcl;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                if (nib & (1u << c)) {
-                    sum += dec.kept_val(ctx, v0) * dec.xv(x, c4 + c);
-                    ++v0;
+        for (int o = 1; o < G; o <<= 1) {
+            const int t = __shfl_up_sync(gmask, incl, o, G);
+            if (gl >= o) incl += t;
+        }
+        const int exl = incl - pcl;
+        const int total = __shfl_sync(gmask, incl, G - 1, G);
+#pragma unroll 4
+        for (int j0 = 0; j0 < nblk; j0 += SLOTS) {
+            const int j = j0 + s;
+            const uint64_t w = __shfl_sync(gmask, wl, j & (G - 1), G);
+            const int vblk = vb + __shfl_sync(gmask, exl, j & (G - 1), G);
+            // lanes past the batch read a zero word: nib = 0, nothing loads
+            const uint32_t bm = static_cast<uint32_t>(w >> 32);
+            const uint32_t nib = (bm >> (4 * r)) & 0xFu;
+            if (nib) {
+                const int64_t c4 = static_cast<int64_t>(w & 0x7fffffffULL) * 4;
+                const Acc ctx = dec.block_ctx(batch + j);
+                int v0 = vblk + __popc(bm & ((1u << (4 * r)) - 1u));
+                Acc xs[4];
+                dec.x4(x, c4, vec_x, nib, xs);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if (nib & (1u << c)) {
+                        sum += dec.kept_val(ctx, v0) * xs[c];
+                        ++v0;
+                    }
                 }
             }
         }
+        vb += total;
     }
 
     const int64_t row = br * kBlockRows + r;
@@ -249,18 +303,20 @@ int launch_with(const KernelShape& k, Dec dec, size_t smem, const RouteValues& v
     const T* x = static_cast<const T*>(xv);
     T* y = static_cast<T*>(yv);
     int launches = 0;
+    KernelShape kk = k;
+    kk.x_vec_ok = (reinterpret_cast<uintptr_t>(xv) % 16 == 0) && (k.cols % 4 == 0);
     if (k.nbr > 0) {
         const int64_t groups_per_cta = kThreads / (8 * k.slots);
         const int grid = grid_for(k.nbr, static_cast<int>(groups_per_cta));
         switch (k.slots) {
             case 1:
-                hybrid_main_kernel<T, Dec, 1><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+                hybrid_main_kernel<T, Dec, 1><<<grid, kThreads, smem, s>>>(kk, dec, x, y);
                 break;
             case 2:
-                hybrid_main_kernel<T, Dec, 2><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+                hybrid_main_kernel<T, Dec, 2><<<grid, kThreads, smem, s>>>(kk, dec, x, y);
                 break;
             default:
-                hybrid_main_kernel<T, Dec, 4><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+                hybrid_main_kernel<T, Dec, 4><<<grid, kThreads, smem, s>>>(kk, dec, x, y);
                 break;
         }
         CUDA_LAUNCH_OK();

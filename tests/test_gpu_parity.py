@@ -58,6 +58,21 @@ def assert_streams_equal_split(p, s, dtype):
         s.kept_nnz, s.residual_nnz, s.cost_skipped_nnz)
 
 
+def assert_lossless(y, rows, rp, ci, v, x, y_ref=None):
+    """Lossless bound: normwise 1e-12 (fp64) / 1e-6 (fp32) against the exact
+    product of the stored values (evaluated in fp64).  For fp32 the
+    reference's own fp32-summed output is further off on long rows; it is
+    checked against its float summation bound instead."""
+    tol = LOSSLESS_TOL[v.dtype.type]
+    y_exact = O.spmv_csr(rows, rp, ci, v.astype(np.float64), np.asarray(x, np.float64))
+    rel = O.compare_vectors(y_exact, np.asarray(y, np.float64))[2]
+    assert rel <= tol, rel
+    if y_ref is not None:
+        lens = np.diff(np.asarray(rp))
+        bound = 1e-14 if v.dtype == np.float64 else 1e-7 * max(8.0, float(np.sqrt(lens.max())) * 4)
+        assert O.compare_vectors(np.asarray(y_ref, np.float64), np.asarray(y, np.float64))[2] <= max(tol, bound)
+
+
 def _kat_csr(k):
     return (k["rows"], k["cols"], np.array(k["row_ptr"], np.int64),
             np.array(k["col_idx"], np.int32), np.array(k["values"], np.float64))
@@ -156,8 +171,7 @@ def test_reference_cases_position_streams(ref_cases, split_key):
         # lossless SpMV on the canonical x vs the reference's spmv_csr output
         x = d[f"{name}/canonical_x"]
         y = gpu_spmv(p, x)
-        tol = LOSSLESS_TOL[v.dtype.type]
-        assert O.compare_vectors(d[f"{name}/y_canonical"], y)[2] <= tol, name
+        assert_lossless(y, rows, rp, ci, v, x, d[f"{name}/y_canonical"])
 
 
 def test_reference_cases_value_codecs(ref_cases):
@@ -213,7 +227,7 @@ def test_routes_spmv_and_gate(ref_cases, codec):
         y = gpu_spmv(p, x, route=jr)
         rel = O.compare_vectors(y0, y)[2]
         if jr in (cb.ROUTE_DICT_U8, cb.ROUTE_DICT_U16):
-            assert rel <= LOSSLESS_TOL[v.dtype.type], name
+            assert_lossless(y, rows, rp, ci, v, x, y0)
         else:
             frac = 0.005 if jr == cb.ROUTE_BFP8_OUTLIER else None
             ye = _joint_oracle(rows, cols, rp, ci, v, x, frac)
@@ -348,10 +362,10 @@ def test_full_size_configs(cfg):
     assert p.info.joint_route == want_route
     y0 = O.spmv_csr(rows, rp, ci, v, x)
     yl = gpu_spmv(p, x, route=cb.ROUTE_HYBRID)
-    assert O.compare_vectors(y0, yl)[2] <= LOSSLESS_TOL[v.dtype.type]
+    assert_lossless(yl, rows, rp, ci, v, x, y0)
     yj = gpu_spmv(p, x, route=want_route)
     if want_route == cb.ROUTE_DICT_U8:
-        assert O.compare_vectors(y0, yj)[2] <= LOSSLESS_TOL[v.dtype.type]
+        assert_lossless(yj, rows, rp, ci, v, x, y0)
     else:
         q, sc = O.bfp8_encode(s.kept)
         assert np.array_equal(p.stream("bfp8_int8"), q) and np.array_equal(p.stream("bfp8_scale"), sc)
