@@ -102,7 +102,8 @@ class ValuesDesc(C.Structure):
                 ("block_scale", C.c_void_p), ("codebook", C.c_void_p),
                 ("codebook_size", C.c_int64), ("num_outliers", C.c_int64),
                 ("outlier_rows", C.c_void_p), ("outlier_cols", C.c_void_p),
-                ("outlier_vals", C.c_void_p)]
+                ("outlier_vals", C.c_void_p), ("tile_code_words", C.c_void_p),
+                ("tile_bits", C.c_int32)]
 
 
 class CgResult(C.Structure):
@@ -115,7 +116,7 @@ EXPORTED = [
     "cove_last_error", "cove_status_string", "cove_version", "cove_plan_opts_default",
     "cove_plan_build", "cove_plan_destroy", "cove_plan_get_info", "cove_route_name",
     "cove_plan_stream", "cove_hybrid_spmv", "cove_spmv", "cove_spmv_route", "cove_spmv_host",
-    "cove_spmv_launches", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
+    "cove_spmv_launches", "cove_plan_device_error", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
     "cove_dist_halo_plan", "cove_dist_id_bytes", "cove_dist_make_id", "cove_dist_create", "cove_dist_destroy",
     "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv",
     "cove_rng_u64", "cove_rng_uniform01", "cove_synth_lapl2d", "cove_synth_lapl3d",
@@ -155,6 +156,8 @@ def _setup(L):
     L.cove_spmv.argtypes = [vp, vp, vp, vp]
     L.cove_spmv_route.argtypes = [vp, i32, vp, vp, vp]
     L.cove_spmv_host.argtypes = [vp, vp, vp, vp]
+    L.cove_plan_device_error.restype = C.c_int
+    L.cove_plan_device_error.argtypes = [vp, C.POINTER(C.c_int32), vp]
     L.cove_spmv_launches.restype = i32
     L.cove_spmv_launches.argtypes = [vp, i32]
     L.cove_compare_vectors.argtypes = [vp, vp, i64, i32, vp, vp]
@@ -348,6 +351,12 @@ class Plan:
         check(lib().cove_spmv_host(self._h, _np_ptr(x_host), _np_ptr(y_host),
                                    _stream_handle(stream)))
         return y_host
+
+    def device_error(self, stream=None) -> int:
+        """Raise if a bounded wait inside an SpMV kernel of this plan gave up."""
+        flag = C.c_int32(0)
+        check(lib().cove_plan_device_error(self._h, C.byref(flag), _stream_handle(stream)))
+        return flag.value
 
     def launches(self, route=None) -> int:
         return int(lib().cove_spmv_launches(self._h, self.info.dispatched_route if route is None

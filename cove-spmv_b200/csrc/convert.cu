@@ -373,7 +373,7 @@ __global__ void lb_count_kernel(int32_t nbr, const int32_t* __restrict__ kbrp, i
 }
 
 __global__ void lb_fill_kernel(int32_t nbr, const int32_t* __restrict__ kbrp,
-                               const int32_t* __restrict__ kbvp,
+                               const int32_t* __restrict__ kbrvp,
                                const uint32_t* __restrict__ kbitmap,
                                const int32_t* __restrict__ item_rp, int chunk, int split,
                                int style, uint64_t* __restrict__ words,
@@ -387,11 +387,11 @@ __global__ void lb_fill_kernel(int32_t nbr, const int32_t* __restrict__ kbrp,
     int out = item_rp[br];
     if (re == rs) {
         if (pieces == 1) items[out] = WorkItem{static_cast<uint32_t>(br), static_cast<uint32_t>(rs), 0u,
-                                               static_cast<uint32_t>(kbvp[rs])};
+                                               static_cast<uint32_t>(kbrvp[br])};
         return;
     }
     int blk = rs;
-    int vp = kbvp[rs];
+    int vp = kbrvp[br];
     while (blk < re) {
         const int c = min(eff, re - blk);
         items[out++] = WorkItem{static_cast<uint32_t>(br), static_cast<uint32_t>(blk),
@@ -429,14 +429,6 @@ __global__ void chunk_fill_kernel(int32_t rows, const int32_t* __restrict__ rp, 
         ccount[o] = min(chunk_nnz, len - off);
         ++o;
     }
-}
-
-__global__ void block_row_val_ptr_kernel(int32_t nbr, const int32_t* __restrict__ brp,
-                                         const int32_t* __restrict__ bvp,
-                                         int32_t* __restrict__ out) {
-    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (br > nbr) return;
-    out[br] = bvp[brp[br]];
 }
 
 int32_t checked_i32(int64_t v, const char* what) {
@@ -675,7 +667,7 @@ void build_layout(const SplitParts& sp, int32_t nbr, const cove_plan_opts& o, La
     alloc_n<WorkItem>(out.items, out.num_items);
     if (nbr > 0 && out.num_items > 0) {
         lb_fill_kernel<<<grid_for(nbr, kThreads), kThreads, 0, s>>>(
-            nbr, sp.kept_block_row_ptr.as<int32_t>(), sp.kept_block_val_ptr.as<int32_t>(),
+            nbr, sp.kept_block_row_ptr.as<int32_t>(), sp.kept_block_row_val_ptr.as<int32_t>(),
             sp.kept_bitmap.as<uint32_t>(), out.item_row_ptr.as<int32_t>(), chunk, split,
             o.lb_style, out.words.as<uint64_t>(), out.items.as<WorkItem>());
         CUDA_LAUNCH_OK();

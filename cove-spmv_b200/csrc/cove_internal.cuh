@@ -82,10 +82,12 @@ struct DevBuf {
         p = nullptr;
         bytes = 0;
     }
+    // Every buffer carries kTailSlack readable bytes past its logical end, so
+    // 16-byte-rounded bulk copies of a stream's last range stay in bounds.
+    static constexpr size_t kTailSlack = 64;
     void alloc(size_t n) {
         release();
-        if (n == 0) n = 16;  // keep a valid pointer for empty streams
-        CUDA_OK(cudaMalloc(&p, n));
+        CUDA_OK(cudaMalloc(&p, n + kTailSlack));
         bytes = n;
     }
     template <typename T>

@@ -46,6 +46,7 @@ struct cove_plan {
 
     // staging for cove_spmv_host
     cove::DevBuf x_stage, y_stage;
+    cove::DevBuf err;  // int, set by a kernel whose bounded wait gave up
 
     cove::KernelShape shape() const;
     cove::RouteValues route_values(int route) const;

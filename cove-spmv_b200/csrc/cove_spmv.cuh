@@ -17,6 +17,8 @@ struct RouteValues {
     const int32_t* out_rows = nullptr;
     const int32_t* out_cols = nullptr;
     const void* out_vals = nullptr;    // T
+    const void* tile_words = nullptr;  // family tile codes: Bits u32 words per block
+    int tile_bits = 0;
 };
 
 // Position streams and the kernel's own work split.
@@ -33,6 +35,8 @@ struct KernelShape {
     int heavy_limit = 0x7fffffff;         // blocks a block row handles in the main pass
     int long_tau = 0;                     // residual rows longer than this go to chunks
     bool x_vec_ok = false;                // set per launch: x 16-byte aligned, cols % 4 == 0
+    bool stage_ok = false;                // value streams carry tail slack: TMA staging allowed
+    int* err = nullptr;                   // device flag set when a bounded wait gives up
     // overflow tasks (second launch)
     int64_t num_heavy = 0;
     const int32_t* heavy_br = nullptr;

@@ -70,6 +70,8 @@ cove::KernelShape cove_plan::shape() const {
     k.res_rp = sp.res_row_ptr.as<int32_t>();
     k.res_col = sp.res_col.as<int32_t>();
     k.slots = slots;
+    k.stage_ok = true;  // every plan buffer carries DevBuf::kTailSlack
+    k.err = err.as<int>();
     k.heavy_limit = heavy_limit;
     k.long_tau = long_tau;
     k.num_heavy = num_heavy;
@@ -132,6 +134,8 @@ template <typename T>
 void build_plan_typed(cove_plan* P, const cove_csr_desc& d, cudaStream_t s) {
     const cove_plan_opts& o = P->opts;
     validate_csr<T>(d, s);
+    alloc_n<int>(P->err, 1);
+    CUDA_OK(cudaMemsetAsync(P->err.p, 0, sizeof(int), s));
     build_full_bitbsr<T>(d, P->full, s);
     P->nnz = P->full.nnz;
     P->nbr = P->full.nbr;
@@ -382,6 +386,18 @@ const char* cove_route_name(int32_t route) {
     return "unknown";
 }
 
+cove_status cove_plan_device_error(const cove_plan* P, int32_t* flag, void* stream) {
+    return guarded([&] {
+        if (!P || !flag) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        int h = 0;
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        CUDA_OK(cudaMemcpyAsync(&h, P->err.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+        CUDA_OK(cudaStreamSynchronize(s));
+        *flag = h;
+        if (h) COVE_THROW(COVE_ERR_TIMEOUT, "a bounded wait in an SpMV kernel gave up");
+    });
+}
+
 cove_status cove_plan_get_info(const cove_plan* P, cove_plan_info* info) {
     return guarded([&] {
         if (!P || !info) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
@@ -540,10 +556,10 @@ cove_status cove_hybrid_spmv(const cove_hybrid_desc* a, const cove_values_desc* 
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "fused CSR+BitBSR shape mismatch");
         }
         if (a->dtype != COVE_F64 && a->dtype != COVE_F32) COVE_THROW(COVE_ERR_UNSUPPORTED, "dtype");
-        if (v->route < COVE_ROUTE_HYBRID || v->route > COVE_ROUTE_BFP8_OUTLIER) {
+        if (v->route < COVE_ROUTE_HYBRID || v->route > COVE_ROUTE_BF16_NNZ) {
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "unknown route");
         }
-        if (a->rows > 0 && (!a->block_row_ptr || !a->block_row_val_ptr || !a->res_row_ptr || !y)) {
+        if (a->rows > 0 && (!a->block_row_ptr || !a->block_row_val_ptr || !y)) {
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null stream");
         }
         if (a->num_chunks > 0 && (!a->chunk_row || !a->chunk_pbegin || !a->chunk_pcount)) {
@@ -577,6 +593,11 @@ cove_status cove_hybrid_spmv(const cove_hybrid_desc* a, const cove_values_desc* 
             rv.out_rows = v->outlier_rows;
             rv.out_cols = v->outlier_cols;
             rv.out_vals = v->outlier_vals;
+        }
+        rv.tile_words = v->tile_code_words;
+        rv.tile_bits = v->tile_bits;
+        if (v->route == COVE_ROUTE_TILE_CODE && !v->tile_code_words) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "tile-code route needs tile_code_words");
         }
         if (v->route == COVE_ROUTE_DICT_U8 && v->codebook_size > 256) {
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "u8 dictionary holds at most 256 values");

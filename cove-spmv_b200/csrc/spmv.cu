@@ -5,35 +5,79 @@
 // (structural/src/main_gpu_csr_bitbsr_spmv.cu:517-634 lossless,
 // :755-860 joint/quantized) and the outlier correction (:967-979).
 //
-// Work split: one group of 8*SLOTS lanes owns one block row.  Lane (s, r)
-// of a group handles local row r of every SLOTS-th kept block, starting at
-// block s, so each lane covers one 4-cell row segment of a block per step:
-// the segment's values are contiguous (bit order is row-major), the four x
-// values are contiguous, and the value base of each block comes from a
-// two-step shuffle scan of the blocks' popcounts over the slots.  The same
-// lanes then stride the eight residual rows (SLOTS lanes per row), reduce
-// over the slots with two xor-shuffles, and store y once per row: no
-// atomics, no zero-fill, deterministic.
+// Work split: one group of 8*SLOTS lanes owns one block row.  At the top of
+// the block row the group leader starts a 1-D TMA bulk copy
+// (cp.async.bulk, completion on an mbarrier) of the block row's whole packed
+// value range into a shared-memory stage; while it is in flight the group
+// loads the block words (one coalesced load per G blocks), scans their
+// popcounts for the value bases and runs the residual rows.  Then lane
+// (s, r) handles local row r of every SLOTS-th block: the four cells of a
+// row segment are contiguous in the value stream (bit order is row-major)
+// and the four x values are contiguous (two 16-byte loads).  The slots are
+// reduced with xor-shuffles and each row is stored once: no atomics, no
+// zero-fill, deterministic.  Block rows whose values do not fit the stage,
+// and streams without tail slack (the caller-stream entry point), read the
+// values straight from global memory.
 //
 // Block rows with more than `heavy_limit` kept blocks and residual rows
 // longer than `long_tau` are finished by a second launch (one warp per
 // piece / 1024-nnz chunk, atomicAdd into y), which also applies the exact
 // BFP8 outlier side list.  Matrices without such rows need one launch.
 //
-// Accumulation: raw and dict routes accumulate in T (exact decode); the
-// BFP8 route accumulates in fp32 with x cast to float, as the reference's
-// joint kernel does (:795, :811).
+// Accumulation: lossless routes accumulate in double; the BFP8 and bf16
+// routes accumulate in fp32 with x cast to float, as the reference's joint
+// kernel does (:795, :811).
 #include "cove_spmv.cuh"
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 namespace cove {
 namespace {
 
 constexpr int kThreads = 256;
-#ifndef COVE_MAIN_MIN_CTAS
-#define COVE_MAIN_MIN_CTAS 8  // resident CTAs per SM the main kernel is register-budgeted for
-#endif
+constexpr uint32_t kWaitLimit = 1u << 24;  // bounded mbarrier polls before giving up
+
+// ---- PTX helpers: mbarrier + 1-D bulk copy (no multicast) --------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 
 __device__ __forceinline__ float bf16_to_float(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
@@ -69,29 +113,31 @@ __device__ __forceinline__ void load_x4(const T* __restrict__ x, int64_t c4, boo
     for (int c = 0; c < 4; ++c) out[c] = (nib & (1u << c)) ? static_cast<Acc>(__ldg(x + c4 + c)) : Acc(0);
 }
 
-// ---- value decoders --------------------------------------------------------
+// ---- value decoders ------------------------------------------------------------
+// V: element type of the kept value stream; decode(raw, ctx, bit) turns a
+// stored element into the accumulator type (ctx is per block, bit the cell).
 
 // Lossless routes accumulate in double (fp32 matrices too: a long fp32 row
 // summed in fp32 drifts by ~sqrt(len) ulps, above a 1e-6 normwise bound).
 template <typename T>
 struct RawDec {
     using Acc = double;
+    using V = T;
+    static constexpr bool kStage = true;
     const T* __restrict__ kept;
     const T* __restrict__ res;
     __device__ __forceinline__ void prepare(void*) {}
     __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
-    __device__ __forceinline__ Acc kept_val(Acc, int64_t k) const { return static_cast<Acc>(kept[k]); }
+    __device__ __forceinline__ Acc decode(V raw, Acc, int) const { return static_cast<Acc>(raw); }
     __device__ __forceinline__ Acc res_val(int64_t p) const { return static_cast<Acc>(res[p]); }
     __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return static_cast<Acc>(x[c]); }
-    __device__ __forceinline__ void x4(const T* __restrict__ x, int64_t c4, bool vec, uint32_t nib,
-                                       Acc* out) const {
-        load_x4<Acc, T>(x, c4, vec, nib, out);
-    }
 };
 
 template <typename T, typename IdxT, bool Smem>
 struct DictDec {
     using Acc = double;
+    using V = IdxT;
+    static constexpr bool kStage = true;
     const IdxT* __restrict__ kept;
     const IdxT* __restrict__ res;
     const T* __restrict__ codebook;
@@ -107,65 +153,167 @@ struct DictDec {
         }
     }
     __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
-    __device__ __forceinline__ Acc kept_val(Acc, int64_t k) const { return static_cast<Acc>(cb[kept[k]]); }
+    __device__ __forceinline__ Acc decode(V raw, Acc, int) const { return static_cast<Acc>(cb[raw]); }
     __device__ __forceinline__ Acc res_val(int64_t p) const { return static_cast<Acc>(cb[res[p]]); }
     __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return static_cast<Acc>(x[c]); }
-    __device__ __forceinline__ void x4(const T* __restrict__ x, int64_t c4, bool vec, uint32_t nib,
-                                       Acc* out) const {
-        load_x4<Acc, T>(x, c4, vec, nib, out);
-    }
 };
 
 template <typename T>
 struct Bfp8Dec {
     using Acc = float;
+    using V = int8_t;
+    static constexpr bool kStage = true;
     const int8_t* __restrict__ kept;
     const uint16_t* __restrict__ res;
     const uint16_t* __restrict__ scale;
     __device__ __forceinline__ void prepare(void*) {}
     __device__ __forceinline__ float block_ctx(int64_t b) const { return bf16_to_float(scale[b]); }
-    __device__ __forceinline__ float kept_val(float sc, int64_t k) const {
-        return static_cast<float>(kept[k]) * sc;
+    __device__ __forceinline__ float decode(V raw, float sc, int) const {
+        return static_cast<float>(raw) * sc;
     }
     __device__ __forceinline__ float res_val(int64_t p) const { return bf16_to_float(res[p]); }
     __device__ __forceinline__ float xv(const T* __restrict__ x, int64_t c) const {
         return static_cast<float>(x[c]);
     }
-    __device__ __forceinline__ void x4(const T* __restrict__ x, int64_t c4, bool vec, uint32_t nib,
-                                       float* out) const {
-        load_x4<float, T>(x, c4, vec, nib, out);
+};
+
+// Family-runner exact dictionary with per-cell tile codes: Bits-bit code of
+// cell `bit` in the block's tile words (common.cuh:62-93, 147-160), value =
+// codebook[code], accumulated in double.  The block context is the block.
+template <typename T, int Bits>
+struct TileDec {
+    using Acc = double;
+    using V = uint8_t;  // no per-nnz kept stream
+    static constexpr bool kStage = false;
+    static constexpr int kWords = Bits;  // words_per_tile = Bits for 8x4 cells
+    static constexpr int kPerWord = 32 / Bits;
+    static constexpr uint32_t kMask = (1u << Bits) - 1u;
+    const uint32_t* __restrict__ words;
+    const T* __restrict__ codebook;
+    const T* __restrict__ res;
+    const uint8_t* kept = nullptr;
+    __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ Acc block_ctx(int64_t b) const { return static_cast<Acc>(b); }
+    __device__ __forceinline__ Acc decode(V, Acc blk, int bit) const {
+        const int64_t b = static_cast<int64_t>(blk);
+        const uint32_t w = __ldg(words + b * kWords + bit / kPerWord);
+        return static_cast<Acc>(codebook[(w >> ((bit % kPerWord) * Bits)) & kMask]);
     }
+    __device__ __forceinline__ Acc res_val(int64_t p) const { return static_cast<Acc>(res[p]); }
+    __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return static_cast<Acc>(x[c]); }
+};
+
+// Per-nnz bf16 values (round16_nnz, common.cuh:632-687), fp32 accumulate.
+template <typename T>
+struct Bf16NnzDec {
+    using Acc = float;
+    using V = uint16_t;
+    static constexpr bool kStage = true;
+    const uint16_t* __restrict__ kept;
+    const uint16_t* __restrict__ res;
+    __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ float block_ctx(int64_t) const { return 1.0f; }
+    __device__ __forceinline__ float decode(V raw, float, int) const { return bf16_to_float(raw); }
+    __device__ __forceinline__ float res_val(int64_t p) const { return bf16_to_float(res[p]); }
+    __device__ __forceinline__ float xv(const T* __restrict__ x, int64_t c) const {
+        return static_cast<float>(x[c]);
+    }
+};
+
+// Shared-memory layout of the main kernel: [codebook][barriers][stages].
+struct SmemLayout {
+    int codebook_bytes = 0;  // rounded to 16
+    int stage_bytes = 0;     // per group, 0 = no staging
+    int groups = 0;          // per CTA
+    __host__ __device__ int barrier_off() const { return codebook_bytes; }
+    __host__ __device__ int stage_off() const { return codebook_bytes + 16 * groups; }
+    __host__ __device__ int total() const { return stage_off() + stage_bytes * groups; }
 };
 
 // ---- main pass -----------------------------------------------------------------
 
 template <typename T, typename Dec, int SLOTS>
-__global__ void __launch_bounds__(kThreads, COVE_MAIN_MIN_CTAS)
-hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    dec.prepare(smem);
-    if constexpr (sizeof(Dec) > 0) {
-        // the shared codebook is complete before any lane reads it
-        __syncthreads();
-    }
+__global__ void __launch_bounds__(kThreads)
+hybrid_main_kernel(const KernelShape k, Dec dec, const SmemLayout L, const T* __restrict__ x,
+                   T* __restrict__ y) {
+    extern __shared__ __align__(128) unsigned char smem[];
     using Acc = typename Dec::Acc;
+    using V = typename Dec::V;
     constexpr int G = 8 * SLOTS;
     const int lane = threadIdx.x & 31;
     const int gl = lane & (G - 1);
+    const int grp = threadIdx.x / G;
     const int s = gl >> 3;
     const int r = gl & 7;
     const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
-    const int64_t br = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.barrier_off()) + 2 * grp;
+    unsigned char* stage = smem + L.stage_off() + L.stage_bytes * grp;
+
+    dec.prepare(smem);
+    if (L.stage_bytes > 0 && gl == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();  // codebook copy and barrier init are visible to all lanes
+
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * (kThreads / G) + grp;
     if (br >= k.nbr) return;  // the whole group leaves together
 
     const int b0 = k.kept_brp[br];
     int b1 = k.kept_brp[br + 1];
-    if (b1 - b0 > k.heavy_limit) b1 = b0 + k.heavy_limit;
-    int vb = k.kept_brvp[br];
+    const bool heavy = b1 - b0 > k.heavy_limit;
+    if (heavy) b1 = b0 + k.heavy_limit;
+    const int vb0 = k.kept_brvp[br];
+    const int ve0 = k.kept_brvp[br + 1];
+
+    // start the bulk copy of this block row's value range
+    const V* __restrict__ kept = dec.kept;
+    bool staged = false;
+    int stage_shift = 0;  // bytes between the stage start and value vb0
+    if constexpr (Dec::kStage) {
+        if (L.stage_bytes > 0 && !heavy && ve0 > vb0) {
+            const uintptr_t a0 = reinterpret_cast<uintptr_t>(kept + vb0);
+            const uintptr_t a1 = reinterpret_cast<uintptr_t>(kept + ve0);
+            const uintptr_t s0 = a0 & ~uintptr_t{15};
+            const uint32_t bytes = static_cast<uint32_t>(((a1 + 15) & ~uintptr_t{15}) - s0);
+            if (bytes <= static_cast<uint32_t>(L.stage_bytes)) {
+                staged = true;
+                stage_shift = static_cast<int>(a0 - s0);
+                if (gl == 0) {
+                    mbar_expect_tx(bar, bytes);
+                    bulk_copy_g2s(stage, reinterpret_cast<const void*>(s0), bytes, bar);
+                }
+            }
+        }
+    }
+
+    Acc sum = Acc(0);
+    // residual rows while the copy is in flight
+    const int64_t row = br * kBlockRows + r;
+    if (row < k.rows && k.res_rp != nullptr) {
+        const int rs = k.res_rp[row];
+        const int re = k.res_rp[row + 1];
+        if (!(k.long_tau > 0 && re - rs > k.long_tau)) {
+            const int32_t* __restrict__ rc = k.res_col;
+#pragma unroll 2
+            for (int q = rs + s; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
+        }
+    }
+
+    if (staged) {
+        bool ok = false;
+        for (uint32_t it = 0; it < kWaitLimit && !ok; ++it) ok = mbar_try_wait(bar, 0);
+        if (!__all_sync(gmask, ok)) {
+            if (gl == 0 && k.err) atomicExch(k.err, 1);
+            return;
+        }
+    }
+    const V* __restrict__ vsrc =
+        staged ? reinterpret_cast<const V*>(stage + stage_shift) - vb0 : kept;
+
     const uint64_t* __restrict__ words = k.words;
     const bool vec_x = k.x_vec_ok;
-    Acc sum = Acc(0);
-
+    int vb = vb0;
     // One coalesced load brings G block words into the group; a group scan of
     // their popcounts gives every block's value base; the blocks are then
     // handed to the slots by shuffle, so consecutive steps are independent.
@@ -184,8 +332,8 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
 #pragma unroll 4
         for (int j0 = 0; j0 < nblk; j0 += SLOTS) {
             const int j = j0 + s;
-            const uint64_t w = __shfl_sync(gmask, wl, j & (G - 1), G);
-            const int vblk = vb + __shfl_sync(gmask, exl, j & (G - 1), G);
+            const uint64_t w = __shfl_sync(gmask, wl, j, G);
+            const int vblk = vb + __shfl_sync(gmask, exl, j, G);
             // lanes past the batch read a zero word: nib = 0, nothing loads
             const uint32_t bm = static_cast<uint32_t>(w >> 32);
             const uint32_t nib = (bm >> (4 * r)) & 0xFu;
@@ -194,11 +342,13 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
                 const Acc ctx = dec.block_ctx(batch + j);
                 int v0 = vblk + __popc(bm & ((1u << (4 * r)) - 1u));
                 Acc xs[4];
-                dec.x4(x, c4, vec_x, nib, xs);
+                load_x4<Acc, T>(x, c4, vec_x, nib, xs);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if (nib & (1u << c)) {
-                        sum += dec.kept_val(ctx, v0) * xs[c];
+                        V raw{};
+                        if constexpr (Dec::kStage) raw = vsrc[v0];
+                        sum += dec.decode(raw, ctx, 4 * r + c) * xs[c];
                         ++v0;
                     }
                 }
@@ -207,15 +357,6 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
         vb += total;
     }
 
-    const int64_t row = br * kBlockRows + r;
-    if (row < k.rows) {
-        const int rs = k.res_rp[row];
-        const int re = k.res_rp[row + 1];
-        if (!(k.long_tau > 0 && re - rs > k.long_tau)) {
-            const int32_t* __restrict__ rc = k.res_col;
-            for (int q = rs + s; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
-        }
-    }
     if constexpr (SLOTS > 1) sum += __shfl_xor_sync(gmask, sum, 8, G);
     if constexpr (SLOTS > 2) sum += __shfl_xor_sync(gmask, sum, 16, G);
     if (s == 0 && row < k.rows) y[row] = static_cast<T>(sum);
@@ -229,10 +370,11 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
                        int heavy_ctas, int chunk_ctas, int64_t num_out,
                        const int32_t* __restrict__ orow, const int32_t* __restrict__ ocol,
                        const T* __restrict__ oval) {
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     dec.prepare(smem);
     __syncthreads();
     using Acc = typename Dec::Acc;
+    using V = typename Dec::V;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int cta = static_cast<int>(blockIdx.x);
@@ -267,7 +409,9 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if (nib & (1u << c)) {
-                        sum += dec.kept_val(ctx, v0) * dec.xv(x, c4 + c);
+                        V raw{};
+                        if constexpr (Dec::kStage) raw = dec.kept[v0];
+                        sum += dec.decode(raw, ctx, 4 * r + c) * dec.xv(x, c4 + c);
                         ++v0;
                     }
                 }
@@ -297,6 +441,38 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
     if (i < num_out) atomicAdd(&y[orow[i]], oval[i] * x[ocol[i]]);
 }
 
+// Opt a kernel into more than 48 KB of dynamic shared memory (once per size).
+void allow_smem(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::map<const void*, int> done;
+    if (bytes <= 48 * 1024) return;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = done.find(fn);
+    if (it != done.end() && it->second >= bytes) return;
+    CUDA_OK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[fn] = bytes;
+}
+
+template <typename T, typename Dec, int SLOTS>
+void launch_main(const KernelShape& k, const Dec& dec, int codebook_bytes, const T* x, T* y,
+                 cudaStream_t s) {
+    constexpr int G = 8 * SLOTS;
+    SmemLayout L;
+    L.groups = kThreads / G;
+    L.codebook_bytes = (codebook_bytes + 15) & ~15;
+    // a stage holds one block row of up to 32 fully dense blocks per 8 lanes
+    // of the group (plus 16-byte rounding), in the value stream's type
+    L.stage_bytes = (Dec::kStage && k.stage_ok)
+                        ? static_cast<int>(32 * 32 * (G / 8) * sizeof(typename Dec::V) / 4 + 32)
+                        : 0;
+    L.stage_bytes = (L.stage_bytes + 15) & ~15;
+    const int grid = grid_for(k.nbr, L.groups);
+    auto fn = hybrid_main_kernel<T, Dec, SLOTS>;
+    allow_smem(reinterpret_cast<const void*>(fn), L.total());
+    fn<<<grid, kThreads, L.total(), s>>>(k, dec, L, x, y);
+    CUDA_LAUNCH_OK();
+}
+
 template <typename T, typename Dec>
 int launch_with(const KernelShape& k, Dec dec, size_t smem, const RouteValues& v, const void* xv,
                 void* yv, cudaStream_t s) {
@@ -306,20 +482,11 @@ int launch_with(const KernelShape& k, Dec dec, size_t smem, const RouteValues& v
     KernelShape kk = k;
     kk.x_vec_ok = (reinterpret_cast<uintptr_t>(xv) % 16 == 0) && (k.cols % 4 == 0);
     if (k.nbr > 0) {
-        const int64_t groups_per_cta = kThreads / (8 * k.slots);
-        const int grid = grid_for(k.nbr, static_cast<int>(groups_per_cta));
         switch (k.slots) {
-            case 1:
-                hybrid_main_kernel<T, Dec, 1><<<grid, kThreads, smem, s>>>(kk, dec, x, y);
-                break;
-            case 2:
-                hybrid_main_kernel<T, Dec, 2><<<grid, kThreads, smem, s>>>(kk, dec, x, y);
-                break;
-            default:
-                hybrid_main_kernel<T, Dec, 4><<<grid, kThreads, smem, s>>>(kk, dec, x, y);
-                break;
+            case 1: launch_main<T, Dec, 1>(kk, dec, static_cast<int>(smem), x, y, s); break;
+            case 2: launch_main<T, Dec, 2>(kk, dec, static_cast<int>(smem), x, y, s); break;
+            default: launch_main<T, Dec, 4>(kk, dec, static_cast<int>(smem), x, y, s); break;
         }
-        CUDA_LAUNCH_OK();
         ++launches;
     }
     const int heavy_ctas = grid_for(k.num_heavy, kThreads / 32);
@@ -327,7 +494,7 @@ int launch_with(const KernelShape& k, Dec dec, size_t smem, const RouteValues& v
     const int out_ctas = grid_for(v.num_outliers, kThreads);
     if (heavy_ctas + chunk_ctas + out_ctas > 0) {
         hybrid_overflow_kernel<T, Dec><<<heavy_ctas + chunk_ctas + out_ctas, kThreads, smem, s>>>(
-            k, dec, x, y, heavy_ctas, chunk_ctas, v.num_outliers, v.out_rows, v.out_cols,
+            kk, dec, x, y, heavy_ctas, chunk_ctas, v.num_outliers, v.out_rows, v.out_cols,
             static_cast<const T*>(v.out_vals));
         CUDA_LAUNCH_OK();
         ++launches;
@@ -359,6 +526,23 @@ int launch_typed(const KernelShape& k, const RouteValues& v, const void* x, void
         case COVE_ROUTE_BFP8_OUTLIER: {
             Bfp8Dec<T> d{static_cast<const int8_t*>(v.kept), static_cast<const uint16_t*>(v.res),
                          v.scale};
+            return launch_with<T>(k, d, 0, v, x, y, s);
+        }
+        case COVE_ROUTE_TILE_CODE: {
+            const auto* w = static_cast<const uint32_t*>(v.tile_words);
+            const auto* cbk = static_cast<const T*>(v.codebook);
+            const auto* res = static_cast<const T*>(v.res);
+            switch (v.tile_bits) {
+                case 1: return launch_with<T>(k, TileDec<T, 1>{w, cbk, res}, 0, v, x, y, s);
+                case 2: return launch_with<T>(k, TileDec<T, 2>{w, cbk, res}, 0, v, x, y, s);
+                case 4: return launch_with<T>(k, TileDec<T, 4>{w, cbk, res}, 0, v, x, y, s);
+                case 8: return launch_with<T>(k, TileDec<T, 8>{w, cbk, res}, 0, v, x, y, s);
+                case 16: return launch_with<T>(k, TileDec<T, 16>{w, cbk, res}, 0, v, x, y, s);
+                default: COVE_THROW(COVE_ERR_UNSUPPORTED, "tile codes must have 1, 2, 4, 8 or 16 bits");
+            }
+        }
+        case COVE_ROUTE_BF16_NNZ: {
+            Bf16NnzDec<T> d{static_cast<const uint16_t*>(v.kept), static_cast<const uint16_t*>(v.res)};
             return launch_with<T>(k, d, 0, v, x, y, s);
         }
         default:

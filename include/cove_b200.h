@@ -58,7 +58,10 @@ typedef enum {
     COVE_ROUTE_DICT_U8 = 1,       /* "dict_u8_lossless" */
     COVE_ROUTE_DICT_U16 = 2,      /* "dict_u16_lossless" */
     COVE_ROUTE_BFP8 = 3,          /* "bfp8_blocks+bf16_residual" */
-    COVE_ROUTE_BFP8_OUTLIER = 4   /* "bfp8_outlier_blocks+bf16_residual" */
+    COVE_ROUTE_BFP8_OUTLIER = 4,  /* "bfp8_outlier_blocks+bf16_residual" */
+    /* BitBSR-only value codecs of the family runner, cove_hybrid_spmv only: */
+    COVE_ROUTE_TILE_CODE = 5,     /* exact dict, per-cell tile codes (common.cuh:270-319) */
+    COVE_ROUTE_BF16_NNZ = 6       /* per-nnz bf16 values (common.cuh:632-687) */
 } cove_route;
 
 /* Split policy (main_gpu_csr_bitbsr_spmv.cu:35, :1087-1093). */
@@ -254,6 +257,8 @@ typedef struct {
     const int32_t* outlier_rows;
     const int32_t* outlier_cols;
     const void* outlier_vals;
+    const uint32_t* tile_code_words;  /* tile-code route: tile_bits words per kept block */
+    int32_t tile_bits;                /* 1, 2, 4, 8 or 16 */
 } cove_values_desc;
 
 /*
@@ -274,6 +279,14 @@ COVE_API cove_status cove_spmv_route(const cove_plan* plan, int32_t route, const
  * device staging buffers belong to the plan.
  */
 COVE_API cove_status cove_spmv_host(cove_plan* plan, const void* x_host, void* y_host, void* stream);
+
+/*
+ * Device error flag of a plan's kernels (synchronizes `stream`): *flag is
+ * non-zero, and the status COVE_ERR_TIMEOUT, when a bounded wait inside an
+ * SpMV kernel (the shared-memory staging barrier) gave up; the affected
+ * rows of that call's y were not written.
+ */
+COVE_API cove_status cove_plan_device_error(const cove_plan* plan, int32_t* flag, void* stream);
 
 /* Number of kernel launches one cove_spmv / cove_spmv_route call makes. */
 COVE_API int32_t cove_spmv_launches(const cove_plan* plan, int32_t route);

@@ -372,7 +372,11 @@ def test_full_size_configs(cfg):
         ye = O.joint_bfp8_spmv(s.kept, q, sc, s.res_row_ptr, s.res_col_idx,
                                O.bf16_half_up(s.res_values), np.zeros(0, np.int32),
                                np.zeros(0, np.int32), np.zeros(0, v.dtype), x)
-        assert np.abs(ye - yj).max() / np.abs(ye).max() <= 1e-5
+        # fp32 sums in two different orders: bounded by the longest row's
+        # float summation error (R-MAT rows reach ~10^5 entries)
+        lens = np.diff(rp)
+        bound = 1e-7 * max(16.0, 4.0 * float(np.sqrt(lens.max())))
+        assert np.abs(ye - yj).max() / np.abs(ye).max() <= bound
         # gate decision = the oracle's on the canonical x
         xc = O.canonical_x(cols, v.dtype)
         yc0 = O.spmv_csr(rows, rp, ci, v, xc)
