@@ -498,16 +498,12 @@ void validate_csr(const cove_csr_desc& d, cudaStream_t s) {
 }
 
 template <typename T>
-void build_full_bitbsr(const cove_csr_desc& d, FullBitBsr& out, cudaStream_t s) {
-    out.rows = d.rows;
-    out.cols = d.cols;
-    out.nbr = (d.rows + kBlockRows - 1) / kBlockRows;
-    const int32_t nbr = out.nbr;
+void bitbsr_count(const cove_csr_desc& d, int32_t* brp, int32_t* brvp, int64_t* num_blocks,
+                  int64_t* nnz, cudaStream_t s) {
+    const int32_t nbr = (d.rows + kBlockRows - 1) / kBlockRows;
     DevBuf counts, nnzc;
     alloc_n<int32_t>(counts, nbr);
     alloc_n<int32_t>(nnzc, nbr);
-    alloc_n<int32_t>(out.block_row_ptr, nbr + 1);
-    alloc_n<int32_t>(out.block_row_val_ptr, nbr + 1);
     const T* v = static_cast<const T*>(d.values);
     const int grid = grid_for(static_cast<int64_t>(nbr) * 8, kThreads);
     if (nbr > 0) {
@@ -522,30 +518,78 @@ void build_full_bitbsr(const cove_csr_desc& d, FullBitBsr& out, cudaStream_t s) 
         }
         CUDA_LAUNCH_OK();
     }
-    // scans into int64 first so an overflow is detected, then narrowed
-    out.num_blocks = checked_i32(
-        exclusive_scan_total<int32_t, int32_t>(counts.as<int32_t>(), out.block_row_ptr.as<int32_t>(), nbr, s),
-        "BitBSR block count");
-    out.nnz = checked_i32(
-        exclusive_scan_total<int32_t, int32_t>(nnzc.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(), nbr, s),
-        "BitBSR nnz");
+    // the scans carry int64 totals, so an int32 overflow is detected
+    *num_blocks = checked_i32(exclusive_scan_total<int32_t, int32_t>(counts.as<int32_t>(), brp, nbr, s),
+                              "BitBSR block count");
+    *nnz = checked_i32(exclusive_scan_total<int32_t, int32_t>(nnzc.as<int32_t>(), brvp, nbr, s),
+                       "BitBSR nnz");
+}
+
+template <typename T>
+void bitbsr_fill(const cove_csr_desc& d, const int32_t* brp, const int32_t* brvp, int32_t* col,
+                 uint32_t* bitmap, T* values, cudaStream_t s) {
+    const int32_t nbr = (d.rows + kBlockRows - 1) / kBlockRows;
+    if (nbr == 0 || d.nnz == 0) return;
+    const T* v = static_cast<const T*>(d.values);
+    const int grid = grid_for(static_cast<int64_t>(nbr) * 8, kThreads);
+    if (d.row_ptr_i32) {
+        full_fill_kernel<T, int32_t><<<grid, kThreads, 0, s>>>(
+            d.rows, nbr, static_cast<const int32_t*>(d.row_ptr), d.col_idx, v, brp, brvp, col,
+            bitmap, values);
+    } else {
+        full_fill_kernel<T, int64_t><<<grid, kThreads, 0, s>>>(
+            d.rows, nbr, static_cast<const int64_t*>(d.row_ptr), d.col_idx, v, brp, brvp, col,
+            bitmap, values);
+    }
+    CUDA_LAUNCH_OK();
+}
+
+template <typename T>
+void build_full_bitbsr(const cove_csr_desc& d, FullBitBsr& out, cudaStream_t s) {
+    out.rows = d.rows;
+    out.cols = d.cols;
+    out.nbr = (d.rows + kBlockRows - 1) / kBlockRows;
+    alloc_n<int32_t>(out.block_row_ptr, out.nbr + 1);
+    alloc_n<int32_t>(out.block_row_val_ptr, out.nbr + 1);
+    bitbsr_count<T>(d, out.block_row_ptr.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(),
+                    &out.num_blocks, &out.nnz, s);
     alloc_n<int32_t>(out.block_col_idx, out.num_blocks);
     alloc_n<uint32_t>(out.bitmap, out.num_blocks);
     alloc_n<T>(out.values, out.nnz);
-    if (nbr > 0 && out.num_blocks > 0) {
-        if (d.row_ptr_i32) {
-            full_fill_kernel<T, int32_t><<<grid, kThreads, 0, s>>>(
-                d.rows, nbr, static_cast<const int32_t*>(d.row_ptr), d.col_idx, v,
-                out.block_row_ptr.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(),
-                out.block_col_idx.as<int32_t>(), out.bitmap.as<uint32_t>(), out.values.as<T>());
-        } else {
-            full_fill_kernel<T, int64_t><<<grid, kThreads, 0, s>>>(
-                d.rows, nbr, static_cast<const int64_t*>(d.row_ptr), d.col_idx, v,
-                out.block_row_ptr.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(),
-                out.block_col_idx.as<int32_t>(), out.bitmap.as<uint32_t>(), out.values.as<T>());
-        }
+    if (out.num_blocks > 0) {
+        bitbsr_fill<T>(d, out.block_row_ptr.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(),
+                       out.block_col_idx.as<int32_t>(), out.bitmap.as<uint32_t>(),
+                       out.values.as<T>(), s);
+    }
+}
+
+void pack_words(int64_t nb, const int32_t* col, const uint32_t* bitmap, uint64_t* words,
+                cudaStream_t s) {
+    if (nb <= 0) return;
+    pack_words_kernel<<<grid_for(nb, kThreads), kThreads, 0, s>>>(nb, col, bitmap, words);
+    CUDA_LAUNCH_OK();
+}
+
+int64_t lb_count(int32_t nbr, const int32_t* brp, int chunk, int split, int style,
+                 int32_t* item_rp, cudaStream_t s) {
+    DevBuf cnt;
+    alloc_n<int32_t>(cnt, nbr);
+    if (nbr > 0) {
+        lb_count_kernel<<<grid_for(nbr, kThreads), kThreads, 0, s>>>(nbr, brp, chunk, split, style,
+                                                                     cnt.as<int32_t>());
         CUDA_LAUNCH_OK();
     }
+    return checked_i32(exclusive_scan_total<int32_t, int32_t>(cnt.as<int32_t>(), item_rp, nbr, s),
+                       "work items");
+}
+
+void lb_fill(int32_t nbr, const int32_t* brp, const int32_t* brvp, const uint32_t* bitmap,
+             const int32_t* item_rp, int chunk, int split, int style, uint64_t* words,
+             WorkItem* items, cudaStream_t s) {
+    if (nbr <= 0) return;
+    lb_fill_kernel<<<grid_for(nbr, kThreads), kThreads, 0, s>>>(nbr, brp, brvp, bitmap, item_rp,
+                                                                chunk, split, style, words, items);
+    CUDA_LAUNCH_OK();
 }
 
 // CsrBitBsrSplitCostModel::should_move_to_residual (csr_bitbsr_split.hpp:66-73)

@@ -54,6 +54,10 @@ __device__ __forceinline__ void mbar_fence_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                  "r"(bytes)
@@ -221,14 +225,23 @@ struct Bf16NnzDec {
 };
 
 // Shared-memory layout of the main kernel: [codebook][barriers][stages].
+// Each group owns two barriers and two stage buffers of `stage_bytes`.
 struct SmemLayout {
     int codebook_bytes = 0;  // rounded to 16
-    int stage_bytes = 0;     // per group, 0 = no staging
+    int stage_bytes = 0;     // per buffer, 0 = no staging
+    int chunk_blocks = 0;    // blocks staged per chunk (multiple of SLOTS)
     int groups = 0;          // per CTA
     __host__ __device__ int barrier_off() const { return codebook_bytes; }
     __host__ __device__ int stage_off() const { return codebook_bytes + 16 * groups; }
-    __host__ __device__ int total() const { return stage_off() + stage_bytes * groups; }
+    __host__ __device__ int total() const { return stage_off() + 2 * stage_bytes * groups; }
 };
+
+// Bounded wait on a stage barrier; false when the copy did not land in time.
+__device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity, unsigned gmask) {
+    bool ok = false;
+    for (uint32_t it = 0; it < kWaitLimit && !ok; ++it) ok = mbar_try_wait(bar, parity);
+    return __all_sync(gmask, ok);
+}
 
 // ---- main pass -----------------------------------------------------------------
 
@@ -246,12 +259,14 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const SmemLayout L, const T* __
     const int s = gl >> 3;
     const int r = gl & 7;
     const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.barrier_off()) + 2 * grp;
-    unsigned char* stage = smem + L.stage_off() + L.stage_bytes * grp;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.barrier_off()) + 2 * grp;
+    unsigned char* stages = smem + L.stage_off() + 2 * L.stage_bytes * grp;
+    const bool staging = Dec::kStage && L.stage_bytes > 0;
 
     dec.prepare(smem);
-    if (L.stage_bytes > 0 && gl == 0) {
-        mbar_init(bar, 1);
+    if (staging && gl == 0) {
+        mbar_init(bars, 1);
+        mbar_init(bars + 1, 1);
         mbar_fence_init();
     }
     __syncthreads();  // codebook copy and barrier init are visible to all lanes
@@ -261,76 +276,32 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const SmemLayout L, const T* __
 
     const int b0 = k.kept_brp[br];
     int b1 = k.kept_brp[br + 1];
-    const bool heavy = b1 - b0 > k.heavy_limit;
-    if (heavy) b1 = b0 + k.heavy_limit;
-    const int vb0 = k.kept_brvp[br];
-    const int ve0 = k.kept_brvp[br + 1];
-
-    // start the bulk copy of this block row's value range
+    if (b1 - b0 > k.heavy_limit) b1 = b0 + k.heavy_limit;
     const V* __restrict__ kept = dec.kept;
-    bool staged = false;
-    int stage_shift = 0;  // bytes between the stage start and value vb0
-    if constexpr (Dec::kStage) {
-        if (L.stage_bytes > 0 && !heavy && ve0 > vb0) {
-            const uintptr_t a0 = reinterpret_cast<uintptr_t>(kept + vb0);
-            const uintptr_t a1 = reinterpret_cast<uintptr_t>(kept + ve0);
-            const uintptr_t s0 = a0 & ~uintptr_t{15};
-            const uint32_t bytes = static_cast<uint32_t>(((a1 + 15) & ~uintptr_t{15}) - s0);
-            if (bytes <= static_cast<uint32_t>(L.stage_bytes)) {
-                staged = true;
-                stage_shift = static_cast<int>(a0 - s0);
-                if (gl == 0) {
-                    mbar_expect_tx(bar, bytes);
-                    bulk_copy_g2s(stage, reinterpret_cast<const void*>(s0), bytes, bar);
-                }
-            }
-        }
-    }
-
-    Acc sum = Acc(0);
-    // residual rows while the copy is in flight
-    const int64_t row = br * kBlockRows + r;
-    if (row < k.rows && k.res_rp != nullptr) {
-        const int rs = k.res_rp[row];
-        const int re = k.res_rp[row + 1];
-        if (!(k.long_tau > 0 && re - rs > k.long_tau)) {
-            const int32_t* __restrict__ rc = k.res_col;
-#pragma unroll 2
-            for (int q = rs + s; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
-        }
-    }
-
-    if (staged) {
-        bool ok = false;
-        for (uint32_t it = 0; it < kWaitLimit && !ok; ++it) ok = mbar_try_wait(bar, 0);
-        if (!__all_sync(gmask, ok)) {
-            if (gl == 0 && k.err) atomicExch(k.err, 1);
-            return;
-        }
-    }
-    const V* __restrict__ vsrc =
-        staged ? reinterpret_cast<const V*>(stage + stage_shift) - vb0 : kept;
-
     const uint64_t* __restrict__ words = k.words;
     const bool vec_x = k.x_vec_ok;
-    int vb = vb0;
-    // One coalesced load brings G block words into the group; a group scan of
-    // their popcounts gives every block's value base; the blocks are then
-    // handed to the slots by shuffle, so consecutive steps are independent.
-    for (int batch = b0; batch < b1; batch += G) {
-        const int nblk = min(G, b1 - batch);
-        const uint64_t wl = gl < nblk ? __ldg(words + batch + gl) : 0ULL;
-        const int pcl = __popc(static_cast<uint32_t>(wl >> 32));
-        int incl = pcl;
-#pragma unroll
-        for (int o = 1; o < G; o <<= 1) {
-            const int t = __shfl_up_sync(gmask, incl, o, G);
-            if (gl >= o) incl += t;
+    const int64_t row = br * kBlockRows + r;
+    const uint32_t lowmask = (1u << (4 * r)) - 1u;
+
+    Acc sum = Acc(0);
+    bool res_done = false;
+    auto residual = [&]() {
+        if (row < k.rows && k.res_rp != nullptr) {
+            const int rs = k.res_rp[row];
+            const int re = k.res_rp[row + 1];
+            if (!(k.long_tau > 0 && re - rs > k.long_tau)) {
+                const int32_t* __restrict__ rc = k.res_col;
+#pragma unroll 2
+                for (int q = rs + s; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
+            }
         }
-        const int exl = incl - pcl;
-        const int total = __shfl_sync(gmask, incl, G - 1, G);
-#pragma unroll 4
-        for (int j0 = 0; j0 < nblk; j0 += SLOTS) {
+        res_done = true;
+    };
+
+    // blocks [jb, je) of the current batch, values read through vsrc
+    auto compute = [&](int batch, int jb, int je, uint64_t wl, int exl, int vb, const V* vsrc) {
+#pragma unroll 2
+        for (int j0 = jb; j0 < je; j0 += SLOTS) {
             const int j = j0 + s;
             const uint64_t w = __shfl_sync(gmask, wl, j, G);
             const int vblk = vb + __shfl_sync(gmask, exl, j, G);
@@ -340,7 +311,7 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const SmemLayout L, const T* __
             if (nib) {
                 const int64_t c4 = static_cast<int64_t>(w & 0x7fffffffULL) * 4;
                 const Acc ctx = dec.block_ctx(batch + j);
-                int v0 = vblk + __popc(bm & ((1u << (4 * r)) - 1u));
+                int v0 = vblk + __popc(bm & lowmask);
                 Acc xs[4];
                 load_x4<Acc, T>(x, c4, vec_x, nib, xs);
 #pragma unroll
@@ -354,8 +325,83 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const SmemLayout L, const T* __
                 }
             }
         }
+    };
+
+    int vb = k.kept_brvp[br];
+    uint32_t cc = 0;  // chunks staged so far in this block row (uniform in the group)
+    // One coalesced load brings G block words into the group; a group scan of
+    // their popcounts gives every block's value base.
+    for (int batch = b0; batch < b1; batch += G) {
+        const int nblk = min(G, b1 - batch);
+        const uint64_t wl = gl < nblk ? __ldg(words + batch + gl) : 0ULL;
+        const int pcl = __popc(static_cast<uint32_t>(wl >> 32));
+        int incl = pcl;
+#pragma unroll
+        for (int o = 1; o < G; o <<= 1) {
+            const int t = __shfl_up_sync(gmask, incl, o, G);
+            if (gl >= o) incl += t;
+        }
+        const int exl = incl - pcl;
+        const int total = __shfl_sync(gmask, incl, G - 1, G);
+        if (!staging) {
+            if (!res_done) residual();
+            compute(batch, 0, nblk, wl, exl, vb, kept);
+        } else {
+            // chunks of CB blocks, double-buffered: the copy of chunk i+1 is in
+            // flight while chunk i is computed from shared memory
+            const int CB = L.chunk_blocks;
+            const int nch = (nblk + CB - 1) / CB;
+            // per buffer: byte shift of the first value and its value index
+            int shift0 = 0, shift1 = 0, vstart0 = 0, vstart1 = 0;
+            auto issue = [&](int ci) {
+                const int jb = ci * CB;
+                const int je = min(jb + CB, nblk);
+                const int vs = vb + __shfl_sync(gmask, exl, jb, G);
+                const int ve = je < nblk ? vb + __shfl_sync(gmask, exl, je, G) : vb + total;
+                const uintptr_t a0 = reinterpret_cast<uintptr_t>(kept + vs);
+                const uintptr_t a1 = reinterpret_cast<uintptr_t>(kept + ve);
+                const uintptr_t s0 = a0 & ~uintptr_t{15};
+                const uint32_t bytes = ve > vs ? static_cast<uint32_t>(((a1 + 15) & ~uintptr_t{15}) - s0) : 0u;
+                const int buf = static_cast<int>((cc + ci) & 1u);
+                if (buf) {
+                    shift1 = static_cast<int>(a0 - s0);
+                    vstart1 = vs;
+                } else {
+                    shift0 = static_cast<int>(a0 - s0);
+                    vstart0 = vs;
+                }
+                if (gl == 0) {
+                    // the lanes' earlier shared-memory reads of this buffer are
+                    // ordered before the bulk copy that overwrites it
+                    fence_proxy_async();
+                    mbar_expect_tx(bars + buf, bytes);
+                    if (bytes) {
+                        bulk_copy_g2s(stages + buf * L.stage_bytes, reinterpret_cast<const void*>(s0),
+                                      bytes, bars + buf);
+                    }
+                }
+            };
+            issue(0);
+            if (!res_done) residual();  // overlaps the first copy
+            for (int ci = 0; ci < nch; ++ci) {
+                if (ci + 1 < nch) issue(ci + 1);
+                const uint32_t c = cc + ci;
+                const int buf = static_cast<int>(c & 1u);
+                if (!stage_wait(bars + buf, (c >> 1) & 1u, gmask)) {
+                    if (gl == 0 && k.err) atomicExch(k.err, 1);
+                    return;
+                }
+                const V* vsrc = reinterpret_cast<const V*>(stages + buf * L.stage_bytes +
+                                                           (buf ? shift1 : shift0)) -
+                                (buf ? vstart1 : vstart0);
+                compute(batch, ci * CB, min((ci + 1) * CB, nblk), wl, exl, vb, vsrc);
+                __syncwarp(gmask);  // every lane is done with this buffer before it is refilled
+            }
+            cc += static_cast<uint32_t>(nch);
+        }
         vb += total;
     }
+    if (!res_done) residual();
 
     if constexpr (SLOTS > 1) sum += __shfl_xor_sync(gmask, sum, 8, G);
     if constexpr (SLOTS > 2) sum += __shfl_xor_sync(gmask, sum, 16, G);
@@ -457,15 +503,19 @@ template <typename T, typename Dec, int SLOTS>
 void launch_main(const KernelShape& k, const Dec& dec, int codebook_bytes, const T* x, T* y,
                  cudaStream_t s) {
     constexpr int G = 8 * SLOTS;
+    using V = typename Dec::V;
     SmemLayout L;
     L.groups = kThreads / G;
     L.codebook_bytes = (codebook_bytes + 15) & ~15;
-    // a stage holds one block row of up to 32 fully dense blocks per 8 lanes
-    // of the group (plus 16-byte rounding), in the value stream's type
-    L.stage_bytes = (Dec::kStage && k.stage_ok)
-                        ? static_cast<int>(32 * 32 * (G / 8) * sizeof(typename Dec::V) / 4 + 32)
-                        : 0;
-    L.stage_bytes = (L.stage_bytes + 15) & ~15;
+    if (Dec::kStage && k.stage_ok) {
+        // about 512 * SLOTS bytes of values per chunk (32 cells per block),
+        // at least one step of the slots and at most one word batch
+        int cb = (512 * SLOTS) / static_cast<int>(32 * sizeof(V));
+        cb = std::max(SLOTS, std::min(G, cb));
+        cb -= cb % SLOTS;
+        L.chunk_blocks = cb;
+        L.stage_bytes = (cb * 32 * static_cast<int>(sizeof(V)) + 32 + 15) & ~15;
+    }
     const int grid = grid_for(k.nbr, L.groups);
     auto fn = hybrid_main_kernel<T, Dec, SLOTS>;
     allow_smem(reinterpret_cast<const void*>(fn), L.total());
