@@ -115,7 +115,9 @@ class CgResult(C.Structure):
 EXPORTED = [
     "cove_last_error", "cove_status_string", "cove_version", "cove_plan_opts_default",
     "cove_plan_build", "cove_plan_destroy", "cove_plan_get_info", "cove_route_name",
-    "cove_plan_stream", "cove_hybrid_spmv", "cove_spmv", "cove_spmv_route", "cove_spmv_host",
+    "cove_plan_stream", "cove_bitbsr8x4_count", "cove_bitbsr8x4_fill", "cove_pack_words",
+    "cove_lb_layout_count", "cove_lb_layout_fill",
+    "cove_hybrid_spmv", "cove_spmv", "cove_spmv_route", "cove_spmv_host",
     "cove_spmv_launches", "cove_plan_device_error", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
     "cove_dist_halo_plan", "cove_dist_id_bytes", "cove_dist_make_id", "cove_dist_create", "cove_dist_destroy",
     "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv",
@@ -153,6 +155,12 @@ def _setup(L):
     L.cove_route_name.argtypes = [i32]
     L.cove_plan_stream.argtypes = [vp, i32, vp, C.c_size_t, C.POINTER(C.c_size_t), vp]
     L.cove_hybrid_spmv.argtypes = [C.POINTER(HybridDesc), C.POINTER(ValuesDesc), vp, vp, vp]
+    L.cove_bitbsr8x4_count.argtypes = [C.POINTER(CsrDesc), vp, vp, C.POINTER(C.c_int64),
+                                       C.POINTER(C.c_int64), vp]
+    L.cove_bitbsr8x4_fill.argtypes = [C.POINTER(CsrDesc), vp, vp, vp, vp, vp, vp]
+    L.cove_pack_words.argtypes = [i64, vp, vp, vp, vp]
+    L.cove_lb_layout_count.argtypes = [i32, vp, i32, i32, i32, vp, C.POINTER(C.c_int64), vp]
+    L.cove_lb_layout_fill.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp]
     L.cove_spmv.argtypes = [vp, vp, vp, vp]
     L.cove_spmv_route.argtypes = [vp, i32, vp, vp, vp]
     L.cove_spmv_host.argtypes = [vp, vp, vp, vp]
@@ -196,7 +204,8 @@ def _setup(L):
     L.cove_synth_vector_device.restype = C.c_int
     L.cove_synth_vector_device.argtypes = [i32, u64, u64, i64, i64, vp, vp]
     for fn in ("cove_plan_build", "cove_plan_destroy", "cove_plan_get_info", "cove_plan_stream",
-               "cove_hybrid_spmv",
+               "cove_hybrid_spmv", "cove_bitbsr8x4_count", "cove_bitbsr8x4_fill", "cove_pack_words",
+               "cove_lb_layout_count", "cove_lb_layout_fill",
                "cove_spmv", "cove_spmv_route", "cove_spmv_host", "cove_compare_vectors",
                "cove_canonical_x", "cove_cg_solve", "cove_dist_make_id", "cove_dist_create",
                "cove_dist_destroy", "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv"):

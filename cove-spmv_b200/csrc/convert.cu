@@ -753,6 +753,12 @@ template void validate_csr<double>(const cove_csr_desc&, cudaStream_t);
 template void validate_csr<float>(const cove_csr_desc&, cudaStream_t);
 template void build_full_bitbsr<double>(const cove_csr_desc&, FullBitBsr&, cudaStream_t);
 template void build_full_bitbsr<float>(const cove_csr_desc&, FullBitBsr&, cudaStream_t);
+template void bitbsr_count<double>(const cove_csr_desc&, int32_t*, int32_t*, int64_t*, int64_t*, cudaStream_t);
+template void bitbsr_count<float>(const cove_csr_desc&, int32_t*, int32_t*, int64_t*, int64_t*, cudaStream_t);
+template void bitbsr_fill<double>(const cove_csr_desc&, const int32_t*, const int32_t*, int32_t*, uint32_t*,
+                                  double*, cudaStream_t);
+template void bitbsr_fill<float>(const cove_csr_desc&, const int32_t*, const int32_t*, int32_t*, uint32_t*,
+                                 float*, cudaStream_t);
 template void build_split<double>(const FullBitBsr&, const cove_plan_opts&, SplitParts&, cudaStream_t);
 template void build_split<float>(const FullBitBsr&, const cove_plan_opts&, SplitParts&, cudaStream_t);
 

@@ -548,6 +548,68 @@ cove_status cove_spmv_route(const cove_plan* P, int32_t route, const void* x, vo
     });
 }
 
+cove_status cove_bitbsr8x4_count(const cove_csr_desc* csr, int32_t* brp, int32_t* brvp,
+                                 int64_t* num_blocks, int64_t* nnz, void* stream) {
+    return guarded([&] {
+        if (!csr || !brp || !brvp || !num_blocks || !nnz) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (csr->dtype == COVE_F64) {
+            validate_csr<double>(*csr, s);
+            bitbsr_count<double>(*csr, brp, brvp, num_blocks, nnz, s);
+        } else if (csr->dtype == COVE_F32) {
+            validate_csr<float>(*csr, s);
+            bitbsr_count<float>(*csr, brp, brvp, num_blocks, nnz, s);
+        } else {
+            COVE_THROW(COVE_ERR_UNSUPPORTED, "dtype must be float64 or float32");
+        }
+    });
+}
+
+cove_status cove_bitbsr8x4_fill(const cove_csr_desc* csr, const int32_t* brp, const int32_t* brvp,
+                                int32_t* col, uint32_t* bitmap, void* values, void* stream) {
+    return guarded([&] {
+        if (!csr || !brp || !brvp) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        if (csr->nnz > 0 && (!col || !bitmap || !values)) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null output");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (csr->dtype == COVE_F64) bitbsr_fill<double>(*csr, brp, brvp, col, bitmap, static_cast<double*>(values), s);
+        else bitbsr_fill<float>(*csr, brp, brvp, col, bitmap, static_cast<float*>(values), s);
+    });
+}
+
+cove_status cove_pack_words(int64_t nb, const int32_t* col, const uint32_t* bitmap, uint64_t* words,
+                            void* stream) {
+    return guarded([&] {
+        if (nb < 0 || (nb > 0 && (!col || !bitmap || !words))) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "bad argument");
+        pack_words(nb, col, bitmap, words, static_cast<cudaStream_t>(stream));
+    });
+}
+
+cove_status cove_lb_layout_count(int32_t nbr, const int32_t* brp, int32_t chunk, int32_t split,
+                                 int32_t style, int32_t* item_rp, int64_t* num_items, void* stream) {
+    return guarded([&] {
+        if (chunk <= 0) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "GPU BitBSR load-balance chunk_blocks must be positive");
+        if (split < 0) split = chunk;
+        if (split == 0) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "GPU BitBSR load-balance split_threshold_blocks must be positive");
+        if (style != COVE_LB_HYBRID && style != COVE_LB_DEVICE) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "unknown layout style");
+        if (nbr < 0 || !brp || !item_rp || !num_items) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "bad argument");
+        *num_items = lb_count(nbr, brp, chunk, split, style, item_rp, static_cast<cudaStream_t>(stream));
+    });
+}
+
+cove_status cove_lb_layout_fill(int32_t nbr, const int32_t* brp, const int32_t* brvp,
+                                const uint32_t* bitmap, const int32_t* item_rp, int32_t chunk,
+                                int32_t split, int32_t style, uint64_t* words, void* items,
+                                void* stream) {
+    return guarded([&] {
+        if (chunk <= 0) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "GPU BitBSR load-balance chunk_blocks must be positive");
+        if (split < 0) split = chunk;
+        if (split == 0) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "GPU BitBSR load-balance split_threshold_blocks must be positive");
+        if (nbr < 0 || !brp || !brvp || !item_rp) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "bad argument");
+        lb_fill(nbr, brp, brvp, bitmap, item_rp, chunk, split, style, words,
+                static_cast<WorkItem*>(items), static_cast<cudaStream_t>(stream));
+    });
+}
+
 cove_status cove_hybrid_spmv(const cove_hybrid_desc* a, const cove_values_desc* v, const void* x,
                              void* y, void* stream) {
     return guarded([&] {

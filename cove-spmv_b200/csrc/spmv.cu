@@ -5,19 +5,15 @@
 // (structural/src/main_gpu_csr_bitbsr_spmv.cu:517-634 lossless,
 // :755-860 joint/quantized) and the outlier correction (:967-979).
 //
-// Work split: one group of 8*SLOTS lanes owns one block row.  At the top of
-// the block row the group leader starts a 1-D TMA bulk copy
-// (cp.async.bulk, completion on an mbarrier) of the block row's whole packed
-// value range into a shared-memory stage; while it is in flight the group
-// loads the block words (one coalesced load per G blocks), scans their
-// popcounts for the value bases and runs the residual rows.  Then lane
-// (s, r) handles local row r of every SLOTS-th block: the four cells of a
-// row segment are contiguous in the value stream (bit order is row-major)
-// and the four x values are contiguous (two 16-byte loads).  The slots are
-// reduced with xor-shuffles and each row is stored once: no atomics, no
-// zero-fill, deterministic.  Block rows whose values do not fit the stage,
-// and streams without tail slack (the caller-stream entry point), read the
-// values straight from global memory.
+// Work split: one group of 8*SLOTS lanes owns one block row.  The group
+// loads G block words with one coalesced load, scans their popcounts for the
+// value bases and hands the blocks to the slots by shuffle; lane (s, r)
+// handles local row r of every SLOTS-th block: the four cells of a row
+// segment are contiguous in the value stream (bit order is row-major) and
+// the four x values are contiguous (two 16-byte loads).  The SLOTS lanes of
+// a row then stride its residual entries, the slots are reduced with
+// xor-shuffles and each row is stored once: no atomics, no zero-fill,
+// deterministic.
 //
 // Block rows with more than `heavy_limit` kept blocks and residual rows
 // longer than `long_tau` are finished by a second launch (one warp per
@@ -30,58 +26,11 @@
 #include "cove_spmv.cuh"
 
 #include <algorithm>
-#include <map>
-#include <mutex>
 
 namespace cove {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr uint32_t kWaitLimit = 1u << 24;  // bounded mbarrier polls before giving up
-
-// ---- PTX helpers: mbarrier + 1-D bulk copy (no multicast) --------------------
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_fence_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
-                                              uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
 
 __device__ __forceinline__ float bf16_to_float(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
@@ -127,7 +76,7 @@ template <typename T>
 struct RawDec {
     using Acc = double;
     using V = T;
-    static constexpr bool kStage = true;
+    static constexpr bool kHasKept = true;
     const T* __restrict__ kept;
     const T* __restrict__ res;
     __device__ __forceinline__ void prepare(void*) {}
@@ -141,7 +90,7 @@ template <typename T, typename IdxT, bool Smem>
 struct DictDec {
     using Acc = double;
     using V = IdxT;
-    static constexpr bool kStage = true;
+    static constexpr bool kHasKept = true;
     const IdxT* __restrict__ kept;
     const IdxT* __restrict__ res;
     const T* __restrict__ codebook;
@@ -166,7 +115,7 @@ template <typename T>
 struct Bfp8Dec {
     using Acc = float;
     using V = int8_t;
-    static constexpr bool kStage = true;
+    static constexpr bool kHasKept = true;
     const int8_t* __restrict__ kept;
     const uint16_t* __restrict__ res;
     const uint16_t* __restrict__ scale;
@@ -188,7 +137,7 @@ template <typename T, int Bits>
 struct TileDec {
     using Acc = double;
     using V = uint8_t;  // no per-nnz kept stream
-    static constexpr bool kStage = false;
+    static constexpr bool kHasKept = false;
     static constexpr int kWords = Bits;  // words_per_tile = Bits for 8x4 cells
     static constexpr int kPerWord = 32 / Bits;
     static constexpr uint32_t kMask = (1u << Bits) - 1u;
@@ -212,7 +161,7 @@ template <typename T>
 struct Bf16NnzDec {
     using Acc = float;
     using V = uint16_t;
-    static constexpr bool kStage = true;
+    static constexpr bool kHasKept = true;
     const uint16_t* __restrict__ kept;
     const uint16_t* __restrict__ res;
     __device__ __forceinline__ void prepare(void*) {}
@@ -224,84 +173,52 @@ struct Bf16NnzDec {
     }
 };
 
-// Shared-memory layout of the main kernel: [codebook][barriers][stages].
-// Each group owns two barriers and two stage buffers of `stage_bytes`.
-struct SmemLayout {
-    int codebook_bytes = 0;  // rounded to 16
-    int stage_bytes = 0;     // per buffer, 0 = no staging
-    int chunk_blocks = 0;    // blocks staged per chunk (multiple of SLOTS)
-    int groups = 0;          // per CTA
-    __host__ __device__ int barrier_off() const { return codebook_bytes; }
-    __host__ __device__ int stage_off() const { return codebook_bytes + 16 * groups; }
-    __host__ __device__ int total() const { return stage_off() + 2 * stage_bytes * groups; }
-};
-
-// Bounded wait on a stage barrier; false when the copy did not land in time.
-__device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity, unsigned gmask) {
-    bool ok = false;
-    for (uint32_t it = 0; it < kWaitLimit && !ok; ++it) ok = mbar_try_wait(bar, parity);
-    return __all_sync(gmask, ok);
-}
-
 // ---- main pass -----------------------------------------------------------------
 
 template <typename T, typename Dec, int SLOTS>
 __global__ void __launch_bounds__(kThreads)
-hybrid_main_kernel(const KernelShape k, Dec dec, const SmemLayout L, const T* __restrict__ x,
-                   T* __restrict__ y) {
-    extern __shared__ __align__(128) unsigned char smem[];
+hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    dec.prepare(smem);
+    __syncthreads();  // a shared codebook is complete before any lane reads it
     using Acc = typename Dec::Acc;
     using V = typename Dec::V;
     constexpr int G = 8 * SLOTS;
     const int lane = threadIdx.x & 31;
     const int gl = lane & (G - 1);
-    const int grp = threadIdx.x / G;
     const int s = gl >> 3;
     const int r = gl & 7;
     const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.barrier_off()) + 2 * grp;
-    unsigned char* stages = smem + L.stage_off() + 2 * L.stage_bytes * grp;
-    const bool staging = Dec::kStage && L.stage_bytes > 0;
-
-    dec.prepare(smem);
-    if (staging && gl == 0) {
-        mbar_init(bars, 1);
-        mbar_init(bars + 1, 1);
-        mbar_fence_init();
-    }
-    __syncthreads();  // codebook copy and barrier init are visible to all lanes
-
-    const int64_t br = static_cast<int64_t>(blockIdx.x) * (kThreads / G) + grp;
+    const int64_t br = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
     if (br >= k.nbr) return;  // the whole group leaves together
 
     const int b0 = k.kept_brp[br];
     int b1 = k.kept_brp[br + 1];
     if (b1 - b0 > k.heavy_limit) b1 = b0 + k.heavy_limit;
-    const V* __restrict__ kept = dec.kept;
+    int vb = k.kept_brvp[br];
     const uint64_t* __restrict__ words = k.words;
+    const V* __restrict__ kept = dec.kept;
     const bool vec_x = k.x_vec_ok;
-    const int64_t row = br * kBlockRows + r;
     const uint32_t lowmask = (1u << (4 * r)) - 1u;
-
     Acc sum = Acc(0);
-    bool res_done = false;
-    auto residual = [&]() {
-        if (row < k.rows && k.res_rp != nullptr) {
-            const int rs = k.res_rp[row];
-            const int re = k.res_rp[row + 1];
-            if (!(k.long_tau > 0 && re - rs > k.long_tau)) {
-                const int32_t* __restrict__ rc = k.res_col;
-#pragma unroll 2
-                for (int q = rs + s; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
-            }
-        }
-        res_done = true;
-    };
 
-    // blocks [jb, je) of the current batch, values read through vsrc
-    auto compute = [&](int batch, int jb, int je, uint64_t wl, int exl, int vb, const V* vsrc) {
-#pragma unroll 2
-        for (int j0 = jb; j0 < je; j0 += SLOTS) {
+    // One coalesced load brings G block words into the group; a group scan of
+    // their popcounts gives every block's value base; the blocks are then
+    // handed to the slots by shuffle, so consecutive steps are independent.
+    for (int batch = b0; batch < b1; batch += G) {
+        const int nblk = min(G, b1 - batch);
+        const uint64_t wl = gl < nblk ? __ldg(words + batch + gl) : 0ULL;
+        const int pcl = __popc(static_cast<uint32_t>(wl >> 32));
+        int incl = pcl;
+#pragma unroll
+        for (int o = 1; o < G; o <<= 1) {
+            const int t = __shfl_up_sync(gmask, incl, o, G);
+            if (gl >= o) incl += t;
+        }
+        const int exl = incl - pcl;
+        const int total = __shfl_sync(gmask, incl, G - 1, G);
+#pragma unroll 4
+        for (int j0 = 0; j0 < nblk; j0 += SLOTS) {
             const int j = j0 + s;
             const uint64_t w = __shfl_sync(gmask, wl, j, G);
             const int vblk = vb + __shfl_sync(gmask, exl, j, G);
@@ -318,91 +235,26 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const SmemLayout L, const T* __
                 for (int c = 0; c < 4; ++c) {
                     if (nib & (1u << c)) {
                         V raw{};
-                        if constexpr (Dec::kStage) raw = vsrc[v0];
+                        if constexpr (Dec::kHasKept) raw = kept[v0];
                         sum += dec.decode(raw, ctx, 4 * r + c) * xs[c];
                         ++v0;
                     }
                 }
             }
         }
-    };
-
-    int vb = k.kept_brvp[br];
-    uint32_t cc = 0;  // chunks staged so far in this block row (uniform in the group)
-    // One coalesced load brings G block words into the group; a group scan of
-    // their popcounts gives every block's value base.
-    for (int batch = b0; batch < b1; batch += G) {
-        const int nblk = min(G, b1 - batch);
-        const uint64_t wl = gl < nblk ? __ldg(words + batch + gl) : 0ULL;
-        const int pcl = __popc(static_cast<uint32_t>(wl >> 32));
-        int incl = pcl;
-#pragma unroll
-        for (int o = 1; o < G; o <<= 1) {
-            const int t = __shfl_up_sync(gmask, incl, o, G);
-            if (gl >= o) incl += t;
-        }
-        const int exl = incl - pcl;
-        const int total = __shfl_sync(gmask, incl, G - 1, G);
-        if (!staging) {
-            if (!res_done) residual();
-            compute(batch, 0, nblk, wl, exl, vb, kept);
-        } else {
-            // chunks of CB blocks, double-buffered: the copy of chunk i+1 is in
-            // flight while chunk i is computed from shared memory
-            const int CB = L.chunk_blocks;
-            const int nch = (nblk + CB - 1) / CB;
-            // per buffer: byte shift of the first value and its value index
-            int shift0 = 0, shift1 = 0, vstart0 = 0, vstart1 = 0;
-            auto issue = [&](int ci) {
-                const int jb = ci * CB;
-                const int je = min(jb + CB, nblk);
-                const int vs = vb + __shfl_sync(gmask, exl, jb, G);
-                const int ve = je < nblk ? vb + __shfl_sync(gmask, exl, je, G) : vb + total;
-                const uintptr_t a0 = reinterpret_cast<uintptr_t>(kept + vs);
-                const uintptr_t a1 = reinterpret_cast<uintptr_t>(kept + ve);
-                const uintptr_t s0 = a0 & ~uintptr_t{15};
-                const uint32_t bytes = ve > vs ? static_cast<uint32_t>(((a1 + 15) & ~uintptr_t{15}) - s0) : 0u;
-                const int buf = static_cast<int>((cc + ci) & 1u);
-                if (buf) {
-                    shift1 = static_cast<int>(a0 - s0);
-                    vstart1 = vs;
-                } else {
-                    shift0 = static_cast<int>(a0 - s0);
-                    vstart0 = vs;
-                }
-                if (gl == 0) {
-                    // the lanes' earlier shared-memory reads of this buffer are
-                    // ordered before the bulk copy that overwrites it
-                    fence_proxy_async();
-                    mbar_expect_tx(bars + buf, bytes);
-                    if (bytes) {
-                        bulk_copy_g2s(stages + buf * L.stage_bytes, reinterpret_cast<const void*>(s0),
-                                      bytes, bars + buf);
-                    }
-                }
-            };
-            issue(0);
-            if (!res_done) residual();  // overlaps the first copy
-            for (int ci = 0; ci < nch; ++ci) {
-                if (ci + 1 < nch) issue(ci + 1);
-                const uint32_t c = cc + ci;
-                const int buf = static_cast<int>(c & 1u);
-                if (!stage_wait(bars + buf, (c >> 1) & 1u, gmask)) {
-                    if (gl == 0 && k.err) atomicExch(k.err, 1);
-                    return;
-                }
-                const V* vsrc = reinterpret_cast<const V*>(stages + buf * L.stage_bytes +
-                                                           (buf ? shift1 : shift0)) -
-                                (buf ? vstart1 : vstart0);
-                compute(batch, ci * CB, min((ci + 1) * CB, nblk), wl, exl, vb, vsrc);
-                __syncwarp(gmask);  // every lane is done with this buffer before it is refilled
-            }
-            cc += static_cast<uint32_t>(nch);
-        }
         vb += total;
     }
-    if (!res_done) residual();
 
+    const int64_t row = br * kBlockRows + r;
+    if (row < k.rows && k.res_rp != nullptr) {
+        const int rs = k.res_rp[row];
+        const int re = k.res_rp[row + 1];
+        if (!(k.long_tau > 0 && re - rs > k.long_tau)) {
+            const int32_t* __restrict__ rc = k.res_col;
+#pragma unroll 2
+            for (int q = rs + s; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
+        }
+    }
     if constexpr (SLOTS > 1) sum += __shfl_xor_sync(gmask, sum, 8, G);
     if constexpr (SLOTS > 2) sum += __shfl_xor_sync(gmask, sum, 16, G);
     if (s == 0 && row < k.rows) y[row] = static_cast<T>(sum);
@@ -416,7 +268,7 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
                        int heavy_ctas, int chunk_ctas, int64_t num_out,
                        const int32_t* __restrict__ orow, const int32_t* __restrict__ ocol,
                        const T* __restrict__ oval) {
-    extern __shared__ __align__(128) unsigned char smem[];
+    extern __shared__ __align__(16) unsigned char smem[];
     dec.prepare(smem);
     __syncthreads();
     using Acc = typename Dec::Acc;
@@ -456,7 +308,7 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
                 for (int c = 0; c < 4; ++c) {
                     if (nib & (1u << c)) {
                         V raw{};
-                        if constexpr (Dec::kStage) raw = dec.kept[v0];
+                        if constexpr (Dec::kHasKept) raw = dec.kept[v0];
                         sum += dec.decode(raw, ctx, 4 * r + c) * dec.xv(x, c4 + c);
                         ++v0;
                     }
@@ -487,39 +339,11 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
     if (i < num_out) atomicAdd(&y[orow[i]], oval[i] * x[ocol[i]]);
 }
 
-// Opt a kernel into more than 48 KB of dynamic shared memory (once per size).
-void allow_smem(const void* fn, int bytes) {
-    static std::mutex mu;
-    static std::map<const void*, int> done;
-    if (bytes <= 48 * 1024) return;
-    std::lock_guard<std::mutex> lock(mu);
-    auto it = done.find(fn);
-    if (it != done.end() && it->second >= bytes) return;
-    CUDA_OK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    done[fn] = bytes;
-}
-
 template <typename T, typename Dec, int SLOTS>
-void launch_main(const KernelShape& k, const Dec& dec, int codebook_bytes, const T* x, T* y,
-                 cudaStream_t s) {
+void launch_main(const KernelShape& k, const Dec& dec, int smem, const T* x, T* y, cudaStream_t s) {
     constexpr int G = 8 * SLOTS;
-    using V = typename Dec::V;
-    SmemLayout L;
-    L.groups = kThreads / G;
-    L.codebook_bytes = (codebook_bytes + 15) & ~15;
-    if (Dec::kStage && k.stage_ok) {
-        // about 512 * SLOTS bytes of values per chunk (32 cells per block),
-        // at least one step of the slots and at most one word batch
-        int cb = (512 * SLOTS) / static_cast<int>(32 * sizeof(V));
-        cb = std::max(SLOTS, std::min(G, cb));
-        cb -= cb % SLOTS;
-        L.chunk_blocks = cb;
-        L.stage_bytes = (cb * 32 * static_cast<int>(sizeof(V)) + 32 + 15) & ~15;
-    }
-    const int grid = grid_for(k.nbr, L.groups);
-    auto fn = hybrid_main_kernel<T, Dec, SLOTS>;
-    allow_smem(reinterpret_cast<const void*>(fn), L.total());
-    fn<<<grid, kThreads, L.total(), s>>>(k, dec, L, x, y);
+    const int grid = grid_for(k.nbr, kThreads / G);
+    hybrid_main_kernel<T, Dec, SLOTS><<<grid, kThreads, smem, s>>>(k, dec, x, y);
     CUDA_LAUNCH_OK();
 }
 

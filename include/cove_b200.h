@@ -215,6 +215,43 @@ COVE_API const char* cove_route_name(int32_t route);
 COVE_API cove_status cove_plan_stream(const cove_plan* plan, int32_t which, void* dst_host,
                              size_t capacity, size_t* bytes, void* stream);
 
+/* ---- step-by-step device API on caller-owned buffers ------------------- */
+
+/*
+ * CSR -> BitBSR 8x4, first step: validates the CSR and writes
+ * block_row_ptr and block_row_val_ptr (both num_block_rows + 1 int32) and
+ * the block and nnz totals, so the caller can size the next step.
+ * With cove_bitbsr8x4_fill this replaces
+ * convert_to_bitbsr_gpu_warp_direct_8x4_device (gpu_convert.cuh:406-512).
+ */
+COVE_API cove_status cove_bitbsr8x4_count(const cove_csr_desc* csr, int32_t* block_row_ptr,
+                                          int32_t* block_row_val_ptr, int64_t* num_blocks,
+                                          int64_t* nnz, void* stream);
+/* Second step: block_col_idx (int32), bitmap (uint32) per block, values (T) per nnz. */
+COVE_API cove_status cove_bitbsr8x4_fill(const cove_csr_desc* csr, const int32_t* block_row_ptr,
+                                         const int32_t* block_row_val_ptr, int32_t* block_col_idx,
+                                         uint32_t* bitmap, void* values, void* stream);
+/* Packed words without flags: make_bitbsr_8x4_col_bitmap_packed (common.cuh:1024-1050). */
+COVE_API cove_status cove_pack_words(int64_t num_blocks, const int32_t* block_col_idx,
+                                     const uint32_t* bitmap, uint64_t* words, void* stream);
+/*
+ * Work items, first step: item_row_ptr (num_block_rows + 1) and the item
+ * count.  style = cove_lb_style.  Second step fills the 16-byte items and
+ * sets the flag bit of `words` where the layout asks for it.  Together they
+ * replace make_bitbsr_8x4_col_bitmap_flag_load_balance_work_items
+ * (common.cuh:1052-1147, style DEVICE) and make_fused_8x4_load_balance_layout_host
+ * (main_gpu_csr_bitbsr_spmv.cu:387-475, style HYBRID).
+ */
+COVE_API cove_status cove_lb_layout_count(int32_t num_block_rows, const int32_t* block_row_ptr,
+                                          int32_t chunk_blocks, int32_t split_threshold_blocks,
+                                          int32_t style, int32_t* item_row_ptr,
+                                          int64_t* num_items, void* stream);
+COVE_API cove_status cove_lb_layout_fill(int32_t num_block_rows, const int32_t* block_row_ptr,
+                                         const int32_t* block_row_val_ptr, const uint32_t* bitmap,
+                                         const int32_t* item_row_ptr, int32_t chunk_blocks,
+                                         int32_t split_threshold_blocks, int32_t style,
+                                         uint64_t* words, void* items, void* stream);
+
 /* ---- SpMV ----------------------------------------------------------- */
 
 /*
