@@ -373,13 +373,149 @@ def run_fem(args):
     return 0
 
 
+LAPL3D = dict(n=768, seed=4, iters=50)
+MAX_SHARD_NNZ = 2_000_000_000  # one plan per shard keeps the int32 offsets of the format
+
+
+def lapl3d_partition(rank, world, nx, ny, nz):
+    """z-slab rows [row_begin, row_end) of rank, its window (one plane of halo
+    each side) and its shards (whole planes, < MAX_SHARD_NNZ nnz each)."""
+    plane = nx * ny
+    cuts = [round(r * nz / world) for r in range(world + 1)]
+    k0, k1 = cuts[rank], cuts[rank + 1]
+    per_shard = max(1, MAX_SHARD_NNZ // (7 * plane))
+    shards = [(k * plane, min(k1, k + per_shard) * plane) for k in range(k0, k1, per_shard)]
+    wb = max(0, k0 - 1) * plane
+    we = min(nz, k1 + 1) * plane
+    return dict(row_begin=k0 * plane, row_end=k1 * plane, window_begin=wb, window_len=we - wb,
+                shards=shards)
+
+
+def run_lapl3d_cg(args):
+    """3D 7-point Laplacian CG, rows partitioned across the ranks (strong scaling)."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    import cove_b200 as cb
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    n1 = args.grid or LAPL3D["n"]
+    nx = ny = nz = n1
+    part = lapl3d_partition(rank, world, nx, ny, nz)
+    stream = torch.cuda.current_stream()
+    sh = C.c_void_p(stream.cuda_stream)
+    L = cb.lib()
+    plans = []
+    nnz_local = 0
+    t0 = time.perf_counter()
+    for (sb, se) in part["shards"]:
+        rows = se - sb
+        nnz = C.c_int64(0)
+        cb.check(L.cove_synth_lapl3d_device(nx, ny, nz, sb, se, part["window_begin"], None, None,
+                                            None, C.byref(nnz), sh))
+        rp = torch.empty(rows + 1, dtype=torch.int32, device=dev)
+        ci = torch.empty(nnz.value, dtype=torch.int32, device=dev)
+        v = torch.empty(nnz.value, dtype=torch.float64, device=dev)
+        cb.check(L.cove_synth_lapl3d_device(nx, ny, nz, sb, se, part["window_begin"],
+                                            C.c_void_p(rp.data_ptr()), C.c_void_p(ci.data_ptr()),
+                                            C.c_void_p(v.data_ptr()), C.byref(nnz), sh))
+        csr = cb.DeviceCsr(rows, part["window_len"], rp, ci, v)
+        plans.append(cb.Plan(csr, value_codec=args.codec, keep_lossless=0, stream=stream))
+        nnz_local += int(plans[-1].info.nnz)
+        del csr, rp, ci, v
+        torch.cuda.empty_cache()
+    build_s = time.perf_counter() - t0
+    rows_local = part["row_end"] - part["row_begin"]
+    b = torch.empty(rows_local, dtype=torch.float64, device=dev)
+    cb.check(L.cove_synth_vector_device(0, LAPL3D["seed"], 7, part["row_begin"], rows_local,
+                                        C.c_void_p(b.data_ptr()), sh))
+    x = torch.zeros(rows_local, dtype=torch.float64, device=dev)
+
+    idb = L.cove_dist_id_bytes()
+    idbuf = np.zeros(idb, np.uint8)
+    if rank == 0:
+        cb.check(L.cove_dist_make_id(idbuf.ctypes.data_as(C.c_void_p)))
+    if world > 1:
+        obj = [idbuf.tobytes()]
+        dist.broadcast_object_list(obj, src=0)
+        idbuf = np.frombuffer(obj[0], np.uint8).copy()
+    D = C.c_void_p()
+    arr = (C.c_void_p * len(plans))(*[p.handle.value for p in plans])
+    cb.check(L.cove_dist_create(rank, world, idbuf.ctypes.data_as(C.c_void_p), arr, len(plans),
+                                nx * ny * nz, part["row_begin"], part["row_end"],
+                                part["window_begin"], part["window_len"], 300000, C.byref(D)))
+    res = cb.CgResult()
+    # warm-up solve (untimed), then the timed solve; each is LAPL3D iterations
+    iters = args.cg_iters
+    cb.check(L.cove_dist_cg_solve(D, C.c_void_p(b.data_ptr()), C.c_void_p(x.data_ptr()),
+                                  min(iters, args.warmup), C.byref(res), sh))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.3)
+    cb.check(L.cove_dist_cg_solve(D, C.c_void_p(b.data_ptr()), C.c_void_p(x.data_ptr()), iters,
+                                  C.byref(res), sh))
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    # residual check of the solve: rs_final / rs_initial
+    vals = torch.tensor([res.ms_total, res.ms_spmv, float(nnz_local), res.rs_initial, res.rs_final],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = vals.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms_total, ms_spmv, nnz_total = float(mx[0]), float(mx[1]), float(sm[2])
+    else:
+        ms_total, ms_spmv, nnz_total = res.ms_total, res.ms_spmv, float(nnz_local)
+    if rank == 0:
+        per_iter = ms_total / iters
+        per_spmv = ms_spmv / iters
+        line = {
+            "metric": "cg_spmv_gflops", "value": round(2.0 * nnz_total / (per_spmv * 1e-3) / 1e9, 3),
+            "unit": "GFLOP/s", "n_gpus": world, "steps": iters, "warmup": args.warmup,
+            "ms_per_step": round(per_iter, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": f"3D 7-point Laplacian {nx}x{ny}x{nz} (n={nx * ny * nz}, nnz={int(nnz_total)}),"
+                                   f" {iters} textbook CG iterations",
+                       "route": cb.ROUTE_NAMES[plans[0].info.dispatched_route],
+                       "ms_per_iteration": round(per_iter, 5), "ms_per_spmv": round(per_spmv, 5),
+                       "cg_gflops_per_iteration": round((2.0 * nnz_total + 10.0 * nx * ny * nz) /
+                                                        (per_iter * 1e-3) / 1e9, 3),
+                       "rs_ratio": res.rs_final / res.rs_initial if res.rs_initial else None,
+                       "shards_per_rank": len(plans), "plan_build_s": round(build_s, 2),
+                       "parallelism": f"z-slab row blocks x{world}, NCCL halo + allreduce"},
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    L.cove_dist_destroy(D)
+    for p in plans:
+        p.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="fem27", choices=["fem27"])
+    ap.add_argument("--workload", default="fem27", choices=["fem27", "lapl3d_cg"])
+    ap.add_argument("--grid", type=int, default=0, help="lapl3d_cg: grid edge (default 768)")
+    ap.add_argument("--cg-iters", type=int, default=50)
     ap.add_argument("--codec", default="auto")
     ap.add_argument("--route", default=None,
                     help="time this route instead of the dispatched one (analysis only)")
@@ -389,6 +525,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload == "lapl3d_cg":
+        return run_lapl3d_cg(args)
     return run_fem(args)
 
 
