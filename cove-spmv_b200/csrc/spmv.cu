@@ -202,6 +202,24 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
     const uint32_t lowmask = (1u << (4 * r)) - 1u;
     Acc sum = Acc(0);
 
+    // The residual rows' pointers and each lane's first two residual entries
+    // are requested before the block loop, so the residual's dependent loads
+    // (row_ptr -> col -> x) overlap the blocks' (words -> values, x).
+    const int64_t row = br * kBlockRows + r;
+    int rq = 0, re = 0;
+    if (row < k.rows && k.res_rp != nullptr) {
+        rq = k.res_rp[row] + s;
+        re = k.res_rp[row + 1];
+        if (k.long_tau > 0 && re - (rq - s) > k.long_tau) re = rq;  // finished by the overflow pass
+    }
+    const int32_t* __restrict__ rc = k.res_col;
+    const bool have0 = rq < re;
+    const bool have1 = rq + SLOTS < re;
+    const int col0 = have0 ? __ldg(rc + rq) : 0;
+    const int col1 = have1 ? __ldg(rc + rq + SLOTS) : 0;
+    const Acc val0 = have0 ? dec.res_val(rq) : Acc(0);
+    const Acc val1 = have1 ? dec.res_val(rq + SLOTS) : Acc(0);
+
     // One coalesced load brings G block words into the group; a group scan of
     // their popcounts gives every block's value base; the blocks are then
     // handed to the slots by shuffle, so consecutive steps are independent.
@@ -245,16 +263,10 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
         vb += total;
     }
 
-    const int64_t row = br * kBlockRows + r;
-    if (row < k.rows && k.res_rp != nullptr) {
-        const int rs = k.res_rp[row];
-        const int re = k.res_rp[row + 1];
-        if (!(k.long_tau > 0 && re - rs > k.long_tau)) {
-            const int32_t* __restrict__ rc = k.res_col;
+    if (have0) sum += val0 * dec.xv(x, col0);
+    if (have1) sum += val1 * dec.xv(x, col1);
 #pragma unroll 2
-            for (int q = rs + s; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
-        }
-    }
+    for (int q = rq + 2 * SLOTS; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
     if constexpr (SLOTS > 1) sum += __shfl_xor_sync(gmask, sum, 8, G);
     if constexpr (SLOTS > 2) sum += __shfl_xor_sync(gmask, sum, 16, G);
     if (s == 0 && row < k.rows) y[row] = static_cast<T>(sum);

@@ -1,0 +1,207 @@
+// test_shim.cu -- the structural:: C++ API of the B200 library, exercised the
+// way the reference's own tests use it (structural/tests/test_gpu_convert.cu,
+// structural/src/main_gpu_csr_bitbsr_spmv.cu): GPU converter vs a host
+// conversion, packed words and work-item known answers, BitBSR-only
+// operators, the hybrid/joint launchers, and the device pipeline handle.
+// Built and run by tests/test_gpu_shim.py (needs a GPU).
+#include "structural/csr_bitbsr_hybrid.cuh"
+
+#include <cassert>
+#include <cmath>
+#include <cstdio>
+#include <map>
+#include <vector>
+
+#define CHECK(cond)                                                              \
+    do {                                                                         \
+        if (!(cond)) {                                                           \
+            std::fprintf(stderr, "%s:%d: CHECK failed: %s\n", __FILE__, __LINE__, #cond); \
+            std::exit(1);                                                        \
+        }                                                                        \
+    } while (0)
+
+using structural::CsrMatrix;
+
+namespace {
+
+std::vector<double> cpu_spmv(const CsrMatrix<double>& a, const std::vector<double>& x) {
+    std::vector<double> y(a.rows, 0.0);
+    for (int r = 0; r < a.rows; ++r)
+        for (int p = a.row_ptr[r]; p < a.row_ptr[r + 1]; ++p) y[r] += a.values[p] * x[a.col_idx[p]];
+    return y;
+}
+
+template <typename V>
+std::vector<V> host(const thrust::device_vector<V>& d) {
+    std::vector<V> h(d.size());
+    thrust::copy(d.begin(), d.end(), h.begin());
+    return h;
+}
+
+void close(const std::vector<double>& a, const std::vector<double>& b, double tol) {
+    CHECK(a.size() == b.size());
+    for (size_t i = 0; i < a.size(); ++i) CHECK(std::abs(a[i] - b[i]) <= tol);
+}
+
+CsrMatrix<double> kat_9x4404() {  // test_gpu_convert.cu:496-563
+    CsrMatrix<double> csr;
+    csr.rows = 9;
+    csr.cols = 4404;
+    csr.row_ptr = {0, 3, 5, 6, 7, 8, 8, 9, 9, 12};
+    csr.col_idx = {400, 416, 2000, 401, 417, 2001, 418, 402, 2002, 2800, 3600, 4400};
+    csr.values = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12};
+    return csr;
+}
+
+void test_converter_and_work_items() {
+    const auto csr = kat_9x4404();
+    structural::GpuBitBsrWorkspace<double> ws;
+    structural::DeviceBitBsrMatrix<double> dev;
+    structural::convert_to_bitbsr_gpu_warp_direct_8x4_device(csr, ws, dev);
+    CHECK(dev.num_blocks == 6 && dev.nnz == 12);
+    CHECK(host(dev.block_row_ptr) == (std::vector<int>{0, 3, 6}));
+    const auto h = dev.to_host();
+    CHECK(h.block_val_ptr.back() == 12);
+
+    thrust::device_vector<std::uint64_t> packed;
+    structural::make_bitbsr_8x4_col_bitmap_packed(dev, packed);
+    structural::BitBsrLoadBalanceLayout8x4 lb;
+    structural::make_bitbsr_8x4_col_bitmap_flag_load_balance_work_items(dev, lb, 2, packed);
+    const auto items = host(lb.work_items);
+    const auto words = host(packed);
+    CHECK(items.size() == 4);
+    const unsigned want[4][4] = {{0, 0, 2, 0}, {0, 2, 1, 6}, {1, 3, 2, 9}, {1, 5, 1, 11}};
+    for (int i = 0; i < 4; ++i) {
+        CHECK(items[i].br == want[i][0] && items[i].block_begin == want[i][1]);
+        CHECK(items[i].block_count == want[i][2] && items[i].value_begin == want[i][3]);
+    }
+    for (int b : {0, 2, 3, 5}) CHECK(structural::gpu_detail::unpack_col_bitmap_flag(words[b]));
+
+    structural::make_bitbsr_8x4_col_bitmap_flag_load_balance_work_items(dev, lb, 2, 4, packed);
+    CHECK(lb.work_items.size() == 2);  // :913-970
+    for (const auto w : host(packed)) CHECK(!structural::gpu_detail::unpack_col_bitmap_flag(w));
+}
+
+void test_bitbsr_only_operators() {
+    const auto csr = kat_9x4404();
+    std::vector<double> x(csr.cols);
+    for (int i = 0; i < csr.cols; ++i) x[i] = ((i % 13) - 6) * 0.25;
+    const auto expected = cpu_spmv(csr, x);
+    structural::GpuBitBsrWorkspace<double> ws;
+    const auto dev = structural::convert_to_bitbsr_gpu_warp_direct_8x4_device(csr, ws);
+    thrust::device_vector<double> dx(x.begin(), x.end()), dy;
+
+    structural::BitBsrSpmvPlan8x4<double> plan;
+    structural::make_bitbsr_8x4_col_bitmap_packed(dev, plan.packed_col_bitmap_meta);
+    structural::make_bitbsr_8x4_col_bitmap_flag_load_balance_work_items(
+        dev, plan.load_balance, 32, plan.packed_col_bitmap_meta);
+    float ms = -1.0f;
+    structural::run_bitbsr_spmv_once(dev, plan, dx, dy, &ms);
+    CHECK(ms >= 0.0f);
+    close(expected, host(dy), 1e-12);
+
+    // exact dictionary with per-cell 8-bit tile codes (codebook = sorted values)
+    const auto h = dev.to_host();
+    std::map<double, unsigned> id;
+    for (double v : h.values) id.emplace(v, 0);
+    std::vector<double> codebook;
+    for (auto& kv : id) {
+        kv.second = static_cast<unsigned>(codebook.size());
+        codebook.push_back(kv.first);
+    }
+    std::vector<std::uint32_t> tile(static_cast<size_t>(h.num_blocks()) * 8, 0);
+    for (int b = 0; b < h.num_blocks(); ++b) {
+        int k = h.block_val_ptr[b];
+        for (int bit = 0; bit < 32; ++bit) {
+            if (!(h.bitmap_words[b] & (1u << bit))) continue;
+            tile[b * 8 + bit / 4] |= id[h.values[k++]] << ((bit % 4) * 8);
+        }
+    }
+    plan.value_codec = structural::BitBsrValueCodecKind8x4::Dict256U8;
+    plan.tile_code_words = tile;
+    plan.value_codebook = codebook;
+    structural::run_bitbsr_spmv_once(dev, plan, dx, dy);
+    close(expected, host(dy), 1e-12);
+
+    plan.value_codec = structural::BitBsrValueCodecKind8x4::K256U8;
+    bool threw = false;
+    try {
+        structural::run_bitbsr_spmv_once(dev, plan, dx, dy);
+    } catch (const std::runtime_error&) {
+        threw = true;
+    }
+    CHECK(threw);
+}
+
+void test_hybrid_launchers_and_plan() {
+    // 4 x 8 matrix of test_gpu_csr_bitbsr_spmv_cli.sh:11-18, residual threshold 2
+    CsrMatrix<double> csr;
+    csr.rows = 4;
+    csr.cols = 8;
+    csr.row_ptr = {0, 2, 3, 4, 5};
+    csr.col_idx = {0, 7, 3, 1, 6};
+    csr.values = {1, 2, 3, 4, 5};
+    std::vector<double> x(8);
+    for (int i = 0; i < 8; ++i) x[i] = ((i % 17) - 8) * 0.125;
+    const auto expected = cpu_spmv(csr, x);
+
+    // split by hand: block (0, 0) kept (3 nnz), block (0, 1) residual (2 nnz)
+    structural::BitBsrMatrix<double> kept;
+    kept.rows = 4;
+    kept.cols = 8;
+    kept.block_rows = 8;
+    kept.block_cols = 4;
+    kept.num_block_rows = 1;
+    kept.num_block_cols = 2;
+    kept.words_per_block = 1;
+    kept.block_row_ptr = {0, 1};
+    kept.block_col_idx = {0};
+    kept.bitmap_words = {(1u << 0) | (1u << 7) | (1u << 9)};
+    kept.block_val_ptr = {0, 3};
+    kept.values = {1, 3, 4};
+    const auto dev = structural::copy_bitbsr_to_device(kept);
+    thrust::device_vector<std::uint64_t> packed;
+    structural::BitBsrLoadBalanceLayout8x4 lb;
+    structural::make_fused_8x4_load_balance_layout_host(kept, lb, packed, 32, 32);
+    CHECK(lb.work_items.size() == 1);
+    thrust::device_vector<int> rrp(std::vector<int>{0, 1, 1, 1, 2});
+    thrust::device_vector<int> rci(std::vector<int>{7, 6});
+    thrust::device_vector<double> rv(std::vector<double>{2, 5});
+    thrust::device_vector<int> cr, cb, cc;
+    thrust::device_vector<double> dx(x.begin(), x.end()), dy(4, 0.0);
+    structural::run_csr_bitbsr_fused_8x4_lb(dev, packed, lb, rrp, rci, rv, 0, cr, cb, cc, dx, dy);
+    close(expected, host(dy), 1e-12);
+
+    thrust::device_vector<std::uint8_t> kidx(std::vector<std::uint8_t>{0, 1, 2});
+    thrust::device_vector<std::uint8_t> ridx(std::vector<std::uint8_t>{3, 4});
+    thrust::device_vector<double> book(std::vector<double>{1, 3, 4, 2, 5});
+    structural::run_csr_bitbsr_fused_8x4_lb_dict<double, std::uint8_t>(dev, packed, lb, rrp, rci, kidx,
+                                                                       book, ridx, 0, cr, cb, cc, dx, dy);
+    close(expected, host(dy), 1e-12);
+
+    // the full device pipeline on the same CSR
+    cove_plan_opts o;
+    cove_plan_opts_default(&o);
+    o.residual_threshold = 2;
+    o.value_codec = COVE_CODEC_AUTO;
+    structural::cove::Plan<double> p(csr, &o);
+    CHECK(p.info().kept_blocks == 1 && p.info().residual_blocks == 1);
+    CHECK(p.info().joint_route == COVE_ROUTE_DICT_U8);
+    p.spmv(dx, dy);
+    close(expected, host(dy), 1e-12);
+}
+
+}  // namespace
+
+int main() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        std::fprintf(stderr, "SKIP: no CUDA device\n");
+        return 0;
+    }
+    test_converter_and_work_items();
+    test_bitbsr_only_operators();
+    test_hybrid_launchers_and_plan();
+    std::printf("shim tests passed\n");
+    return 0;
+}
