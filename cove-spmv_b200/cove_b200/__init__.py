@@ -119,6 +119,7 @@ EXPORTED = [
     "cove_lb_layout_count", "cove_lb_layout_fill",
     "cove_hybrid_spmv", "cove_spmv", "cove_spmv_route", "cove_spmv_host",
     "cove_spmv_launches", "cove_plan_device_error", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
+    "cove_cg_solve_noalloc",
     "cove_dist_halo_plan", "cove_dist_id_bytes", "cove_dist_make_id", "cove_dist_create", "cove_dist_destroy",
     "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv",
     "cove_rng_u64", "cove_rng_uniform01", "cove_synth_lapl2d", "cove_synth_lapl3d",
@@ -171,6 +172,7 @@ def _setup(L):
     L.cove_compare_vectors.argtypes = [vp, vp, i64, i32, vp, vp]
     L.cove_canonical_x.argtypes = [vp, i64, i32, vp]
     L.cove_cg_solve.argtypes = [vp, vp, vp, i32, C.POINTER(CgResult), vp]
+    L.cove_cg_solve_noalloc.argtypes = [vp, vp, vp, i32, C.POINTER(CgResult), vp]
     L.cove_dist_halo_plan.restype = i32
     L.cove_dist_halo_plan.argtypes = [i32, i32, vp, vp, i32]
     L.cove_dist_id_bytes.restype = C.c_size_t

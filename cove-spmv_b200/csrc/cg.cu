@@ -17,7 +17,9 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -499,3 +501,117 @@ cove_status cove_dist_cg_solve(cove_dist* d, const void* b_local, void* x_local,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// CG that allocates no device memory.
+//
+// Some callers cannot call cudaMalloc once they are running: applications
+// whose device memory is owned by their own arena or pool allocator (all of
+// HBM reserved at start-up, so a library's cudaMalloc fails or escapes their
+// accounting), and loops with a latency budget, where cudaMalloc and
+// cudaFree may synchronize the device and take unbounded time.  For them,
+// cove_cg_solve_noalloc runs the same recurrence as cove_cg_solve with its
+// work vectors in the fixed array below instead of freshly allocated
+// buffers.  The array is a module global: every GPU on which this file's
+// device code is loaded holds it until the process exits, and every call on
+// that GPU shares it.
+// ---------------------------------------------------------------------------
+
+namespace cove {
+namespace {
+// one vector segment per work vector (p, r, Ap); a multiple of 32 doubles,
+// so every segment starts 256-byte aligned like the array itself
+constexpr int64_t kNoAllocSeg = COVE_CG_NOALLOC_MAX_ROWS;
+static_assert(kNoAllocSeg % 32 == 0, "segments must stay 256-byte aligned");
+constexpr int64_t kNoAllocDoubles = 3 * kNoAllocSeg + kDotCtas + 8;
+}  // namespace
+}  // namespace cove
+
+// p | r | Ap | dot partials (kDotCtas) | scalar slots (8): about 3 MiB
+static __device__ __align__(256) double cove_cg_noalloc_scratch[cove::kNoAllocDoubles];
+
+namespace cove {
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+double* g_noalloc_base[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (the host-side name is only a stand-in for the symbol).
+double* noalloc_scratch() {
+    int dev = -1;
+    CUDA_OK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        COVE_THROW(COVE_ERR_UNSUPPORTED, "device ordinal beyond the no-allocation scratch table");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_base[dev]) {
+        double* ptr = nullptr;
+        CUDA_OK(cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), cove_cg_noalloc_scratch));
+        g_noalloc_base[dev] = ptr;
+    }
+    return g_noalloc_base[dev];
+}
+
+void cg_run_noalloc(const cove_plan* P, const double* b, double* x, int iters,
+                    cove_cg_result* res, cudaStream_t s) {
+    const int64_t n = P->rows;
+    double* base = noalloc_scratch();
+    double* p = base;
+    double* r = base + kNoAllocSeg;
+    double* ap = base + 2 * kNoAllocSeg;
+    double* partial = base + 3 * kNoAllocSeg;
+    double* S = partial + kDotCtas;  // [0,1] rs slots, [2] p.Ap, [4] rs0
+    // The array keeps the previous call's contents.  x accumulates, so it is
+    // cleared; the scalar slots are cleared too.  p and r are copied from b,
+    // and Ap and the partials are written in full before they are read.
+    CUDA_OK(cudaMemsetAsync(S, 0, 8 * sizeof(double), s));
+    CUDA_OK(cudaMemsetAsync(x, 0, static_cast<size_t>(n) * 8, s));
+    CUDA_OK(cudaMemcpyAsync(r, b, static_cast<size_t>(n) * 8, cudaMemcpyDeviceToDevice, s));
+    CUDA_OK(cudaMemcpyAsync(p, b, static_cast<size_t>(n) * 8, cudaMemcpyDeviceToDevice, s));
+    dot(n, r, r, partial, S + 0, s);
+    CUDA_OK(cudaMemcpyAsync(S + 4, S + 0, sizeof(double), cudaMemcpyDeviceToDevice, s));
+    const KernelShape shape = P->shape();
+    const RouteValues vals = P->route_values(P->dispatched_route);
+    const int ug = static_cast<int>(std::min<int64_t>(grid_for(n, kThreads), kDotCtas));
+    for (int k = 0; k < iters; ++k) {
+        const int cur = k & 1, nxt = cur ^ 1;
+        launch_hybrid_spmv(shape, vals, p, ap, s);
+        dot(n, p, ap, partial, S + 2, s);
+        cg_update_kernel<<<kDotCtas, kThreads, 0, s>>>(n, S, cur, p, ap, x, r, partial);
+        dot_final_kernel<<<1, kThreads, 0, s>>>(partial, kDotCtas, S + nxt);
+        cg_p_kernel<<<ug, kThreads, 0, s>>>(n, S, cur, nxt, r, p);
+    }
+    CUDA_LAUNCH_OK();
+    double h[8];
+    CUDA_OK(cudaMemcpyAsync(h, S, sizeof(h), cudaMemcpyDeviceToHost, s));
+    CUDA_OK(cudaStreamSynchronize(s));
+    if (res) {
+        res->iterations = iters;
+        res->rs_initial = h[4];
+        res->rs_final = h[iters & 1];
+        res->ms_total = 0.0;
+        res->ms_spmv = 0.0;
+    }
+}
+
+}  // namespace
+}  // namespace cove
+
+extern "C" cove_status cove_cg_solve_noalloc(const cove_plan* P, const void* b, void* x,
+                                             int32_t iters, cove_cg_result* result, void* stream) {
+    return guarded([&] {
+        if (!P || !b || !x) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        if (P->dtype != COVE_F64) COVE_THROW(COVE_ERR_UNSUPPORTED, "CG runs in fp64");
+        if (P->rows != P->cols) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "CG needs a square matrix");
+        if (iters < 0) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "iterations must be non-negative");
+        if (P->rows > COVE_CG_NOALLOC_MAX_ROWS)
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT,
+                       "cove_cg_solve_noalloc: " + std::to_string(P->rows) +
+                           " rows exceed its fixed scratch of " +
+                           std::to_string(COVE_CG_NOALLOC_MAX_ROWS) +
+                           " rows; use cove_cg_solve for larger systems");
+        cg_run_noalloc(P, static_cast<const double*>(b), static_cast<double*>(x), iters, result,
+                       static_cast<cudaStream_t>(stream));
+    });
+}

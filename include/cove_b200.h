@@ -358,6 +358,34 @@ typedef struct {
 COVE_API cove_status cove_cg_solve(const cove_plan* plan, const void* b, void* x, int32_t iters,
                           cove_cg_result* result, void* stream);
 
+/*
+ * CG that allocates no device memory.  It has no counterpart in the
+ * reference.
+ *
+ * For callers that cannot call cudaMalloc while they run: applications whose
+ * device memory belongs to their own pool or arena allocator (HBM reserved
+ * up front, so a library's cudaMalloc fails or bypasses their accounting),
+ * and loops with a latency budget, where cudaMalloc/cudaFree may synchronize
+ * the device and take unbounded time.  Build the plan at set-up; this call
+ * then runs the same recurrence as cove_cg_solve (same x and rs values)
+ * with its work vectors in one fixed device array of about 3 MiB, held by
+ * every GPU on which the library's CG code is loaded until the process
+ * exits.  It calls no cudaMalloc, cudaFree or other allocating routine.
+ *
+ * Limits and rules:
+ *  - plan rows <= COVE_CG_NOALLOC_MAX_ROWS; a larger plan is rejected with
+ *    COVE_ERR_INVALID_ARGUMENT and a message naming the limit;
+ *  - the first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture begins;
+ *  - all calls on one device share the array: calls that overlap on the GPU
+ *    (other streams, other host threads) race and give wrong results;
+ *  - synchronizes `stream`; result->ms_total and ms_spmv are 0 (no timing).
+ */
+#define COVE_CG_NOALLOC_MAX_ROWS 131072
+COVE_API cove_status cove_cg_solve_noalloc(const cove_plan* plan, const void* b, void* x,
+                                           int32_t iters, cove_cg_result* result, void* stream);
+
 /* ---- multi-GPU row-block partition (one process per GPU) -------------- */
 
 typedef struct cove_dist cove_dist;
