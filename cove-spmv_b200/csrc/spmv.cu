@@ -208,23 +208,24 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
     // overlap the blocks'.  Wide groups (block-dense rows) keep the registers
     // for the block loop and walk the residual afterwards.
     constexpr bool kPrefetch = SLOTS <= 2;
-    const int64_t row = br * kBlockRows + r;
-    auto residual_range = [&](int& q0, int& q1) {
+    int rq = 0, re = 0, col0 = 0, col1 = 0;
+    Acc val0 = Acc(0), val1 = Acc(0);
+    if constexpr (kPrefetch) {
+        const int64_t row = br * kBlockRows + r;
         if (row < k.rows && k.res_rp != nullptr) {
-            q0 = k.res_rp[row] + s;
-            q1 = k.res_rp[row + 1];
-            if (k.long_tau > 0 && q1 - (q0 - s) > k.long_tau) q1 = q0;  // finished by the overflow pass
+            rq = k.res_rp[row] + s;
+            re = k.res_rp[row + 1];
+            if (k.long_tau > 0 && re - (rq - s) > k.long_tau) re = rq;  // finished by the overflow pass
         }
-    };
-    int rq = 0, re = 0;
-    if constexpr (kPrefetch) residual_range(rq, re);
-    const int32_t* __restrict__ rc = k.res_col;
-    const bool have0 = kPrefetch && rq < re;
-    const bool have1 = kPrefetch && rq + SLOTS < re;
-    const int col0 = have0 ? __ldg(rc + rq) : 0;
-    const int col1 = have1 ? __ldg(rc + rq + SLOTS) : 0;
-    const Acc val0 = have0 ? dec.res_val(rq) : Acc(0);
-    const Acc val1 = have1 ? dec.res_val(rq + SLOTS) : Acc(0);
+        if (rq < re) {
+            col0 = __ldg(k.res_col + rq);
+            val0 = dec.res_val(rq);
+        }
+        if (rq + SLOTS < re) {
+            col1 = __ldg(k.res_col + rq + SLOTS);
+            val1 = dec.res_val(rq + SLOTS);
+        }
+    }
 
     // One coalesced load brings G block words into the group; a group scan of
     // their popcounts gives every block's value base; the blocks are then
@@ -269,12 +270,21 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
         vb += total;
     }
 
-    if constexpr (!kPrefetch) residual_range(rq, re);
-    if (have0) sum += val0 * dec.xv(x, col0);
-    if (have1) sum += val1 * dec.xv(x, col1);
+    const int64_t row = br * kBlockRows + r;
+    const int32_t* __restrict__ rc = k.res_col;
+    if constexpr (kPrefetch) {
+        if (rq < re) sum += val0 * dec.xv(x, col0);
+        if (rq + SLOTS < re) sum += val1 * dec.xv(x, col1);
 #pragma unroll 2
-    for (int q = kPrefetch ? rq + 2 * SLOTS : rq; q < re; q += SLOTS)
-        sum += dec.res_val(q) * dec.xv(x, rc[q]);
+        for (int q = rq + 2 * SLOTS; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
+    } else if (row < k.rows && k.res_rp != nullptr) {
+        const int rs = k.res_rp[row];
+        const int re_ = k.res_rp[row + 1];
+        if (!(k.long_tau > 0 && re_ - rs > k.long_tau)) {
+#pragma unroll 2
+            for (int q = rs + s; q < re_; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
+        }
+    }
     if constexpr (SLOTS > 1) sum += __shfl_xor_sync(gmask, sum, 8, G);
     if constexpr (SLOTS > 2) sum += __shfl_xor_sync(gmask, sum, 16, G);
     if (s == 0 && row < k.rows) y[row] = static_cast<T>(sum);
