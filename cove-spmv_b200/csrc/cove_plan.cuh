@@ -4,6 +4,33 @@
 #include "cove_codecs.cuh"
 #include "cove_spmv.cuh"
 
+#include <memory>
+
+namespace cove {
+
+// Copy/compute overlap of cove_spmv_host: x arrives in kx slices on one
+// copy stream; the main pass runs in ky block-row slices, each as soon as
+// the x slices up to its highest column have landed; each y slice leaves on
+// a second copy stream as soon as its rows are final.  Built on first use;
+// the sequence is replayed as a CUDA graph while the host buffers stay the same.
+struct HostPipeline {
+    int kx = 0, ky = 0;
+    std::vector<int64_t> x_cut;   // kx+1 element offsets into x
+    std::vector<int32_t> br_cut;  // ky+1 block-row offsets
+    std::vector<int> need;        // per block-row slice: last x slice it reads (-1: none)
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    std::vector<cudaEvent_t> x_ready, y_ready;
+    cudaEvent_t start = nullptr, out_done = nullptr;
+    // the sequence captured as a graph for one pair of host buffers
+    cudaStream_t s_cap = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    const void* graph_x = nullptr;
+    const void* graph_y = nullptr;
+    ~HostPipeline();
+};
+
+}  // namespace cove
+
 struct cove_plan {
     cove_plan_opts opts{};
     int dtype = COVE_F64;
@@ -46,6 +73,7 @@ struct cove_plan {
 
     // staging for cove_spmv_host
     cove::DevBuf x_stage, y_stage;
+    std::unique_ptr<cove::HostPipeline> pipe;
     cove::DevBuf err;  // int, set by a kernel whose bounded wait gave up
 
     cove::KernelShape shape() const;

@@ -25,6 +25,8 @@ struct RouteValues {
 struct KernelShape {
     int dtype = COVE_F64;
     int32_t rows = 0, cols = 0, nbr = 0;
+    int32_t br_begin = 0;                 // the main pass covers block rows [br_begin, nbr)
+    int part = 0;                         // 0: main + overflow pass, 1: main only, 2: overflow only
     const int32_t* kept_brp = nullptr;    // int32 nbr+1
     const int32_t* kept_brvp = nullptr;   // int32 nbr+1
     const int32_t* kept_bvp = nullptr;    // int32 kept blocks+1

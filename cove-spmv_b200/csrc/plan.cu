@@ -8,6 +8,7 @@
 // lossless hybrid instead.
 #include "cove_plan.cuh"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 
@@ -49,9 +50,173 @@ __global__ void canonical_x_kernel(int64_t n, T* __restrict__ x) {
     if (i < n) x[i] = static_cast<T>(static_cast<int>(i % 17) - 8) * static_cast<T>(0.125);
 }
 
+// Highest column of x each block row reads (kept blocks: the block's last
+// column, clipped to cols; residual rows are column-sorted, so their last
+// entry).  -1 for a block row without nonzeros.
+__global__ void block_row_max_col_kernel(int32_t nbr, int32_t rows, int32_t cols,
+                                         const int32_t* __restrict__ kbrp,
+                                         const uint64_t* __restrict__ words,
+                                         const int32_t* __restrict__ rrp,
+                                         const int32_t* __restrict__ rcol,
+                                         int32_t* __restrict__ out) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (br >= nbr) return;
+    int m = -1;
+    for (int b = kbrp[br]; b < kbrp[br + 1]; ++b)
+        m = max(m, min(static_cast<int>(words[b] & 0x7fffffffULL) * 4 + 3, cols - 1));
+    if (rrp != nullptr) {
+        const int64_t r1 = (br + 1) * kBlockRows < rows ? (br + 1) * kBlockRows : rows;
+        for (int64_t r = br * kBlockRows; r < r1; ++r)
+            if (rrp[r + 1] > rrp[r]) m = max(m, rcol[rrp[r + 1] - 1]);
+    }
+    out[br] = m;
+}
+
 }  // namespace
 
 void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+HostPipeline::~HostPipeline() {
+    for (cudaEvent_t e : x_ready) cudaEventDestroy(e);
+    for (cudaEvent_t e : y_ready) cudaEventDestroy(e);
+    if (start) cudaEventDestroy(start);
+    if (out_done) cudaEventDestroy(out_done);
+    if (s_in) cudaStreamDestroy(s_in);
+    if (s_out) cudaStreamDestroy(s_out);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (s_cap) cudaStreamDestroy(s_cap);
+}
+
+namespace {
+
+// Slices for a vector of n elements of esz bytes: about 2^COVE_HOST_SLICE_SHIFT
+// bytes each, at most COVE_HOST_MAX_SLICES; x boundaries on 32-element multiples.
+#ifndef COVE_HOST_SLICE_SHIFT
+#define COVE_HOST_SLICE_SHIFT 20
+#endif
+#ifndef COVE_HOST_MAX_SLICES
+#define COVE_HOST_MAX_SLICES 8
+#endif
+int slice_count(int64_t n, size_t esz) {
+    const int64_t bytes = n * static_cast<int64_t>(esz);
+    return static_cast<int>(std::max<int64_t>(
+        1, std::min<int64_t>(COVE_HOST_MAX_SLICES, bytes >> COVE_HOST_SLICE_SHIFT)));
+}
+
+std::unique_ptr<HostPipeline> build_host_pipeline(const cove_plan* P) {
+    auto hp = std::make_unique<HostPipeline>();
+    hp->kx = slice_count(P->cols, P->esz);
+    hp->ky = std::min<int>(slice_count(P->rows, P->esz), std::max<int32_t>(P->nbr, 1));
+    hp->x_cut.resize(hp->kx + 1);
+    for (int i = 0; i <= hp->kx; ++i) {
+        const int64_t c = (static_cast<int64_t>(P->cols) * i / hp->kx) & ~int64_t(31);
+        hp->x_cut[i] = i == hp->kx ? P->cols : c;
+    }
+    hp->br_cut.resize(hp->ky + 1);
+    for (int j = 0; j <= hp->ky; ++j)
+        hp->br_cut[j] = static_cast<int32_t>(static_cast<int64_t>(P->nbr) * j / hp->ky);
+    // the last x slice each block-row slice reads
+    std::vector<int32_t> mc(static_cast<size_t>(P->nbr));
+    if (P->nbr > 0) {
+        DevBuf d;
+        alloc_n<int32_t>(d, P->nbr);
+        const KernelShape k = P->shape();
+        block_row_max_col_kernel<<<grid_for(P->nbr, kThreads), kThreads>>>(
+            P->nbr, P->rows, P->cols, k.kept_brp, k.words, k.res_rp, k.res_col, d.as<int32_t>());
+        CUDA_LAUNCH_OK();
+        CUDA_OK(cudaMemcpy(mc.data(), d.p, mc.size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
+    }
+    hp->need.assign(hp->ky, -1);
+    int run = -1;
+    for (int j = 0; j < hp->ky; ++j) {
+        for (int32_t b = hp->br_cut[j]; b < hp->br_cut[j + 1]; ++b) run = std::max(run, mc[b]);
+        if (run >= 0) {
+            int i = 0;
+            while (hp->x_cut[i + 1] <= run) ++i;
+            hp->need[j] = i;
+        }
+    }
+    CUDA_OK(cudaStreamCreateWithFlags(&hp->s_in, cudaStreamNonBlocking));
+    CUDA_OK(cudaStreamCreateWithFlags(&hp->s_out, cudaStreamNonBlocking));
+    CUDA_OK(cudaStreamCreateWithFlags(&hp->s_cap, cudaStreamNonBlocking));
+    hp->x_ready.resize(hp->kx);
+    hp->y_ready.resize(hp->ky);
+    for (auto& e : hp->x_ready) CUDA_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (auto& e : hp->y_ready) CUDA_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    CUDA_OK(cudaEventCreateWithFlags(&hp->start, cudaEventDisableTiming));
+    CUDA_OK(cudaEventCreateWithFlags(&hp->out_done, cudaEventDisableTiming));
+    return hp;
+}
+
+bool is_pinned(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+// x slices in on s_in; block-row slices of the main pass on s, each after the
+// x slices it reads; y slices out on s_out as soon as their rows are final
+// (after the overflow pass, when the plan has one).  Everything joins s.
+void issue_sliced(const cove_plan* P, HostPipeline& hp, const void* x_host, void* y_host,
+                  cudaStream_t s) {
+    const KernelShape k = P->shape();
+    const RouteValues rv = P->route_values(P->dispatched_route);
+    auto* xs = static_cast<char*>(P->x_stage.p);
+    auto* ys = static_cast<char*>(P->y_stage.p);
+    const auto* xh = static_cast<const char*>(x_host);
+    auto* yh = static_cast<char*>(y_host);
+    const size_t esz = P->esz;
+    CUDA_OK(cudaEventRecord(hp.start, s));
+    CUDA_OK(cudaStreamWaitEvent(hp.s_in, hp.start, 0));
+    CUDA_OK(cudaStreamWaitEvent(hp.s_out, hp.start, 0));
+    for (int i = 0; i < hp.kx; ++i) {
+        const int64_t c0 = hp.x_cut[i], c1 = hp.x_cut[i + 1];
+        if (c1 > c0)
+            CUDA_OK(cudaMemcpyAsync(xs + c0 * esz, xh + c0 * esz, static_cast<size_t>(c1 - c0) * esz,
+                                    cudaMemcpyHostToDevice, hp.s_in));
+        CUDA_OK(cudaEventRecord(hp.x_ready[i], hp.s_in));
+    }
+    const bool late_rows = hybrid_spmv_launch_count(k, rv) > 1;
+    int waited = -1;
+    for (int j = 0; j < hp.ky; ++j) {
+        if (hp.need[j] > waited) {
+            waited = hp.need[j];
+            CUDA_OK(cudaStreamWaitEvent(s, hp.x_ready[waited], 0));
+        }
+        KernelShape kj = k;
+        kj.part = 1;
+        kj.br_begin = hp.br_cut[j];
+        kj.nbr = hp.br_cut[j + 1];
+        launch_hybrid_spmv(kj, rv, xs, ys, s);
+        if (!late_rows) {
+            const int64_t r0 = static_cast<int64_t>(hp.br_cut[j]) * kBlockRows;
+            const int64_t r1 =
+                std::min<int64_t>(static_cast<int64_t>(hp.br_cut[j + 1]) * kBlockRows, P->rows);
+            CUDA_OK(cudaEventRecord(hp.y_ready[j], s));
+            CUDA_OK(cudaStreamWaitEvent(hp.s_out, hp.y_ready[j], 0));
+            if (r1 > r0)
+                CUDA_OK(cudaMemcpyAsync(yh + r0 * esz, ys + r0 * esz, static_cast<size_t>(r1 - r0) * esz,
+                                        cudaMemcpyDeviceToHost, hp.s_out));
+        }
+    }
+    if (waited < hp.kx - 1) CUDA_OK(cudaStreamWaitEvent(s, hp.x_ready[hp.kx - 1], 0));
+    if (late_rows) {
+        KernelShape ko = k;
+        ko.part = 2;
+        launch_hybrid_spmv(ko, rv, xs, ys, s);
+        CUDA_OK(cudaEventRecord(hp.y_ready[0], s));
+        CUDA_OK(cudaStreamWaitEvent(hp.s_out, hp.y_ready[0], 0));
+        CUDA_OK(cudaMemcpyAsync(yh, ys, static_cast<size_t>(P->rows) * esz, cudaMemcpyDeviceToHost,
+                                hp.s_out));
+    }
+    CUDA_OK(cudaEventRecord(hp.out_done, hp.s_out));
+    CUDA_OK(cudaStreamWaitEvent(s, hp.out_done, 0));
+}
+
+}  // namespace
 
 }  // namespace cove
 
@@ -682,12 +847,41 @@ cove_status cove_spmv_host(cove_plan* P, const void* x_host, void* y_host, void*
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         if (!P->x_stage.p) P->x_stage.alloc(static_cast<size_t>(P->cols) * P->esz);
         if (!P->y_stage.p) P->y_stage.alloc(static_cast<size_t>(P->rows) * P->esz);
-        CUDA_OK(cudaMemcpyAsync(P->x_stage.p, x_host, static_cast<size_t>(P->cols) * P->esz,
-                                cudaMemcpyHostToDevice, s));
-        launch_hybrid_spmv(P->shape(), P->route_values(P->dispatched_route), P->x_stage.p,
-                           P->y_stage.p, s);
-        CUDA_OK(cudaMemcpyAsync(y_host, P->y_stage.p, static_cast<size_t>(P->rows) * P->esz,
-                                cudaMemcpyDeviceToHost, s));
+        if (!P->pipe) P->pipe = build_host_pipeline(P);
+        HostPipeline& hp = *P->pipe;
+        const bool overlap = (hp.kx > 1 || hp.ky > 1) && is_pinned(x_host) && is_pinned(y_host);
+        if (!overlap) {  // pageable buffers: copies are host-synchronous anyway
+            CUDA_OK(cudaMemcpyAsync(P->x_stage.p, x_host, static_cast<size_t>(P->cols) * P->esz,
+                                    cudaMemcpyHostToDevice, s));
+            launch_hybrid_spmv(P->shape(), P->route_values(P->dispatched_route), P->x_stage.p,
+                               P->y_stage.p, s);
+            CUDA_OK(cudaMemcpyAsync(y_host, P->y_stage.p, static_cast<size_t>(P->rows) * P->esz,
+                                    cudaMemcpyDeviceToHost, s));
+            CUDA_OK(cudaStreamSynchronize(s));
+            return;
+        }
+        // The sliced sequence is a few dozen API calls; it is captured once per
+        // pair of host buffers and replayed as one graph launch.
+        if (!(hp.exec && hp.graph_x == x_host && hp.graph_y == y_host)) {
+            if (hp.exec) cudaGraphExecDestroy(hp.exec);
+            hp.exec = nullptr;
+            cudaGraph_t g = nullptr;
+            CUDA_OK(cudaStreamBeginCapture(hp.s_cap, cudaStreamCaptureModeThreadLocal));
+            try {
+                issue_sliced(P, hp, x_host, y_host, hp.s_cap);
+            } catch (...) {
+                cudaStreamEndCapture(hp.s_cap, &g);
+                if (g) cudaGraphDestroy(g);
+                throw;
+            }
+            CUDA_OK(cudaStreamEndCapture(hp.s_cap, &g));
+            const cudaError_t ie = cudaGraphInstantiate(&hp.exec, g, 0);
+            cudaGraphDestroy(g);
+            CUDA_OK(ie);
+            hp.graph_x = x_host;
+            hp.graph_y = y_host;
+        }
+        CUDA_OK(cudaGraphLaunch(hp.exec, s));
         CUDA_OK(cudaStreamSynchronize(s));
     });
 }

@@ -189,7 +189,7 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
     const int s = gl >> 3;
     const int r = gl & 7;
     const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
-    const int64_t br = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
+    const int64_t br = k.br_begin + (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
     if (br >= k.nbr) return;  // the whole group leaves together
 
     const int b0 = k.kept_brp[br];
@@ -372,7 +372,7 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
 template <typename T, typename Dec, int SLOTS>
 void launch_main(const KernelShape& k, const Dec& dec, int smem, const T* x, T* y, cudaStream_t s) {
     constexpr int G = 8 * SLOTS;
-    const int grid = grid_for(k.nbr, kThreads / G);
+    const int grid = grid_for(static_cast<int64_t>(k.nbr) - k.br_begin, kThreads / G);
     hybrid_main_kernel<T, Dec, SLOTS><<<grid, kThreads, smem, s>>>(k, dec, x, y);
     CUDA_LAUNCH_OK();
 }
@@ -385,7 +385,7 @@ int launch_with(const KernelShape& k, Dec dec, size_t smem, const RouteValues& v
     int launches = 0;
     KernelShape kk = k;
     kk.x_vec_ok = (reinterpret_cast<uintptr_t>(xv) % 16 == 0) && (k.cols % 4 == 0);
-    if (k.nbr > 0) {
+    if (k.part != 2 && k.nbr > k.br_begin) {
         switch (k.slots) {
             case 1: launch_main<T, Dec, 1>(kk, dec, static_cast<int>(smem), x, y, s); break;
             case 2: launch_main<T, Dec, 2>(kk, dec, static_cast<int>(smem), x, y, s); break;
@@ -396,7 +396,7 @@ int launch_with(const KernelShape& k, Dec dec, size_t smem, const RouteValues& v
     const int heavy_ctas = grid_for(k.num_heavy, kThreads / 32);
     const int chunk_ctas = grid_for(k.num_chunks, kThreads / 32);
     const int out_ctas = grid_for(v.num_outliers, kThreads);
-    if (heavy_ctas + chunk_ctas + out_ctas > 0) {
+    if (k.part != 1 && heavy_ctas + chunk_ctas + out_ctas > 0) {
         hybrid_overflow_kernel<T, Dec><<<heavy_ctas + chunk_ctas + out_ctas, kThreads, smem, s>>>(
             kk, dec, x, y, heavy_ctas, chunk_ctas, v.num_outliers, v.out_rows, v.out_cols,
             static_cast<const T*>(v.out_vals));

@@ -344,6 +344,42 @@ def test_spmv_host_matches_device():
     assert np.array_equal(yh, yd)  # same kernel, deterministic stores
 
 
+def _pinned(n):
+    import torch
+
+    return torch.empty(n, dtype=torch.float64, pin_memory=True).numpy()
+
+
+@pytest.mark.parametrize("long_row", [False, True])
+def test_spmv_host_sliced_overlap_matches_device(long_row):
+    """Pinned host buffers of a few MB take the sliced path (x slices in, block-row
+    slices of the main pass, y slices out on a second copy stream); with a long
+    residual row the y copy waits for the overflow pass instead."""
+    rows, cols, rp, ci, v = cb.synth_lapl3d(100, 100, 100)
+    if long_row:
+        lc = np.arange(0, cols, 3, dtype=np.int32)
+        a, b = rp[5], rp[6]
+        ci = np.concatenate([ci[:a], lc, ci[b:]])
+        v = np.concatenate([v[:a], np.linspace(-1.0, 1.0, lc.size), v[b:]])
+        rp = rp.astype(np.int64)
+        rp[6:] += lc.size - (b - a)
+    p = plan_for(rows, cols, rp, ci, v, value_codec="auto", long_row_split=256)
+    assert (p.info.kernel_overflow_tasks > 0) == long_row
+    x = cb.synth_vector("uniform_pm1", cols, seed=3)
+    yd = gpu_spmv(p, x)
+    xh = _pinned(cols)
+    xh[:] = x
+    for _ in range(2):  # first call builds the slices, second reuses them
+        yh = _pinned(rows)
+        yh[:] = np.nan
+        p.spmv_host(xh, yh)
+        if long_row:  # the long row's chunks add in any order
+            assert np.abs(yh - yd).max() <= 1e-12 * np.abs(yd).max()
+        else:
+            assert np.array_equal(yh, yd)
+    assert np.array_equal(p.spmv_host(x), yd) or long_row  # pageable buffers: one-shot path
+
+
 @pytest.mark.parametrize("cfg", ["lapl2d_512", "fem27_64", "rmat_22"])
 def test_full_size_configs(cfg):
     """BASELINE configs 1-3 at full size: streams bit-exact, routes, SpMV."""
