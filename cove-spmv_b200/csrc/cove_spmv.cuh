@@ -33,7 +33,7 @@ struct KernelShape {
     const uint64_t* words = nullptr;      // packed words (flag bit ignored)
     const int32_t* res_rp = nullptr;      // int32 rows+1
     const int32_t* res_col = nullptr;
-    int slots = 4;                        // lanes per block row = 8 * slots
+    int slots = 4;                        // lanes per block row = 8 * slots; 0: one lane per row
     int heavy_limit = 0x7fffffff;         // blocks a block row handles in the main pass
     int long_tau = 0;                     // residual rows longer than this go to chunks
     bool x_vec_ok = false;                // set per launch: x 16-byte aligned, cols % 4 == 0
@@ -55,7 +55,8 @@ int launch_hybrid_spmv(const KernelShape& k, const RouteValues& v, const void* x
                        cudaStream_t s);
 int hybrid_spmv_launch_count(const KernelShape& k, const RouteValues& v);
 
-// Choose lanes per block row from the average kept blocks / residual nnz.
+// Choose lanes per block row from the average kept blocks per block row and
+// residual entries per row; 0 selects the lane-per-row kernel (short rows).
 int choose_slots(int64_t nbr, int64_t kept_blocks, int64_t rows, int64_t residual_nnz);
 
 }  // namespace cove

@@ -312,7 +312,10 @@ void build_plan_typed(cove_plan* P, const cove_csr_desc& d, cudaStream_t s) {
     // kernel work split
     P->slots = choose_slots(P->nbr, P->sp.kept_blocks, P->rows, P->sp.residual_nnz);
     const double avg_blocks = P->nbr > 0 ? static_cast<double>(P->sp.kept_blocks) / P->nbr : 0.0;
-    P->heavy_limit = static_cast<int>(std::max(256.0, 8.0 * std::ceil(avg_blocks)));
+    // a block row's blocks beyond the limit go to 256-block overflow pieces;
+    // a lane-per-row launch walks blocks serially, so its limit is lower
+    P->heavy_limit = static_cast<int>(
+        std::max(P->slots == 0 ? 32.0 : 256.0, 8.0 * std::ceil(avg_blocks)));
     const int piece = 256;
     {
         DevBuf cnt, off;
@@ -336,8 +339,9 @@ void build_plan_typed(cove_plan* P, const cove_csr_desc& d, cudaStream_t s) {
             CUDA_LAUNCH_OK();
         }
     }
-    // residual rows longer than 64 entries per lane go to 1024-nnz warp chunks
-    P->long_tau = 64 * P->slots;
+    // residual rows longer than 64 entries per lane (32 for one lane per row)
+    // go to 1024-nnz warp chunks
+    P->long_tau = P->slots == 0 ? 32 : 64 * P->slots;
     if (o.long_row_split > 0 && o.long_row_split == P->long_tau) {
         P->kchunks_alias = true;
     } else {
@@ -802,7 +806,8 @@ cove_status cove_hybrid_spmv(const cove_hybrid_desc* a, const cove_values_desc* 
         k.words = a->words;
         k.res_rp = a->res_row_ptr;
         k.res_col = a->res_col_idx;
-        k.slots = choose_slots(a->num_block_rows, a->kept_blocks, a->rows, a->residual_nnz);
+        // the caller's layout has no heavy-row split: keep the group kernel
+        k.slots = std::max(1, choose_slots(a->num_block_rows, a->kept_blocks, a->rows, a->residual_nnz));
         k.long_tau = a->num_chunks > 0 ? a->long_row_tau : 0;
         k.num_chunks = a->num_chunks > 0 ? a->num_chunks : 0;
         k.chunk_row = a->chunk_row;

@@ -290,6 +290,71 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
     if (s == 0 && row < k.rows) y[row] = static_cast<T>(sum);
 }
 
+// ---- main pass, one lane per row (block rows with few blocks) ------------------
+//
+// For short rows (a few kept blocks per block row, a few residual entries
+// per row) the group machinery above costs more instructions than the work
+// itself.  Here lane = row: it walks its row's nibble of each block of its
+// block row in order (the 8 lanes of a block row read the same word, one
+// transaction), then its residual entries.  Same accumulation order as the
+// one-slot group, so the results are identical.
+
+template <typename T, typename Dec>
+__global__ void __launch_bounds__(kThreads)
+hybrid_row_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    dec.prepare(smem);
+    __syncthreads();  // a shared codebook is complete before any lane reads it
+    using Acc = typename Dec::Acc;
+    using V = typename Dec::V;
+    const int64_t row = static_cast<int64_t>(k.br_begin) * kBlockRows +
+                        static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    const int64_t brows = static_cast<int64_t>(k.nbr) * kBlockRows;
+    if (row >= (brows < k.rows ? brows : k.rows)) return;
+    const int64_t br = row / kBlockRows;
+    const int r = static_cast<int>(row % kBlockRows);
+
+    const int b0 = k.kept_brp[br];
+    int b1 = k.kept_brp[br + 1];
+    if (b1 - b0 > k.heavy_limit) b1 = b0 + k.heavy_limit;
+    int vb = k.kept_brvp[br];
+    int q = 0, qe = 0;
+    if (k.res_rp != nullptr) {
+        q = k.res_rp[row];
+        qe = k.res_rp[row + 1];
+        if (k.long_tau > 0 && qe - q > k.long_tau) qe = q;  // finished by the overflow pass
+    }
+    const uint64_t* __restrict__ words = k.words;
+    const V* __restrict__ kept = dec.kept;
+    const int32_t* __restrict__ rc = k.res_col;
+    const uint32_t lowmask = (1u << (4 * r)) - 1u;
+    Acc sum = Acc(0);
+#pragma unroll 2
+    for (int b = b0; b < b1; ++b) {
+        const uint64_t w = __ldg(words + b);
+        const uint32_t bm = static_cast<uint32_t>(w >> 32);
+        const uint32_t nib = (bm >> (4 * r)) & 0xFu;
+        if (nib) {
+            const int64_t c4 = static_cast<int64_t>(w & 0x7fffffffULL) * 4;
+            const Acc ctx = dec.block_ctx(b);
+            int v0 = vb + __popc(bm & lowmask);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (nib & (1u << c)) {
+                    V raw{};
+                    if constexpr (Dec::kHasKept) raw = kept[v0];
+                    sum += dec.decode(raw, ctx, 4 * r + c) * dec.xv(x, c4 + c);
+                    ++v0;
+                }
+            }
+        }
+        vb += __popc(bm);
+    }
+#pragma unroll 4
+    for (; q < qe; ++q) sum += dec.res_val(q) * dec.xv(x, rc[q]);
+    y[row] = static_cast<T>(sum);
+}
+
 // ---- overflow pass: heavy block-row pieces, long residual chunks, outliers ----
 
 template <typename T, typename Dec>
@@ -371,9 +436,15 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
 
 template <typename T, typename Dec, int SLOTS>
 void launch_main(const KernelShape& k, const Dec& dec, int smem, const T* x, T* y, cudaStream_t s) {
-    constexpr int G = 8 * SLOTS;
-    const int grid = grid_for(static_cast<int64_t>(k.nbr) - k.br_begin, kThreads / G);
-    hybrid_main_kernel<T, Dec, SLOTS><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+    if constexpr (SLOTS == 0) {
+        const int64_t rows = std::min<int64_t>(static_cast<int64_t>(k.nbr) * kBlockRows, k.rows) -
+                             static_cast<int64_t>(k.br_begin) * kBlockRows;
+        hybrid_row_kernel<T, Dec><<<grid_for(rows, kThreads), kThreads, smem, s>>>(k, dec, x, y);
+    } else {
+        constexpr int G = 8 * SLOTS;
+        const int grid = grid_for(static_cast<int64_t>(k.nbr) - k.br_begin, kThreads / G);
+        hybrid_main_kernel<T, Dec, SLOTS><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+    }
     CUDA_LAUNCH_OK();
 }
 
@@ -387,6 +458,7 @@ int launch_with(const KernelShape& k, Dec dec, size_t smem, const RouteValues& v
     kk.x_vec_ok = (reinterpret_cast<uintptr_t>(xv) % 16 == 0) && (k.cols % 4 == 0);
     if (k.part != 2 && k.nbr > k.br_begin) {
         switch (k.slots) {
+            case 0: launch_main<T, Dec, 0>(kk, dec, static_cast<int>(smem), x, y, s); break;
             case 1: launch_main<T, Dec, 1>(kk, dec, static_cast<int>(smem), x, y, s); break;
             case 2: launch_main<T, Dec, 2>(kk, dec, static_cast<int>(smem), x, y, s); break;
             default: launch_main<T, Dec, 4>(kk, dec, static_cast<int>(smem), x, y, s); break;
@@ -471,7 +543,9 @@ int hybrid_spmv_launch_count(const KernelShape& k, const RouteValues& v) {
 int choose_slots(int64_t nbr, int64_t kept_blocks, int64_t rows, int64_t residual_nnz) {
     const double kb = nbr > 0 ? static_cast<double>(kept_blocks) / static_cast<double>(nbr) : 0.0;
     const double rr = rows > 0 ? static_cast<double>(residual_nnz) / static_cast<double>(rows) : 0.0;
-    if (kb >= 8.0 || rr >= 8.0) return 4;
+    if (kb >= 8.0) return 4;
+    if (kb < 6.0 && rr < 6.0) return 0;
+    if (rr >= 24.0) return 4;
     if (kb >= 1.5 || rr >= 2.5) return 2;
     return 1;
 }

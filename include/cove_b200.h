@@ -141,7 +141,7 @@ typedef struct {
     double joint_bytes_per_nnz;  /* reference formula, :1261-1263 / :1322-1325 / :1354-1356 */
     double outlier_threshold;
     int64_t algorithmic_bytes[5];/* bytes one SpMV of each cove_route must move (0 if absent) */
-    int32_t kernel_slots;        /* lanes per block row / 8 in the fused kernel */
+    int32_t kernel_slots;        /* lanes per block row / 8 in the fused kernel; 0: one lane per row */
     int32_t kernel_overflow_tasks;
 } cove_plan_info;
 

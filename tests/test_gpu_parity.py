@@ -335,6 +335,29 @@ def test_long_rows_and_heavy_block_rows_overflow_path():
             assert O.compare_vectors(y0, y)[2] <= 1e-2
 
 
+def test_lane_per_row_kernel_with_overflow_pieces():
+    """A 5-point Laplacian selects the one-lane-per-row kernel; a long residual
+    row and a dense block row added to it go to the overflow pass."""
+    import scipy.sparse as sp
+
+    rows, cols, rp, ci, v = cb.synth_lapl2d(256, 256)
+    A = sp.csr_matrix((v, ci, rp), shape=(rows, cols)).tolil()
+    rng = np.random.default_rng(5)
+    A[77, np.arange(0, cols, 21)] = rng.standard_normal(len(range(0, cols, 21)))  # long residual row
+    for r in range(800, 808):  # one block row with 300 dense 8x4 blocks
+        A[r, 4000:5200] = rng.standard_normal(1200)
+    A = A.tocsr()
+    A.sort_indices()
+    p = plan_for(rows, cols, A.indptr.astype(np.int64), A.indices.astype(np.int32), A.data,
+                 value_codec="original", gate_enable=0)
+    assert p.info.kernel_slots == 0
+    assert p.info.kernel_overflow_tasks > 0 and p.launches() == 2
+    x = cb.synth_vector("uniform_pm1", cols, seed=8)
+    y = gpu_spmv(p, x)
+    ref = A @ x
+    assert np.abs(y - ref).max() <= 1e-12 * np.abs(ref).max()
+
+
 def test_spmv_host_matches_device():
     rows, cols, rp, ci, v = cb.synth_fem27(12, 10, 9, 3, seed=5)
     p = plan_for(rows, cols, rp, ci, v, value_codec="auto")
