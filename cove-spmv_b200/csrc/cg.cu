@@ -175,11 +175,25 @@ struct cove_dist {
         int64_t send_off, send_n, recv_off, recv_n;  // offsets into this rank's window
     };
     std::vector<Xfer> xfers;
+    // Halo overlap: per plan, block-row ranges that read only the rank's own
+    // columns (run while the halo is in flight on s_comm) and ranges that
+    // read halo columns (run after it lands).
+    struct Range {
+        int32_t b0, b1;
+        bool halo;
+    };
+    std::vector<std::vector<Range>> ranges;
+    bool overlap = false;
+    cudaStream_t s_comm = nullptr;
+    cudaEvent_t x_ready = nullptr, halo_done = nullptr;
 };
 
 namespace cove {
 namespace {
 
+// A non-blocking communicator finishes enqueuing an operation within
+// microseconds: poll tightly first (every launch after it waits for this),
+// then back off so a stalled peer does not burn a core until the deadline.
 void wait_comm_ready(ncclComm_t comm, int timeout_ms) {
     const auto t0 = std::chrono::steady_clock::now();
     while (true) {
@@ -196,7 +210,11 @@ void wait_comm_ready(ncclComm_t comm, int timeout_ms) {
             nccl().CommAbort(comm);
             COVE_THROW(COVE_ERR_TIMEOUT, "NCCL communicator did not become ready in time");
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(200));
+        if (ms < 5) {
+            std::this_thread::yield();
+        } else {
+            std::this_thread::sleep_for(std::chrono::microseconds(100));
+        }
     }
 }
 
@@ -224,7 +242,11 @@ void wait_stream(cove_dist* d, cudaStream_t s) {
             d->comm = nullptr;
             COVE_THROW(COVE_ERR_TIMEOUT, "stream did not finish before the deadline");
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (ms < 5) {
+            std::this_thread::yield();
+        } else {
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+        }
     }
 }
 
@@ -260,6 +282,86 @@ float spmv_plans(const std::vector<cove_plan*>& plans, const double* xw, double*
         off += P->rows;
     }
     return 0.0f;
+}
+
+// y_local = A_local x_window on a partition: the halo runs on the comm
+// stream while the block rows that read only own columns are computed; the
+// rest follow once it has landed, then any overflow pass.
+void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s) {
+    if (!d->overlap) {
+        halo(d, xw, s);
+        spmv_plans(d->plans, xw, y, s);
+        return;
+    }
+    CUDA_OK(cudaEventRecord(d->x_ready, s));
+    CUDA_OK(cudaStreamWaitEvent(d->s_comm, d->x_ready, 0));
+    halo(d, xw, d->s_comm);
+    CUDA_OK(cudaEventRecord(d->halo_done, d->s_comm));
+    for (int pass = 0; pass < 2; ++pass) {
+        if (pass == 1) CUDA_OK(cudaStreamWaitEvent(s, d->halo_done, 0));
+        int64_t off = 0;
+        for (size_t i = 0; i < d->plans.size(); ++i) {
+            const cove_plan* P = d->plans[i];
+            const KernelShape k = P->shape();
+            const RouteValues rv = P->route_values(P->dispatched_route);
+            for (const auto& r : d->ranges[i]) {
+                if (r.halo != (pass == 1)) continue;
+                KernelShape kr = k;
+                kr.part = 1;
+                kr.br_begin = r.b0;
+                kr.nbr = r.b1;
+                launch_hybrid_spmv(kr, rv, xw, y + off, s);
+            }
+            off += P->rows;
+        }
+    }
+    int64_t off = 0;
+    for (const cove_plan* P : d->plans) {
+        const KernelShape k = P->shape();
+        const RouteValues rv = P->route_values(P->dispatched_route);
+        if (hybrid_spmv_launch_count(k, rv) > 1) {
+            KernelShape ko = k;
+            ko.part = 2;
+            launch_hybrid_spmv(ko, rv, xw, y + off, s);
+        }
+        off += P->rows;
+    }
+}
+
+// Split each plan's block rows into runs that read only the rank's own
+// columns [own_lo, own_hi) of the window and runs that read halo columns.
+void plan_overlap(cove_dist* d) {
+    d->ranges.clear();
+    d->overlap = false;
+    if (d->world == 1 || d->xfers.empty()) return;
+    const int64_t own_lo = d->row_begin - d->wb, own_hi = d->row_end - d->wb;
+    size_t runs = 0;
+    bool any_interior = false;
+    for (const cove_plan* P : d->plans) {
+        std::vector<int32_t> lo, hi;
+        block_row_col_bounds(P, &lo, &hi);
+        std::vector<cove_dist::Range> rs;
+        for (int32_t b = 0; b < P->nbr; ++b) {
+            const bool h = hi[b] >= 0 && (lo[b] < own_lo || hi[b] >= own_hi);
+            if (!rs.empty() && rs.back().halo == h) {
+                rs.back().b1 = b + 1;
+            } else {
+                rs.push_back({b, b + 1, h});
+            }
+            any_interior |= !h;
+        }
+        runs += rs.size();
+        d->ranges.push_back(std::move(rs));
+    }
+    // many short runs would cost more launches than the overlap saves
+    if (!any_interior || runs > 16) {
+        d->ranges.clear();
+        return;
+    }
+    CUDA_OK(cudaStreamCreateWithFlags(&d->s_comm, cudaStreamNonBlocking));
+    CUDA_OK(cudaEventCreateWithFlags(&d->x_ready, cudaEventDisableTiming));
+    CUDA_OK(cudaEventCreateWithFlags(&d->halo_done, cudaEventDisableTiming));
+    d->overlap = true;
 }
 
 void dot(int64_t n, const double* a, const double* b, double* partial, double* out,
@@ -303,9 +405,13 @@ void cg_run(cove_dist* d, const std::vector<cove_plan*>& plans, int64_t n_local,
     CUDA_OK(cudaEventRecord(e0, s));
     for (int k = 0; k < iters; ++k) {
         const int cur = k & 1, nxt = cur ^ 1;
-        halo(d, pw.as<double>(), s);
+        // the distributed SpMV: halo exchange overlapped with own-column rows
         CUDA_OK(cudaEventRecord(ev[2 * k], s));
-        spmv_plans(plans, pw.as<double>(), ap.as<double>(), s);
+        if (d) {
+            spmv_dist(d, pw.as<double>(), ap.as<double>(), s);
+        } else {
+            spmv_plans(plans, pw.as<double>(), ap.as<double>(), s);
+        }
         CUDA_OK(cudaEventRecord(ev[2 * k + 1], s));
         dot(n_local, p, ap.as<double>(), partial.as<double>(), S + 2, s);
         allreduce_scalar(d, S + 2, s);
@@ -453,8 +559,12 @@ cove_status cove_dist_create(int32_t rank, int32_t world, const void* nccl_id,
                 d->xfers.push_back(cove_dist::Xfer{static_cast<int>(xf[5 * i]), xf[5 * i + 1], xf[5 * i + 2],
                                                    xf[5 * i + 3], xf[5 * i + 4]});
             }
+            plan_overlap(d);
         } catch (...) {
             if (d->comm) nccl().CommAbort(d->comm);
+            if (d->x_ready) cudaEventDestroy(d->x_ready);
+            if (d->halo_done) cudaEventDestroy(d->halo_done);
+            if (d->s_comm) cudaStreamDestroy(d->s_comm);
             delete d;
             throw;
         }
@@ -470,6 +580,9 @@ cove_status cove_dist_destroy(cove_dist* d) {
             wait_comm_ready(d->comm, d->timeout_ms);
             nccl().CommDestroy(d->comm);
         }
+        if (d->x_ready) cudaEventDestroy(d->x_ready);
+        if (d->halo_done) cudaEventDestroy(d->halo_done);
+        if (d->s_comm) cudaStreamDestroy(d->s_comm);
         delete d;
     });
 }
@@ -484,9 +597,8 @@ cove_status cove_dist_halo(cove_dist* d, void* x_window, void* stream) {
 cove_status cove_dist_spmv(cove_dist* d, void* x_window, void* y_local, void* stream) {
     return guarded([&] {
         if (!d || !x_window || !y_local) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
-        cudaStream_t s = static_cast<cudaStream_t>(stream);
-        halo(d, static_cast<double*>(x_window), s);
-        spmv_plans(d->plans, static_cast<const double*>(x_window), static_cast<double*>(y_local), s);
+        spmv_dist(d, static_cast<double*>(x_window), static_cast<double*>(y_local),
+                  static_cast<cudaStream_t>(stream));
     });
 }
 

@@ -29,6 +29,10 @@ struct HostPipeline {
     ~HostPipeline();
 };
 
+// Per block row, the lowest and highest column of x the SpMV reads
+// ({INT_MAX, -1} for an empty block row); synchronous.
+void block_row_col_bounds(const cove_plan* P, std::vector<int32_t>* lo, std::vector<int32_t>* hi);
+
 }  // namespace cove
 
 struct cove_plan {

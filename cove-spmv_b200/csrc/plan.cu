@@ -50,31 +50,55 @@ __global__ void canonical_x_kernel(int64_t n, T* __restrict__ x) {
     if (i < n) x[i] = static_cast<T>(static_cast<int>(i % 17) - 8) * static_cast<T>(0.125);
 }
 
-// Highest column of x each block row reads (kept blocks: the block's last
-// column, clipped to cols; residual rows are column-sorted, so their last
-// entry).  -1 for a block row without nonzeros.
-__global__ void block_row_max_col_kernel(int32_t nbr, int32_t rows, int32_t cols,
-                                         const int32_t* __restrict__ kbrp,
-                                         const uint64_t* __restrict__ words,
-                                         const int32_t* __restrict__ rrp,
-                                         const int32_t* __restrict__ rcol,
-                                         int32_t* __restrict__ out) {
+// Lowest and highest column of x each block row reads: a kept block reads
+// its four columns (clipped to cols), a residual row (column-sorted) its
+// first to last entry.  {INT_MAX, -1} for a block row without nonzeros.
+__global__ void block_row_col_bounds_kernel(int32_t nbr, int32_t rows, int32_t cols,
+                                            const int32_t* __restrict__ kbrp,
+                                            const uint64_t* __restrict__ words,
+                                            const int32_t* __restrict__ rrp,
+                                            const int32_t* __restrict__ rcol,
+                                            int32_t* __restrict__ lo, int32_t* __restrict__ hi) {
     const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (br >= nbr) return;
-    int m = -1;
-    for (int b = kbrp[br]; b < kbrp[br + 1]; ++b)
-        m = max(m, min(static_cast<int>(words[b] & 0x7fffffffULL) * 4 + 3, cols - 1));
+    int mn = 0x7fffffff, mx = -1;
+    for (int b = kbrp[br]; b < kbrp[br + 1]; ++b) {
+        const int c4 = static_cast<int>(words[b] & 0x7fffffffULL) * 4;
+        mn = min(mn, c4);
+        mx = max(mx, min(c4 + 3, cols - 1));
+    }
     if (rrp != nullptr) {
         const int64_t r1 = (br + 1) * kBlockRows < rows ? (br + 1) * kBlockRows : rows;
-        for (int64_t r = br * kBlockRows; r < r1; ++r)
-            if (rrp[r + 1] > rrp[r]) m = max(m, rcol[rrp[r + 1] - 1]);
+        for (int64_t r = br * kBlockRows; r < r1; ++r) {
+            if (rrp[r + 1] > rrp[r]) {
+                mn = min(mn, rcol[rrp[r]]);
+                mx = max(mx, rcol[rrp[r + 1] - 1]);
+            }
+        }
     }
-    out[br] = m;
+    lo[br] = mn;
+    hi[br] = mx;
 }
 
 }  // namespace
 
 void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+void block_row_col_bounds(const cove_plan* P, std::vector<int32_t>* lo, std::vector<int32_t>* hi) {
+    lo->assign(static_cast<size_t>(P->nbr), 0);
+    hi->assign(static_cast<size_t>(P->nbr), -1);
+    if (P->nbr == 0) return;
+    DevBuf dlo, dhi;
+    alloc_n<int32_t>(dlo, P->nbr);
+    alloc_n<int32_t>(dhi, P->nbr);
+    const KernelShape k = P->shape();
+    block_row_col_bounds_kernel<<<grid_for(P->nbr, kThreads), kThreads>>>(
+        P->nbr, P->rows, P->cols, k.kept_brp, k.words, k.res_rp, k.res_col, dlo.as<int32_t>(),
+        dhi.as<int32_t>());
+    CUDA_LAUNCH_OK();
+    CUDA_OK(cudaMemcpy(lo->data(), dlo.p, lo->size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
+    CUDA_OK(cudaMemcpy(hi->data(), dhi.p, hi->size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
+}
 
 HostPipeline::~HostPipeline() {
     for (cudaEvent_t e : x_ready) cudaEventDestroy(e);
@@ -116,16 +140,8 @@ std::unique_ptr<HostPipeline> build_host_pipeline(const cove_plan* P) {
     for (int j = 0; j <= hp->ky; ++j)
         hp->br_cut[j] = static_cast<int32_t>(static_cast<int64_t>(P->nbr) * j / hp->ky);
     // the last x slice each block-row slice reads
-    std::vector<int32_t> mc(static_cast<size_t>(P->nbr));
-    if (P->nbr > 0) {
-        DevBuf d;
-        alloc_n<int32_t>(d, P->nbr);
-        const KernelShape k = P->shape();
-        block_row_max_col_kernel<<<grid_for(P->nbr, kThreads), kThreads>>>(
-            P->nbr, P->rows, P->cols, k.kept_brp, k.words, k.res_rp, k.res_col, d.as<int32_t>());
-        CUDA_LAUNCH_OK();
-        CUDA_OK(cudaMemcpy(mc.data(), d.p, mc.size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
-    }
+    std::vector<int32_t> lo, mc;
+    block_row_col_bounds(P, &lo, &mc);
     hp->need.assign(hp->ky, -1);
     int run = -1;
     for (int j = 0; j < hp->ky; ++j) {

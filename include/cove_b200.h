@@ -423,11 +423,14 @@ COVE_API int32_t cove_dist_halo_plan(int32_t rank, int32_t world, const int64_t*
 /* Halo exchange of a window vector (device, window_len T) over NCCL. */
 COVE_API cove_status cove_dist_halo(cove_dist* d, void* x_window, void* stream);
 
-/* Distributed CG over the partition; b and x are the local row blocks. */
+/* Distributed CG over the partition; b and x are the local row blocks.
+ * result->ms_spmv times the distributed SpMV (halo exchange included). */
 COVE_API cove_status cove_dist_cg_solve(cove_dist* d, const void* b_local, void* x_local, int32_t iters,
                                cove_cg_result* result, void* stream);
 
-/* Distributed SpMV: halo exchange of x_window then y_local = A_local x_window. */
+/* Distributed SpMV: y_local = A_local x_window after the halo exchange of
+ * x_window.  The exchange runs on a second stream while the block rows that
+ * read only the rank's own columns are computed; the others follow it. */
 COVE_API cove_status cove_dist_spmv(cove_dist* d, void* x_window, void* y_local, void* stream);
 
 #ifdef __cplusplus
