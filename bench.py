@@ -304,6 +304,7 @@ def run_fem(args):
         if i >= args.warmup:
             e2e_ms.append((time.perf_counter() - t0) * 1e3)
 
+    e2e_median = float(np.median(e2e_ms))
     tot = torch.tensor([ms, float(np.mean(e2e_ms)), float(nnz_local), rel, wall],
                        dtype=torch.float64, device=dev)
     if world > 1:
@@ -353,6 +354,7 @@ def run_fem(args):
                        "l2": "flushed between steps (256 MiB write, outside the timed events)",
                        "parallelism": f"row-block z-slabs x{world}, NCCL halo" if world > 1 else "1 GPU",
                        "plan_build_s": round(build_s, 3), "kernel_slots": info.kernel_slots,
+                       "e2e_ms_mean": round(e2e_all, 4), "e2e_ms_median_rank0": round(e2e_median, 4),
                        "parity_rel_vs_cpu": rel_all},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
