@@ -240,6 +240,46 @@ def test_routes_spmv_and_gate(ref_cases, codec):
             assert p.info.dispatched_route == want
 
 
+@pytest.mark.parametrize("codec", ["auto", "bfp8", "bfp8_outlier"])
+def test_blocksparse_outlier_config_scaled(codec):
+    """Config 4's matrix family at n = 2^16 (same block / entry densities,
+    bf16-representable values in [-8, 8] with 0.1 % outliers of 1e5-1e6):
+    position and value streams bit-exact, route choice and gate as the
+    oracle decides them, and the dispatched SpMV within its route's bound."""
+    rows, cols, rp, ci, v = cb.synth_blocksparse(1 << 16)
+    assert np.abs(v).max() >= 1e5  # the outliers are there
+    p = plan_for(rows, cols, rp, ci, v, value_codec=codec, long_row_split=256)
+    s = O.split(rows, cols, rp, ci, v)
+    assert_streams_equal_split(p, s, v.dtype)
+    if codec == "auto":  # only auto and dict intern the values (the reference's menu)
+        assert p.info.value_cardinality == -1 or p.info.value_cardinality > 256
+    want_joint = cb.ROUTE_BFP8_OUTLIER if codec == "bfp8_outlier" else cb.ROUTE_BFP8
+    assert p.info.joint_route == want_joint
+    if codec == "bfp8_outlier":
+        q, sc, orow, ocol, oval, _ = O.bfp8_outlier_encode(s.kept, 0.005)
+        assert np.array_equal(p.stream("outlier_rows"), orow)
+        assert np.array_equal(p.stream("outlier_cols"), ocol)
+        assert np.array_equal(p.stream("outlier_vals"), oval)
+    else:
+        q, sc = O.bfp8_encode(s.kept)
+    assert np.array_equal(p.stream("bfp8_int8"), q)
+    assert np.array_equal(p.stream("bfp8_scale"), sc)
+    # gate on the canonical x, as the reference evaluates it
+    xc = O.canonical_x(cols)
+    y0 = O.spmv_csr(rows, rp, ci, v, xc)
+    ye = _joint_oracle(rows, cols, rp, ci, v, xc, 0.005 if codec == "bfp8_outlier" else None)
+    rel = O.compare_vectors(y0, ye)[2]
+    assert abs(p.info.joint_rel_err - rel) <= 1e-5 + 1e-3 * rel
+    assert p.info.gate_pass == (rel <= 1e-2)
+    assert p.info.dispatched_route == (want_joint if p.info.gate_pass else cb.ROUTE_HYBRID)
+    # the dispatched route on the config's own x (N(0,1), seed 3)
+    x = cb.synth_vector("normal", cols, seed=3)
+    y = gpu_spmv(p, x)
+    ref = O.spmv_csr(rows, rp, ci, v, x)
+    bound = 1e-12 if p.info.dispatched_route == cb.ROUTE_HYBRID else 1e-2
+    assert O.compare_vectors(ref, y)[2] <= bound
+
+
 def test_auto_route_choice_matches_reference_rule():
     # uniq <= 256 -> dict_u8; > 256 -> bfp8 (main_gpu_csr_bitbsr_spmv.cu:1244-1245)
     rows, cols, rp, ci, v = cb.synth_lapl2d(64, 64)
