@@ -275,13 +275,13 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
     if constexpr (kPrefetch) {
         if (rq < re) sum += val0 * dec.xv(x, col0);
         if (rq + SLOTS < re) sum += val1 * dec.xv(x, col1);
-#pragma unroll 2
+#pragma unroll 4
         for (int q = rq + 2 * SLOTS; q < re; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
     } else if (row < k.rows && k.res_rp != nullptr) {
         const int rs = k.res_rp[row];
         const int re_ = k.res_rp[row + 1];
         if (!(k.long_tau > 0 && re_ - rs > k.long_tau)) {
-#pragma unroll 2
+#pragma unroll 4
             for (int q = rs + s; q < re_; q += SLOTS) sum += dec.res_val(q) * dec.xv(x, rc[q]);
         }
     }
