@@ -282,7 +282,7 @@ def run_fem(args):
     clocks = clk.stop()
     step_ms = [a.elapsed_time(b) for a, b in ev]
     ms = sum(step_ms) / len(step_ms)
-    launches = plan.launches(route)
+    launches = plan.launches(route) if D is None else cb.lib().cove_dist_spmv_launches(D)
 
     # end to end through the public C ABI with host buffers (pinned)
     xh = torch.from_numpy(x_window).pin_memory()

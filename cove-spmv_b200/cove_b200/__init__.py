@@ -121,7 +121,7 @@ EXPORTED = [
     "cove_spmv_launches", "cove_plan_device_error", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
     "cove_cg_solve_noalloc",
     "cove_dist_halo_plan", "cove_dist_id_bytes", "cove_dist_make_id", "cove_dist_create", "cove_dist_destroy",
-    "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv",
+    "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv", "cove_dist_spmv_launches",
     "cove_rng_u64", "cove_rng_uniform01", "cove_synth_lapl2d", "cove_synth_lapl3d",
     "cove_synth_fem27", "cove_synth_fem27_rows", "cove_synth_rmat", "cove_synth_blocksparse", "cove_synth_vector",
     "cove_synth_lapl3d_device", "cove_synth_vector_device",
@@ -183,6 +183,8 @@ def _setup(L):
     L.cove_dist_halo.argtypes = [vp, vp, vp]
     L.cove_dist_cg_solve.argtypes = [vp, vp, vp, i32, C.POINTER(CgResult), vp]
     L.cove_dist_spmv.argtypes = [vp, vp, vp, vp]
+    L.cove_dist_spmv_launches.restype = i32
+    L.cove_dist_spmv_launches.argtypes = [vp]
     L.cove_rng_u64.restype = u64
     L.cove_rng_u64.argtypes = [u64, u64, u64]
     L.cove_rng_uniform01.restype = f64

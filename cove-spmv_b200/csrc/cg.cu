@@ -602,6 +602,24 @@ cove_status cove_dist_spmv(cove_dist* d, void* x_window, void* y_local, void* st
     });
 }
 
+int32_t cove_dist_spmv_launches(const cove_dist* d) {
+    if (!d) return -1;
+    int32_t n = 0;
+    for (size_t i = 0; i < d->plans.size(); ++i) {
+        const cove_plan* P = d->plans[i];
+        const KernelShape k = P->shape();
+        const RouteValues rv = P->route_values(P->dispatched_route);
+        const int full = hybrid_spmv_launch_count(k, rv);
+        if (!d->overlap) {
+            n += full;
+            continue;
+        }
+        for (const auto& r : d->ranges[i]) n += r.b1 > r.b0 ? 1 : 0;  // main pass per range
+        n += full - (k.nbr > 0 ? 1 : 0);                              // the overflow pass
+    }
+    return n;
+}
+
 cove_status cove_dist_cg_solve(cove_dist* d, const void* b_local, void* x_local, int32_t iters,
                                cove_cg_result* result, void* stream) {
     return guarded([&] {

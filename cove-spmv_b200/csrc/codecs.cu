@@ -173,13 +173,21 @@ __global__ void dict_insert_kernel(int64_t nk, int64_t n, const T* __restrict__ 
                                    unsigned int* __restrict__ count,
                                    volatile int* __restrict__ overflow) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= n || *overflow) return;
-    const uint64_t key = value_key(i < nk ? kept[i] : res[i - nk]);
+    const bool valid = i < n && !*overflow;
+    const uint64_t key = valid ? value_key(i < nk ? kept[i] : res[i - nk]) : 0ULL;
+    // Matrices with few distinct values would funnel every thread into the
+    // same slots: lanes holding equal keys elect their lowest lane, which
+    // also holds the group's smallest index, and only it touches the table.
+    const unsigned act = __ballot_sync(0xffffffffu, valid);
+    if (!valid) return;
+    const unsigned peers = __match_any_sync(act, static_cast<unsigned long long>(key));
+    if (static_cast<int>(threadIdx.x & 31) != __ffs(peers) - 1) return;
+    const unsigned int idx = static_cast<unsigned int>(i);
     uint64_t h = mix64(key) & (kTableSize - 1);
     for (uint64_t probe = 0; probe < kTableSize; ++probe) {
         const unsigned long long cur = keys[h];
         if (cur == key) {
-            atomicMin(&first[h], static_cast<unsigned int>(i));
+            if (first[h] > idx) atomicMin(&first[h], idx);  // a stale read only costs an atomic
             return;
         }
         if (cur == 0ULL) {
@@ -187,11 +195,11 @@ __global__ void dict_insert_kernel(int64_t nk, int64_t n, const T* __restrict__ 
             if (prev == 0ULL) {
                 const unsigned int c = atomicAdd(count, 1u);
                 if (c >= kDictLimit) *overflow = 1;
-                atomicMin(&first[h], static_cast<unsigned int>(i));
+                atomicMin(&first[h], idx);
                 return;
             }
             if (prev == key) {
-                atomicMin(&first[h], static_cast<unsigned int>(i));
+                if (first[h] > idx) atomicMin(&first[h], idx);
                 return;
             }
         }

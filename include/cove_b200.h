@@ -433,6 +433,9 @@ COVE_API cove_status cove_dist_cg_solve(cove_dist* d, const void* b_local, void*
  * read only the rank's own columns are computed; the others follow it. */
 COVE_API cove_status cove_dist_spmv(cove_dist* d, void* x_window, void* y_local, void* stream);
 
+/* Kernel launches of this library in one cove_dist_spmv (NCCL's excluded). */
+COVE_API int32_t cove_dist_spmv_launches(const cove_dist* d);
+
 #ifdef __cplusplus
 }
 #endif
