@@ -30,7 +30,7 @@
 namespace cove {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 128;  // measured best for the main passes (64-512 tried)
 
 __device__ __forceinline__ float bf16_to_float(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
