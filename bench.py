@@ -305,6 +305,19 @@ def run_fem(args):
             e2e_ms.append((time.perf_counter() - t0) * 1e3)
 
     e2e_median = float(np.median(e2e_ms))
+    # the host link on its own: plain pinned copies of the same x and y bytes
+    copy_ms = {}
+    for name, dst, src in (("h2d", xd2, xh), ("d2h", yh_t, y)):
+        for _ in range(3):
+            dst.copy_(src, non_blocking=True)
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for _ in range(10):
+            dst.copy_(src, non_blocking=True)
+        c1.record()
+        torch.cuda.synchronize()
+        copy_ms[name] = c0.elapsed_time(c1) / 10
     tot = torch.tensor([ms, float(np.mean(e2e_ms)), float(nnz_local), rel, wall],
                        dtype=torch.float64, device=dev)
     if world > 1:
@@ -355,6 +368,7 @@ def run_fem(args):
                        "parallelism": f"row-block z-slabs x{world}, NCCL halo" if world > 1 else "1 GPU",
                        "plan_build_s": round(build_s, 3), "kernel_slots": info.kernel_slots,
                        "e2e_ms_mean": round(e2e_all, 4), "e2e_ms_median_rank0": round(e2e_median, 4),
+                       "host_copy_ms_rank0": {k: round(v, 4) for k, v in copy_ms.items()},
                        "parity_rel_vs_cpu": rel_all},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,

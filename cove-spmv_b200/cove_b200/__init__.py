@@ -111,6 +111,18 @@ class CgResult(C.Structure):
                 ("rs_final", C.c_double), ("ms_total", C.c_double), ("ms_spmv", C.c_double)]
 
 
+class MmMatrix(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("nnz", C.c_int64),
+                ("row_ptr", C.POINTER(C.c_int64)), ("col_idx", C.POINTER(C.c_int32)),
+                ("values", C.c_void_p), ("dtype", C.c_int32), ("field", C.c_int32),
+                ("symmetry", C.c_int32), ("stored_entries", C.c_int64),
+                ("expanded_entries", C.c_int64), ("coalesced_duplicates", C.c_int64)]
+
+
+MM_FIELDS = ("real", "integer", "complex", "pattern")
+MM_SYMMETRIES = ("general", "symmetric", "skew-symmetric", "hermitian")
+
+
 # every symbol include/cove_b200.h and include/cove_synth.h declare
 EXPORTED = [
     "cove_last_error", "cove_status_string", "cove_version", "cove_plan_opts_default",
@@ -119,6 +131,7 @@ EXPORTED = [
     "cove_lb_layout_count", "cove_lb_layout_fill",
     "cove_hybrid_spmv", "cove_spmv", "cove_spmv_route", "cove_spmv_host",
     "cove_spmv_launches", "cove_plan_device_error", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
+    "cove_mm_read", "cove_mm_free",
     "cove_cg_solve_noalloc",
     "cove_dist_halo_plan", "cove_dist_id_bytes", "cove_dist_make_id", "cove_dist_create", "cove_dist_destroy",
     "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv", "cove_dist_spmv_launches",
@@ -172,6 +185,9 @@ def _setup(L):
     L.cove_compare_vectors.argtypes = [vp, vp, i64, i32, vp, vp]
     L.cove_canonical_x.argtypes = [vp, i64, i32, vp]
     L.cove_cg_solve.argtypes = [vp, vp, vp, i32, C.POINTER(CgResult), vp]
+    L.cove_mm_read.argtypes = [C.c_char_p, i32, C.POINTER(MmMatrix)]
+    L.cove_mm_free.restype = None
+    L.cove_mm_free.argtypes = [C.POINTER(MmMatrix)]
     L.cove_cg_solve_noalloc.argtypes = [vp, vp, vp, i32, C.POINTER(CgResult), vp]
     L.cove_dist_halo_plan.restype = i32
     L.cove_dist_halo_plan.argtypes = [i32, i32, vp, vp, i32]
@@ -466,6 +482,24 @@ def synth_blocksparse(n, p_block=2e-3, p_entry=0.6, outlier_fraction=1e-3, seed=
     rp, ci, v = _two_call(lib().cove_synth_blocksparse, n,
                           (n, p_block, p_entry, outlier_fraction, seed), np.float64)
     return n, n, rp, ci, v
+
+
+def read_matrix_market(path, dtype=np.float64):
+    """CSR of a coordinate MatrixMarket file (structural::read_matrix_market_with_info):
+    (rows, cols, row_ptr int64, col_idx int32, values, info dict)."""
+    m = MmMatrix()
+    check(lib().cove_mm_read(os.fsencode(path), F64 if dtype == np.float64 else F32, C.byref(m)))
+    try:
+        rp = np.ctypeslib.as_array(m.row_ptr, (m.rows + 1,)).copy()
+        ci = np.ctypeslib.as_array(m.col_idx, (max(m.nnz, 1),))[: m.nnz].copy()
+        vt = C.c_double if dtype == np.float64 else C.c_float
+        v = np.ctypeslib.as_array(C.cast(m.values, C.POINTER(vt)), (max(m.nnz, 1),))[: m.nnz].copy()
+        info = {"field": MM_FIELDS[m.field], "symmetry": MM_SYMMETRIES[m.symmetry],
+                "stored_entries": m.stored_entries, "expanded_entries": m.expanded_entries,
+                "coalesced_duplicates": m.coalesced_duplicates}
+        return m.rows, m.cols, rp, ci, v.astype(dtype, copy=False), info
+    finally:
+        lib().cove_mm_free(C.byref(m))
 
 
 def synth_vector(kind, n, seed, stream=7, dtype=np.float64):

@@ -339,6 +339,40 @@ COVE_API cove_status cove_compare_vectors(const void* ref, const void* got, int6
 /* Canonical gate input x[i] = T((i % 17) - 8) * T(0.125) (spmv_harness.hpp:32-39). */
 COVE_API cove_status cove_canonical_x(void* x, int64_t n, int32_t dtype, void* stream);
 
+/* ---- MatrixMarket reader (matrix_market.hpp:327-382) ------------------- */
+
+typedef enum { COVE_MM_REAL = 0, COVE_MM_INTEGER = 1, COVE_MM_COMPLEX = 2, COVE_MM_PATTERN = 3 } cove_mm_field;
+typedef enum {
+    COVE_MM_GENERAL = 0, COVE_MM_SYMMETRIC = 1, COVE_MM_SKEW_SYMMETRIC = 2, COVE_MM_HERMITIAN = 3
+} cove_mm_symmetry;
+
+/* A CSR matrix read from a coordinate MatrixMarket file; host arrays owned
+ * by the library (release with cove_mm_free). */
+typedef struct {
+    int32_t rows, cols;
+    int64_t nnz;                   /* after duplicate summation and zero dropping */
+    int64_t* row_ptr;              /* rows + 1 */
+    int32_t* col_idx;              /* nnz, ascending within each row */
+    void* values;                  /* nnz of dtype */
+    int32_t dtype;                 /* cove_dtype */
+    int32_t field;                 /* cove_mm_field */
+    int32_t symmetry;              /* cove_mm_symmetry */
+    int64_t stored_entries;        /* entries declared in the file */
+    int64_t expanded_entries;      /* after symmetric expansion */
+    int64_t coalesced_duplicates;  /* expanded entries minus nnz */
+} cove_mm_matrix;
+
+/*
+ * read_matrix_market_with_info<T> (matrix_market.hpp:327-382): banner check,
+ * comments, 1-based indices, pattern = 1, symmetric / skew-symmetric
+ * expansion, per-row column sort, duplicates summed (in file order), exact
+ * zeros dropped, values parsed as double and cast to the dtype.  Errors
+ * (bad header, index out of range, short file, complex/hermitian) return a
+ * status with the reference's message in cove_last_error().
+ */
+COVE_API cove_status cove_mm_read(const char* path, int32_t dtype, cove_mm_matrix* out);
+COVE_API void cove_mm_free(cove_mm_matrix* m);
+
 /* ---- conjugate gradient (bench_cg_solve.cu:165-197) ------------------ */
 
 typedef struct {

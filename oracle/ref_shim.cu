@@ -17,10 +17,12 @@
 //   build_bfp8_blkscale_value_codec            gpu_value_codecs.cuh:287-317
 //   build_bfp8_outlier_blkscale_value_codec    gpu_value_codecs.cuh:360-461
 //   float_to_bf16_bits                         value_compression.hpp:105-109
+//   read_matrix_market_with_info               matrix_market.hpp:327-382
 #include "structural/convert.hpp"
 #include "structural/csr.hpp"
 #include "structural/csr_bitbsr_split.hpp"
 #include "structural/gpu_value_codecs.cuh"
+#include "structural/matrix_market.hpp"
 #include "structural/spmv.hpp"
 #include "structural/spmv_harness.hpp"
 #include "structural/value_compression.hpp"
@@ -328,5 +330,36 @@ REF_EXPORT void ref_canonical_x(int32_t n, int32_t esz, void* out) {
     } else {
         const auto x = structural::make_input_vector<float>(n);
         std::memcpy(out, x.data(), x.size() * 4);
+    }
+}
+
+// read_matrix_market_with_info<T> on a file.  Call with row_ptr == nullptr
+// for the sizes: returns nnz (or -1 with ref_last_error() set); shape2 =
+// {rows, cols}, field_sym2 = {field, symmetry} as the reference's enums,
+// counts3 = {stored, expanded, coalesced duplicates}.
+REF_EXPORT int64_t ref_mm_read(const char* path, int32_t esz, int32_t* shape2, int32_t* field_sym2,
+                               int64_t* counts3, int32_t* row_ptr, int32_t* col, void* values) {
+    try {
+        auto copy = [&](const auto& r) {
+            shape2[0] = r.matrix.rows;
+            shape2[1] = r.matrix.cols;
+            field_sym2[0] = static_cast<int32_t>(r.info.field);
+            field_sym2[1] = static_cast<int32_t>(r.info.symmetry);
+            counts3[0] = r.stored_entries;
+            counts3[1] = r.expanded_entries;
+            counts3[2] = r.coalesced_duplicates;
+            if (row_ptr) {
+                std::memcpy(row_ptr, r.matrix.row_ptr.data(), r.matrix.row_ptr.size() * 4);
+                std::memcpy(col, r.matrix.col_idx.data(), r.matrix.col_idx.size() * 4);
+                std::memcpy(values, r.matrix.values.data(),
+                            r.matrix.values.size() * sizeof(r.matrix.values[0]));
+            }
+            return static_cast<int64_t>(r.matrix.nnz());
+        };
+        if (esz == 8) return copy(structural::read_matrix_market_with_info<double>(path));
+        return copy(structural::read_matrix_market_with_info<float>(path));
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
     }
 }
