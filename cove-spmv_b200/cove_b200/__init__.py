@@ -130,7 +130,7 @@ EXPORTED = [
     "cove_plan_stream", "cove_bitbsr8x4_count", "cove_bitbsr8x4_fill", "cove_pack_words",
     "cove_lb_layout_count", "cove_lb_layout_fill",
     "cove_hybrid_spmv", "cove_spmv", "cove_spmv_route", "cove_spmv_host",
-    "cove_spmv_launches", "cove_plan_device_error", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
+    "cove_spmv_launches", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
     "cove_mm_read", "cove_mm_free",
     "cove_cg_solve_noalloc",
     "cove_dist_halo_plan", "cove_dist_id_bytes", "cove_dist_make_id", "cove_dist_create", "cove_dist_destroy",
@@ -178,8 +178,6 @@ def _setup(L):
     L.cove_spmv.argtypes = [vp, vp, vp, vp]
     L.cove_spmv_route.argtypes = [vp, i32, vp, vp, vp]
     L.cove_spmv_host.argtypes = [vp, vp, vp, vp]
-    L.cove_plan_device_error.restype = C.c_int
-    L.cove_plan_device_error.argtypes = [vp, C.POINTER(C.c_int32), vp]
     L.cove_spmv_launches.restype = i32
     L.cove_spmv_launches.argtypes = [vp, i32]
     L.cove_compare_vectors.argtypes = [vp, vp, i64, i32, vp, vp]
@@ -380,12 +378,6 @@ class Plan:
         check(lib().cove_spmv_host(self._h, _np_ptr(x_host), _np_ptr(y_host),
                                    _stream_handle(stream)))
         return y_host
-
-    def device_error(self, stream=None) -> int:
-        """Raise if a bounded wait inside an SpMV kernel of this plan gave up."""
-        flag = C.c_int32(0)
-        check(lib().cove_plan_device_error(self._h, C.byref(flag), _stream_handle(stream)))
-        return flag.value
 
     def launches(self, route=None) -> int:
         return int(lib().cove_spmv_launches(self._h, self.info.dispatched_route if route is None

@@ -75,10 +75,9 @@ struct cove_plan {
     bool gate_pass = false;
     double joint_rel = -1.0;
 
-    // staging for cove_spmv_host
+    // host-call staging of x and y (cove_spmv_host)
     cove::DevBuf x_stage, y_stage;
     std::unique_ptr<cove::HostPipeline> pipe;
-    cove::DevBuf err;  // int, set by a kernel whose bounded wait gave up
 
     cove::KernelShape shape() const;
     cove::RouteValues route_values(int route) const;

@@ -37,8 +37,6 @@ struct KernelShape {
     int heavy_limit = 0x7fffffff;         // blocks a block row handles in the main pass
     int long_tau = 0;                     // residual rows longer than this go to chunks
     bool x_vec_ok = false;                // set per launch: x 16-byte aligned, cols % 4 == 0
-    bool stage_ok = false;                // value streams carry tail slack: TMA staging allowed
-    int* err = nullptr;                   // device flag set when a bounded wait gives up
     // overflow tasks (second launch)
     int64_t num_heavy = 0;
     const int32_t* heavy_br = nullptr;

@@ -251,8 +251,6 @@ cove::KernelShape cove_plan::shape() const {
     k.res_rp = sp.res_row_ptr.as<int32_t>();
     k.res_col = sp.res_col.as<int32_t>();
     k.slots = slots;
-    k.stage_ok = true;  // every plan buffer carries DevBuf::kTailSlack
-    k.err = err.as<int>();
     k.heavy_limit = heavy_limit;
     k.long_tau = long_tau;
     k.num_heavy = num_heavy;
@@ -315,8 +313,6 @@ template <typename T>
 void build_plan_typed(cove_plan* P, const cove_csr_desc& d, cudaStream_t s) {
     const cove_plan_opts& o = P->opts;
     validate_csr<T>(d, s);
-    alloc_n<int>(P->err, 1);
-    CUDA_OK(cudaMemsetAsync(P->err.p, 0, sizeof(int), s));
     build_full_bitbsr<T>(d, P->full, s);
     P->nnz = P->full.nnz;
     P->nbr = P->full.nbr;
@@ -569,18 +565,6 @@ const char* cove_route_name(int32_t route) {
         case COVE_ROUTE_BFP8_OUTLIER: return "bfp8_outlier_blocks+bf16_residual";
     }
     return "unknown";
-}
-
-cove_status cove_plan_device_error(const cove_plan* P, int32_t* flag, void* stream) {
-    return guarded([&] {
-        if (!P || !flag) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
-        int h = 0;
-        cudaStream_t s = static_cast<cudaStream_t>(stream);
-        CUDA_OK(cudaMemcpyAsync(&h, P->err.p, sizeof(int), cudaMemcpyDeviceToHost, s));
-        CUDA_OK(cudaStreamSynchronize(s));
-        *flag = h;
-        if (h) COVE_THROW(COVE_ERR_TIMEOUT, "a bounded wait in an SpMV kernel gave up");
-    });
 }
 
 cove_status cove_plan_get_info(const cove_plan* P, cove_plan_info* info) {

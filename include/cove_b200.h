@@ -38,7 +38,7 @@ typedef enum {
     COVE_ERR_OUT_OF_MEMORY = 5,
     COVE_ERR_UNSUPPORTED = 6,      /* block shape other than 8x4, unknown codec, ... */
     COVE_ERR_NCCL = 7,             /* a collective failed or timed out */
-    COVE_ERR_TIMEOUT = 8           /* a bounded device wait gave up */
+    COVE_ERR_TIMEOUT = 8           /* a partition wait (NCCL or stream) passed its deadline */
 } cove_status;
 
 typedef enum { COVE_F64 = 0, COVE_F32 = 1 } cove_dtype;
@@ -316,14 +316,6 @@ COVE_API cove_status cove_spmv_route(const cove_plan* plan, int32_t route, const
  * device staging buffers belong to the plan.
  */
 COVE_API cove_status cove_spmv_host(cove_plan* plan, const void* x_host, void* y_host, void* stream);
-
-/*
- * Device error flag of a plan's kernels (synchronizes `stream`): *flag is
- * non-zero, and the status COVE_ERR_TIMEOUT, when a bounded wait inside an
- * SpMV kernel (the shared-memory staging barrier) gave up; the affected
- * rows of that call's y were not written.
- */
-COVE_API cove_status cove_plan_device_error(const cove_plan* plan, int32_t* flag, void* stream);
 
 /* Number of kernel launches one cove_spmv / cove_spmv_route call makes. */
 COVE_API int32_t cove_spmv_launches(const cove_plan* plan, int32_t route);
