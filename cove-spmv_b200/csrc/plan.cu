@@ -251,6 +251,7 @@ cove::KernelShape cove_plan::shape() const {
     k.res_rp = sp.res_row_ptr.as<int32_t>();
     k.res_col = sp.res_col.as<int32_t>();
     k.slots = slots;
+    k.l2_prefetch = true;  // DevBuf: cudaMalloc alignment and kTailSlack
     k.heavy_limit = heavy_limit;
     k.long_tau = long_tau;
     k.num_heavy = num_heavy;

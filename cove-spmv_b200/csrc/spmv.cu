@@ -66,6 +66,21 @@ __device__ __forceinline__ void load_x4(const T* __restrict__ x, int64_t c4, boo
     for (int c = 0; c < 4; ++c) out[c] = (nib & (1u << c)) ? static_cast<Acc>(__ldg(x + c4 + c)) : Acc(0);
 }
 
+// Hint: start pulling [p, p + bytes) into L2 before the dependent loads ask
+// for it.  The range is widened to 16-byte bounds; plan buffers are
+// 256-byte aligned and carry tail slack, so it stays inside the allocation.
+#ifndef L2PF
+#define L2PF 1
+#endif
+__device__ __forceinline__ void prefetch_l2(const void* p, int64_t bytes) {
+    if (bytes <= 0) return;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uintptr_t lo = a & ~static_cast<uintptr_t>(15);
+    const uintptr_t hi = (a + static_cast<uintptr_t>(bytes) + 15) & ~static_cast<uintptr_t>(15);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"(static_cast<uint32_t>(hi - lo))
+                 : "memory");
+}
+
 // ---- value decoders ------------------------------------------------------------
 // V: element type of the kept value stream; decode(raw, ctx, bit) turns a
 // stored element into the accumulator type (ctx is per block, bit the cell).
@@ -198,6 +213,12 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
     int vb = k.kept_brvp[br];
     const uint64_t* __restrict__ words = k.words;
     const V* __restrict__ kept = dec.kept;
+    if constexpr (L2PF && Dec::kHasKept) {
+        if (k.l2_prefetch && gl == 0) {  // the block row's words and values, in bulk
+            prefetch_l2(words + b0, static_cast<int64_t>(b1 - b0) * 8);
+            prefetch_l2(kept + vb, static_cast<int64_t>(k.kept_brvp[br + 1] - vb) * sizeof(V));
+        }
+    }
     const bool vec_x = k.x_vec_ok;
     const uint32_t lowmask = (1u << (4 * r)) - 1u;
     Acc sum = Acc(0);
