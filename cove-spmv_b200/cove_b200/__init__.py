@@ -20,6 +20,9 @@ LIB_PATH = os.path.join(_HERE, "libcove_b200.so")
 F64, F32 = 0, 1
 CODEC = {"original": 0, "auto": 1, "dict": 2, "bfp8": 3, "bfp8_outlier": 4}
 ROUTE_HYBRID, ROUTE_DICT_U8, ROUTE_DICT_U16, ROUTE_BFP8, ROUTE_BFP8_OUTLIER = range(5)
+# value codecs of the BitBSR-only family runner (cove_hybrid_spmv)
+(ROUTE_TILE_CODE, ROUTE_BF16_NNZ, ROUTE_IMPLICIT_ONE, ROUTE_CONST_C, ROUTE_SIGN2,
+ ROUTE_FP16_NNZ, ROUTE_BFP4) = range(5, 12)
 ROUTE_NAMES = {0: "original", 1: "dict_u8_lossless", 2: "dict_u16_lossless",
                3: "bfp8_blocks+bf16_residual", 4: "bfp8_outlier_blocks+bf16_residual"}
 ROUTE_NAMES_INV = {v: k for k, v in ROUTE_NAMES.items()}
@@ -103,7 +106,7 @@ class ValuesDesc(C.Structure):
                 ("codebook_size", C.c_int64), ("num_outliers", C.c_int64),
                 ("outlier_rows", C.c_void_p), ("outlier_cols", C.c_void_p),
                 ("outlier_vals", C.c_void_p), ("tile_code_words", C.c_void_p),
-                ("tile_bits", C.c_int32)]
+                ("tile_bits", C.c_int32), ("value_scale", C.c_double), ("sign_masks", C.c_void_p)]
 
 
 class CgResult(C.Structure):

@@ -19,6 +19,8 @@ struct RouteValues {
     const void* out_vals = nullptr;    // T
     const void* tile_words = nullptr;  // family tile codes: Bits u32 words per block
     int tile_bits = 0;
+    double value_scale = 1.0;          // const_c constant, sign2 scale
+    const uint32_t* sign_masks = nullptr;  // sign2: one word per kept block
 };
 
 // Position streams and the kernel's own work split.

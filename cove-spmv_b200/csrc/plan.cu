@@ -564,6 +564,13 @@ const char* cove_route_name(int32_t route) {
         case COVE_ROUTE_DICT_U16: return "dict_u16_lossless";
         case COVE_ROUTE_BFP8: return "bfp8_blocks+bf16_residual";
         case COVE_ROUTE_BFP8_OUTLIER: return "bfp8_outlier_blocks+bf16_residual";
+        case COVE_ROUTE_TILE_CODE: return "tile_code";
+        case COVE_ROUTE_BF16_NNZ: return "bf16_nnz";
+        case COVE_ROUTE_IMPLICIT_ONE: return "implicit_one";
+        case COVE_ROUTE_CONST_C: return "const_c";
+        case COVE_ROUTE_SIGN2: return "sign2";
+        case COVE_ROUTE_FP16_NNZ: return "fp16_nnz";
+        case COVE_ROUTE_BFP4: return "bfp4";
     }
     return "unknown";
 }
@@ -788,8 +795,22 @@ cove_status cove_hybrid_spmv(const cove_hybrid_desc* a, const cove_values_desc* 
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "fused CSR+BitBSR shape mismatch");
         }
         if (a->dtype != COVE_F64 && a->dtype != COVE_F32) COVE_THROW(COVE_ERR_UNSUPPORTED, "dtype");
-        if (v->route < COVE_ROUTE_HYBRID || v->route > COVE_ROUTE_BF16_NNZ) {
+        if (v->route < COVE_ROUTE_HYBRID || v->route > COVE_ROUTE_BFP4) {
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "unknown route");
+        }
+        const bool bitbsr_only = v->route >= COVE_ROUTE_IMPLICIT_ONE;
+        if (bitbsr_only && (a->residual_nnz > 0 || a->num_chunks > 0)) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT,
+                       std::string(cove_route_name(v->route)) + " is a BitBSR-only value codec: no residual");
+        }
+        if (v->route == COVE_ROUTE_SIGN2 && a->kept_blocks > 0 && !v->sign_masks) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "sign2 route needs sign_masks");
+        }
+        if ((v->route == COVE_ROUTE_FP16_NNZ || v->route == COVE_ROUTE_BFP4) && a->kept_nnz > 0 && !v->kept) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "per-nnz value stream missing");
+        }
+        if (v->route == COVE_ROUTE_BFP4 && a->kept_blocks > 0 && !v->block_scale) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "bfp4 route needs block_scale");
         }
         if (a->rows > 0 && (!a->block_row_ptr || !a->block_row_val_ptr || !y)) {
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null stream");
@@ -805,8 +826,8 @@ cove_status cove_hybrid_spmv(const cove_hybrid_desc* a, const cove_values_desc* 
         k.kept_brp = a->block_row_ptr;
         k.kept_brvp = a->block_row_val_ptr;
         k.words = a->words;
-        k.res_rp = a->res_row_ptr;
-        k.res_col = a->res_col_idx;
+        k.res_rp = bitbsr_only ? nullptr : a->res_row_ptr;
+        k.res_col = bitbsr_only ? nullptr : a->res_col_idx;
         // the caller's layout has no heavy-row split: keep the group kernel
         k.slots = std::max(1, choose_slots(a->num_block_rows, a->kept_blocks, a->rows, a->residual_nnz));
         k.long_tau = a->num_chunks > 0 ? a->long_row_tau : 0;
@@ -829,6 +850,8 @@ cove_status cove_hybrid_spmv(const cove_hybrid_desc* a, const cove_values_desc* 
         }
         rv.tile_words = v->tile_code_words;
         rv.tile_bits = v->tile_bits;
+        rv.value_scale = v->value_scale;
+        rv.sign_masks = v->sign_masks;
         if (v->route == COVE_ROUTE_TILE_CODE && !v->tile_code_words) {
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "tile-code route needs tile_code_words");
         }

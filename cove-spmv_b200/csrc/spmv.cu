@@ -25,6 +25,8 @@
 // kernel does (:795, :811).
 #include "cove_spmv.cuh"
 
+#include <cuda_fp16.h>
+
 #include <algorithm>
 
 namespace cove {
@@ -95,6 +97,10 @@ struct RawDec {
     const T* __restrict__ kept;
     const T* __restrict__ res;
     __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ V load(int64_t p) const { return kept[p]; }
+    __device__ __forceinline__ void prefetch_values(int64_t a, int64_t b) const {
+        prefetch_l2(kept + a, (b - a) * static_cast<int64_t>(sizeof(V)));
+    }
     __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
     __device__ __forceinline__ Acc decode(V raw, Acc, int) const { return static_cast<Acc>(raw); }
     __device__ __forceinline__ Acc res_val(int64_t p) const { return static_cast<Acc>(res[p]); }
@@ -120,6 +126,10 @@ struct DictDec {
             cb = codebook;
         }
     }
+    __device__ __forceinline__ V load(int64_t p) const { return kept[p]; }
+    __device__ __forceinline__ void prefetch_values(int64_t a, int64_t b) const {
+        prefetch_l2(kept + a, (b - a) * static_cast<int64_t>(sizeof(V)));
+    }
     __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
     __device__ __forceinline__ Acc decode(V raw, Acc, int) const { return static_cast<Acc>(cb[raw]); }
     __device__ __forceinline__ Acc res_val(int64_t p) const { return static_cast<Acc>(cb[res[p]]); }
@@ -135,6 +145,10 @@ struct Bfp8Dec {
     const uint16_t* __restrict__ res;
     const uint16_t* __restrict__ scale;
     __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ V load(int64_t p) const { return kept[p]; }
+    __device__ __forceinline__ void prefetch_values(int64_t a, int64_t b) const {
+        prefetch_l2(kept + a, (b - a) * static_cast<int64_t>(sizeof(V)));
+    }
     __device__ __forceinline__ float block_ctx(int64_t b) const { return bf16_to_float(scale[b]); }
     __device__ __forceinline__ float decode(V raw, float sc, int) const {
         return static_cast<float>(raw) * sc;
@@ -161,6 +175,7 @@ struct TileDec {
     const T* __restrict__ res;
     const uint8_t* kept = nullptr;
     __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ V load(int64_t) const { return V{}; }
     __device__ __forceinline__ Acc block_ctx(int64_t b) const { return static_cast<Acc>(b); }
     __device__ __forceinline__ Acc decode(V, Acc blk, int bit) const {
         const int64_t b = static_cast<int64_t>(blk);
@@ -180,11 +195,100 @@ struct Bf16NnzDec {
     const uint16_t* __restrict__ kept;
     const uint16_t* __restrict__ res;
     __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ V load(int64_t p) const { return kept[p]; }
+    __device__ __forceinline__ void prefetch_values(int64_t a, int64_t b) const {
+        prefetch_l2(kept + a, (b - a) * static_cast<int64_t>(sizeof(V)));
+    }
     __device__ __forceinline__ float block_ctx(int64_t) const { return 1.0f; }
     __device__ __forceinline__ float decode(V raw, float, int) const { return bf16_to_float(raw); }
     __device__ __forceinline__ float res_val(int64_t p) const { return bf16_to_float(res[p]); }
     __device__ __forceinline__ float xv(const T* __restrict__ x, int64_t c) const {
         return static_cast<float>(x[c]);
+    }
+};
+
+// ---- family value codecs without a per-nnz value stream ---------------------------
+// (BitBSR-only routes, as the reference's family runner; no residual)
+
+// Every stored value is one constant: 1 (implicit_one) or C (const_c),
+// lossless, T-exact accumulation (bitbsr_spmv_8x4_lossless.cuh).
+template <typename T>
+struct ConstDec {
+    using Acc = double;
+    using V = uint8_t;
+    static constexpr bool kHasKept = false;
+    double c;
+    __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ V load(int64_t) const { return V{}; }
+    __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
+    __device__ __forceinline__ Acc decode(V, Acc, int) const { return c; }
+    __device__ __forceinline__ Acc res_val(int64_t) const { return Acc(0); }
+    __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t col) const { return static_cast<Acc>(x[col]); }
+};
+
+// Sign masks, one 32-bit word per block: cell bit set -> +scale, clear ->
+// -scale (decode_sign_tile32_value, common.cuh:119-125; sign2 has scale 1).
+template <typename T>
+struct SignDec {
+    using Acc = double;
+    using V = uint8_t;
+    static constexpr bool kHasKept = false;
+    const uint32_t* __restrict__ masks;
+    double scale;
+    __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ V load(int64_t) const { return V{}; }
+    __device__ __forceinline__ Acc block_ctx(int64_t b) const { return static_cast<Acc>(b); }
+    __device__ __forceinline__ Acc decode(V, Acc blk, int bit) const {
+        return ((__ldg(masks + static_cast<int64_t>(blk)) >> bit) & 1u) ? scale : -scale;
+    }
+    __device__ __forceinline__ Acc res_val(int64_t) const { return Acc(0); }
+    __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t col) const { return static_cast<Acc>(x[col]); }
+};
+
+// Per-nnz fp16 bits, fp32 accumulation (round16_nnz with fp16, common.cuh:626-687).
+template <typename T>
+struct Fp16NnzDec {
+    using Acc = float;
+    using V = uint16_t;
+    static constexpr bool kHasKept = true;
+    const uint16_t* __restrict__ kept;
+    __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ V load(int64_t p) const { return kept[p]; }
+    __device__ __forceinline__ void prefetch_values(int64_t a, int64_t b) const {
+        prefetch_l2(kept + a, (b - a) * 2);
+    }
+    __device__ __forceinline__ float block_ctx(int64_t) const { return 1.0f; }
+    __device__ __forceinline__ float decode(V raw, float, int) const { return __half2float(__ushort_as_half(raw)); }
+    __device__ __forceinline__ float res_val(int64_t) const { return 0.0f; }
+    __device__ __forceinline__ float xv(const T* __restrict__ x, int64_t col) const {
+        return static_cast<float>(x[col]);
+    }
+};
+
+// BFP4: signed 4-bit mantissa (two's complement, [-7, 7]) at the nibble
+// (p & 1) of byte p/2 of the linear nnz position p, times the block's bf16
+// scale, fp32 accumulation (decode_bfp4_nibble, common.cuh:780-835).
+template <typename T>
+struct Bfp4Dec {
+    using Acc = float;
+    using V = int;
+    static constexpr bool kHasKept = true;
+    const uint8_t* __restrict__ packed;
+    const uint16_t* __restrict__ scale;
+    __device__ __forceinline__ void prepare(void*) {}
+    __device__ __forceinline__ V load(int64_t p) const {
+        const uint8_t byte = packed[p >> 1];
+        const int nib = (p & 1) ? (byte >> 4) : (byte & 0xF);
+        return (nib ^ 0x8) - 0x8;
+    }
+    __device__ __forceinline__ void prefetch_values(int64_t a, int64_t b) const {
+        prefetch_l2(packed + (a >> 1), ((b + 1) >> 1) - (a >> 1));
+    }
+    __device__ __forceinline__ float block_ctx(int64_t b) const { return bf16_to_float(scale[b]); }
+    __device__ __forceinline__ float decode(V raw, float sc, int) const { return static_cast<float>(raw) * sc; }
+    __device__ __forceinline__ float res_val(int64_t) const { return 0.0f; }
+    __device__ __forceinline__ float xv(const T* __restrict__ x, int64_t col) const {
+        return static_cast<float>(x[col]);
     }
 };
 
@@ -212,11 +316,10 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
     if (b1 - b0 > k.heavy_limit) b1 = b0 + k.heavy_limit;
     int vb = k.kept_brvp[br];
     const uint64_t* __restrict__ words = k.words;
-    const V* __restrict__ kept = dec.kept;
     if constexpr (L2PF && Dec::kHasKept) {
         if (k.l2_prefetch && gl == 0) {  // the block row's words and values, in bulk
             prefetch_l2(words + b0, static_cast<int64_t>(b1 - b0) * 8);
-            prefetch_l2(kept + vb, static_cast<int64_t>(k.kept_brvp[br + 1] - vb) * sizeof(V));
+            dec.prefetch_values(vb, k.kept_brvp[br + 1]);
         }
     }
     const bool vec_x = k.x_vec_ok;
@@ -281,7 +384,7 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
                 for (int c = 0; c < 4; ++c) {
                     if (nib & (1u << c)) {
                         V raw{};
-                        if constexpr (Dec::kHasKept) raw = kept[v0];
+                        if constexpr (Dec::kHasKept) raw = dec.load(v0);
                         sum += dec.decode(raw, ctx, 4 * r + c) * xs[c];
                         ++v0;
                     }
@@ -346,7 +449,6 @@ hybrid_row_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __re
         if (k.long_tau > 0 && qe - q > k.long_tau) qe = q;  // finished by the overflow pass
     }
     const uint64_t* __restrict__ words = k.words;
-    const V* __restrict__ kept = dec.kept;
     const int32_t* __restrict__ rc = k.res_col;
     const uint32_t lowmask = (1u << (4 * r)) - 1u;
     Acc sum = Acc(0);
@@ -363,7 +465,7 @@ hybrid_row_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __re
             for (int c = 0; c < 4; ++c) {
                 if (nib & (1u << c)) {
                     V raw{};
-                    if constexpr (Dec::kHasKept) raw = kept[v0];
+                    if constexpr (Dec::kHasKept) raw = dec.load(v0);
                     sum += dec.decode(raw, ctx, 4 * r + c) * dec.xv(x, c4 + c);
                     ++v0;
                 }
@@ -424,7 +526,7 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
                 for (int c = 0; c < 4; ++c) {
                     if (nib & (1u << c)) {
                         V raw{};
-                        if constexpr (Dec::kHasKept) raw = dec.kept[v0];
+                        if constexpr (Dec::kHasKept) raw = dec.load(v0);
                         sum += dec.decode(raw, ctx, 4 * r + c) * dec.xv(x, c4 + c);
                         ++v0;
                     }
@@ -542,6 +644,16 @@ int launch_typed(const KernelShape& k, const RouteValues& v, const void* x, void
             Bf16NnzDec<T> d{static_cast<const uint16_t*>(v.kept), static_cast<const uint16_t*>(v.res)};
             return launch_with<T>(k, d, 0, v, x, y, s);
         }
+        case COVE_ROUTE_IMPLICIT_ONE:
+            return launch_with<T>(k, ConstDec<T>{1.0}, 0, v, x, y, s);
+        case COVE_ROUTE_CONST_C:
+            return launch_with<T>(k, ConstDec<T>{v.value_scale}, 0, v, x, y, s);
+        case COVE_ROUTE_SIGN2:
+            return launch_with<T>(k, SignDec<T>{v.sign_masks, v.value_scale}, 0, v, x, y, s);
+        case COVE_ROUTE_FP16_NNZ:
+            return launch_with<T>(k, Fp16NnzDec<T>{static_cast<const uint16_t*>(v.kept)}, 0, v, x, y, s);
+        case COVE_ROUTE_BFP4:
+            return launch_with<T>(k, Bfp4Dec<T>{static_cast<const uint8_t*>(v.kept), v.scale}, 0, v, x, y, s);
         default:
             COVE_THROW(COVE_ERR_UNSUPPORTED, "unknown route");
     }

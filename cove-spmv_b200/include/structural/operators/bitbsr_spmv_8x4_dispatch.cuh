@@ -3,9 +3,12 @@
 // structural/include/structural/operators/bitbsr_spmv_8x4_dispatch.cuh:12-39),
 // BitBsrSpmvPlan8x4 (:83-109) and run_bitbsr_spmv_once (:315-334).
 //
-// Value codecs served: Raw, the exact tile-code dictionaries (Dict2, Unique4,
-// Unique16, Dict256U8, Dict65536U16), Bf16, Bfp8 and Bfp8Outlier.  The other
-// codecs of the enum throw std::runtime_error("unsupported ...").
+// Every value codec of the enum is served by one route of cove_hybrid_spmv:
+// Raw; ImplicitOne and ConstC (a constant); Sign2 and Sign2Scale (sign
+// masks); the tile-code codecs Dict2, Unique4, Unique16, Dict256U8,
+// Dict65536U16, K256U8 and GlobalLogKmeans16..128 (codes + codebook); Fp16
+// and Bf16 (16-bit values per nnz); Bfp8, Bfp8Outlier and Bfp4 (block scale).
+// The payloads are the plan fields the reference's builders fill.
 #pragma once
 
 #include "structural/operators/bitbsr_spmv_8x4_common.cuh"
@@ -99,12 +102,18 @@ cove_hybrid_desc bitbsr_only_desc(const DeviceBitBsrMatrix<T>& device,
 }
 
 inline int tile_bits_of(BitBsrValueCodecKind8x4 c) {
+    using K = BitBsrValueCodecKind8x4;
     switch (c) {
-        case BitBsrValueCodecKind8x4::Dict2: return 1;
-        case BitBsrValueCodecKind8x4::Unique4: return 2;
-        case BitBsrValueCodecKind8x4::Unique16: return 4;
-        case BitBsrValueCodecKind8x4::Dict256U8: return 8;
-        case BitBsrValueCodecKind8x4::Dict65536U16: return 16;
+        case K::Dict2: return 1;
+        case K::Unique4: return 2;
+        case K::Unique16: return 4;
+        case K::Dict256U8: return 8;
+        case K::Dict65536U16: return 16;
+        case K::K256U8:
+        case K::GlobalLogKmeans16:
+        case K::GlobalLogKmeans32:
+        case K::GlobalLogKmeans64:
+        case K::GlobalLogKmeans128: return 8;  // tile256 codes (bitbsr_spmv_8x4_lossy.cuh:59-105)
         default: return 0;
     }
 }
@@ -134,11 +143,48 @@ void run_bitbsr_spmv_once(const DeviceBitBsrMatrix<T>& device, const BitBsrSpmvP
             v.route = COVE_ROUTE_HYBRID;
             v.kept = gpu_detail::raw(device.values);
             break;
+        case K::ImplicitOne:
+            v.route = COVE_ROUTE_IMPLICIT_ONE;
+            break;
+        case K::ConstC:
+            v.route = COVE_ROUTE_CONST_C;
+            v.value_scale = static_cast<double>(plan.value_scale);
+            break;
+        case K::Sign2:
+        case K::Sign2Scale:
+            v.route = COVE_ROUTE_SIGN2;
+            v.value_scale = plan.value_codec == K::Sign2 ? 1.0 : static_cast<double>(plan.value_scale);
+            v.sign_masks = gpu_detail::raw(plan.sign_masks);
+            if (static_cast<Offset>(plan.sign_masks.size()) != device.num_blocks) {
+                throw std::runtime_error("GPU BitBSR sign tile mask count mismatch");
+            }
+            break;
+        case K::Fp16:
+            v.route = COVE_ROUTE_FP16_NNZ;
+            v.kept = gpu_detail::raw(plan.values16);
+            if (static_cast<Offset>(plan.values16.size()) != device.nnz) {
+                throw std::runtime_error("GPU BitBSR round16 nnz value count mismatch");
+            }
+            break;
+        case K::Bfp4:
+            v.route = COVE_ROUTE_BFP4;
+            v.kept = gpu_detail::raw(plan.packed_int4);
+            v.block_scale = gpu_detail::raw(plan.block_scale_bf16);
+            if (static_cast<Offset>(plan.packed_int4.size()) != (device.nnz + 1) / 2 ||
+                static_cast<Offset>(plan.block_scale_bf16.size()) != device.num_blocks) {
+                throw std::runtime_error("GPU BitBSR bfp4 payload size mismatch");
+            }
+            break;
         case K::Dict2:
         case K::Unique4:
         case K::Unique16:
         case K::Dict256U8:
         case K::Dict65536U16:
+        case K::K256U8:
+        case K::GlobalLogKmeans16:
+        case K::GlobalLogKmeans32:
+        case K::GlobalLogKmeans64:
+        case K::GlobalLogKmeans128:
             v.route = COVE_ROUTE_TILE_CODE;
             v.tile_bits = gpu_detail::tile_bits_of(plan.value_codec);
             v.tile_code_words = gpu_detail::raw(plan.tile_code_words);

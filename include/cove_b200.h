@@ -60,8 +60,14 @@ typedef enum {
     COVE_ROUTE_BFP8 = 3,          /* "bfp8_blocks+bf16_residual" */
     COVE_ROUTE_BFP8_OUTLIER = 4,  /* "bfp8_outlier_blocks+bf16_residual" */
     /* BitBSR-only value codecs of the family runner, cove_hybrid_spmv only: */
-    COVE_ROUTE_TILE_CODE = 5,     /* exact dict, per-cell tile codes (common.cuh:270-319) */
-    COVE_ROUTE_BF16_NNZ = 6       /* per-nnz bf16 values (common.cuh:632-687) */
+    COVE_ROUTE_TILE_CODE = 5,     /* per-cell tile codes + codebook: dict2, unique4/16, dict256,
+                                     dict65536, k256, log-k-means (common.cuh:270-319) */
+    COVE_ROUTE_BF16_NNZ = 6,      /* per-nnz bf16 values (common.cuh:632-687) */
+    COVE_ROUTE_IMPLICIT_ONE = 7,  /* every value 1 (bitbsr_spmv_8x4_lossless.cuh:10-105) */
+    COVE_ROUTE_CONST_C = 8,       /* every value value_scale */
+    COVE_ROUTE_SIGN2 = 9,         /* +-value_scale by sign_masks (common.cuh:119-125) */
+    COVE_ROUTE_FP16_NNZ = 10,     /* per-nnz fp16 values, fp32 accumulate (common.cuh:626-687) */
+    COVE_ROUTE_BFP4 = 11          /* packed int4 x per-block bf16 scale (common.cuh:780-835) */
 } cove_route;
 
 /* Split policy (main_gpu_csr_bitbsr_spmv.cu:35, :1087-1093). */
@@ -296,7 +302,13 @@ typedef struct {
     const void* outlier_vals;
     const uint32_t* tile_code_words;  /* tile-code route: tile_bits words per kept block */
     int32_t tile_bits;                /* 1, 2, 4, 8 or 16 */
+    double value_scale;               /* const_c: the constant; sign2: the scale (1 for +-1) */
+    const uint32_t* sign_masks;       /* sign2: one word per kept block, bit = cell, set = + */
 } cove_values_desc;
+/* Routes 7-11 are BitBSR-only value codecs of the family runner: the
+ * hybrid descriptor must carry no residual.  fp16: kept = uint16 bits per
+ * nnz; bfp4: kept = (nnz + 1) / 2 bytes of nibbles, block_scale = bf16 bits
+ * per kept block. */
 
 /*
  * y = A x over caller-owned streams.  Replaces the four launchers of

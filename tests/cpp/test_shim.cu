@@ -6,8 +6,12 @@
 // Built and run by tests/test_gpu_shim.py (needs a GPU).
 #include "structural/csr_bitbsr_hybrid.cuh"
 
+#include <cuda_fp16.h>
+
+#include <algorithm>
 #include <cassert>
 #include <cmath>
+#include <cstring>
 #include <cstdio>
 #include <map>
 #include <vector>
@@ -123,14 +127,145 @@ void test_bitbsr_only_operators() {
     structural::run_bitbsr_spmv_once(dev, plan, dx, dy);
     close(expected, host(dy), 1e-12);
 
+    // k256 / log-k-means are 8-bit code tiles over a 256-entry codebook
     plan.value_codec = structural::BitBsrValueCodecKind8x4::K256U8;
-    bool threw = false;
-    try {
-        structural::run_bitbsr_spmv_once(dev, plan, dx, dy);
-    } catch (const std::runtime_error&) {
-        threw = true;
+    std::vector<double> book256(codebook);
+    book256.resize(256, 0.0);
+    plan.value_codebook = book256;
+    structural::run_bitbsr_spmv_once(dev, plan, dx, dy);
+    close(expected, host(dy), 1e-12);
+    plan.value_codec = structural::BitBsrValueCodecKind8x4::GlobalLogKmeans64;
+    structural::run_bitbsr_spmv_once(dev, plan, dx, dy);
+    close(expected, host(dy), 1e-12);
+}
+
+// A random 8x4-blocked matrix whose values come from `value(k)`.
+CsrMatrix<double> random_csr(int rows, int cols, double density, unsigned seed,
+                             double (*value)(unsigned)) {
+    CsrMatrix<double> a;
+    a.rows = rows;
+    a.cols = cols;
+    a.row_ptr.push_back(0);
+    unsigned s = seed;
+    auto next = [&]() { s = s * 1664525u + 1013904223u; return s >> 8; };
+    for (int r = 0; r < rows; ++r) {
+        for (int c = 0; c < cols; ++c) {
+            if ((next() % 10000) < density * 10000) {
+                a.col_idx.push_back(c);
+                a.values.push_back(value(next()));
+            }
+        }
+        a.row_ptr.push_back(static_cast<int>(a.col_idx.size()));
     }
-    CHECK(threw);
+    return a;
+}
+
+double val_one(unsigned) { return 1.0; }
+double val_const(unsigned) { return 2.5; }
+double val_sign(unsigned u) { return (u & 1) ? 1.0 : -1.0; }
+double val_sign_scale(unsigned u) { return (u & 1) ? 0.75 : -0.75; }
+double val_eighths(unsigned u) { return static_cast<double>(static_cast<int>(u % 64) - 32) / 8.0; }
+double val_wide(unsigned u) { return (static_cast<double>(u % 20001) - 10000.0) * 1e-3; }
+
+std::uint16_t half_bits(double v) {  // the values used are exact in fp16
+    const __half h = __double2half(v);
+    return __half_as_ushort(h);
+}
+
+// bf16 bits, round to nearest even (value_compression.hpp:105-109)
+std::uint16_t bf16_bits(float f) {
+    std::uint32_t u = 0;
+    std::memcpy(&u, &f, 4);
+    return static_cast<std::uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+float bf16_float(std::uint16_t b) {
+    const std::uint32_t u = static_cast<std::uint32_t>(b) << 16;
+    float f = 0.0f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+void test_family_value_codecs() {
+    using K = structural::BitBsrValueCodecKind8x4;
+    struct Case {
+        K codec;
+        double (*value)(unsigned);
+        double tol;
+    };
+    const Case cases[] = {{K::ImplicitOne, val_one, 1e-12},   {K::ConstC, val_const, 1e-12},
+                          {K::Sign2, val_sign, 1e-12},        {K::Sign2Scale, val_sign_scale, 1e-12},
+                          {K::Fp16, val_eighths, 1e-5},       {K::Bfp4, val_wide, 1e-5}};
+    for (const Case& cs : cases) {
+        const auto csr = random_csr(203, 301, 0.08, 7u + static_cast<unsigned>(cs.codec), cs.value);
+        structural::GpuBitBsrWorkspace<double> ws;
+        const auto dev = structural::convert_to_bitbsr_gpu_warp_direct_8x4_device(csr, ws);
+        const auto h = dev.to_host();
+        std::vector<double> x(csr.cols);
+        for (int i = 0; i < csr.cols; ++i) x[i] = ((i % 17) - 8) * 0.125;
+        // the matrix as the codec decodes it, in CSR order
+        std::vector<double> decoded(h.values.begin(), h.values.end());
+        structural::BitBsrSpmvPlan8x4<double> plan;
+        plan.value_codec = cs.codec;
+        const int nb = h.num_blocks();
+        if (cs.codec == K::ConstC) plan.value_scale = 2.5;
+        if (cs.codec == K::Sign2 || cs.codec == K::Sign2Scale) {  // build_sign2_tile32_masks
+            std::vector<std::uint32_t> masks(nb, 0);
+            for (int b = 0; b < nb; ++b) {
+                int k = h.block_val_ptr[b];
+                for (int bit = 0; bit < 32; ++bit)
+                    if (h.bitmap_words[b] & (1u << bit)) {
+                        if (h.values[k++] > 0) masks[b] |= 1u << bit;
+                    }
+            }
+            plan.sign_masks = masks;
+            plan.value_scale = cs.codec == K::Sign2 ? 1.0 : 0.75;
+        }
+        if (cs.codec == K::Fp16) {
+            std::vector<std::uint16_t> v16(h.values.size());
+            for (size_t i = 0; i < v16.size(); ++i) v16[i] = half_bits(h.values[i]);
+            plan.values16 = v16;
+        }
+        if (cs.codec == K::Bfp4) {  // build_bfp4_blkscale_value_codec
+            std::vector<std::uint8_t> packed((h.values.size() + 1) / 2, 0);
+            std::vector<std::uint16_t> scales(nb, 0);
+            for (int b = 0; b < nb; ++b) {
+                double mx = 0.0;
+                for (int k = h.block_val_ptr[b]; k < h.block_val_ptr[b + 1]; ++k)
+                    mx = std::max(mx, std::abs(h.values[k]));
+                float sc = static_cast<float>(mx / 7.0);
+                if (sc == 0.0f) sc = 1.0f;
+                scales[b] = bf16_bits(sc);
+                const float dsc = bf16_float(scales[b]);
+                for (int k = h.block_val_ptr[b]; k < h.block_val_ptr[b + 1]; ++k) {
+                    const long q = std::max(-7L, std::min(7L, std::lround(h.values[k] / static_cast<double>(dsc))));
+                    const std::uint8_t nib = static_cast<std::uint8_t>(q & 0xF);
+                    packed[k >> 1] |= (k & 1) ? static_cast<std::uint8_t>(nib << 4) : nib;
+                    decoded[k] = static_cast<double>(q) * dsc;
+                }
+            }
+            plan.packed_int4 = packed;
+            plan.block_scale_bf16 = scales;
+        }
+        // expected y from the decoded values in block/bit order
+        std::vector<double> expected(csr.rows, 0.0);
+        for (int br = 0; br < h.num_block_rows; ++br)
+            for (int b = h.block_row_ptr[br]; b < h.block_row_ptr[br + 1]; ++b) {
+                int k = h.block_val_ptr[b];
+                for (int bit = 0; bit < 32; ++bit)
+                    if (h.bitmap_words[b] & (1u << bit)) {
+                        const int row = br * 8 + bit / 4, col = h.block_col_idx[b] * 4 + bit % 4;
+                        expected[row] += decoded[k++] * x[col];
+                    }
+            }
+        structural::make_bitbsr_8x4_col_bitmap_packed(dev, plan.packed_col_bitmap_meta);
+        structural::make_bitbsr_8x4_col_bitmap_flag_load_balance_work_items(
+            dev, plan.load_balance, 32, plan.packed_col_bitmap_meta);
+        thrust::device_vector<double> dx(x.begin(), x.end()), dy;
+        structural::run_bitbsr_spmv_once(dev, plan, dx, dy);
+        double mx = 1e-30;
+        for (double e : expected) mx = std::max(mx, std::abs(e));
+        close(expected, host(dy), cs.tol * mx);
+    }
 }
 
 void test_hybrid_launchers_and_plan() {
@@ -201,6 +336,7 @@ int main() {
     }
     test_converter_and_work_items();
     test_bitbsr_only_operators();
+    test_family_value_codecs();
     test_hybrid_launchers_and_plan();
     std::printf("shim tests passed\n");
     return 0;
