@@ -1,0 +1,427 @@
+// gpu_value_codecs.cuh -- payload builders of the BitBSR-only value codecs
+// and the exact-value histogram behind the auto_lossless choice, with the
+// reference's names (structural/include/structural/gpu_value_codecs.cuh:
+// 20-700, value_compression.hpp:105-198, selector main_gpu_spmv.cu:127-174).
+// The payloads are the plan fields run_bitbsr_spmv_once decodes; the
+// encodings (cell bit order, tile packing, bf16/fp16 rounding, BFP scales)
+// are the reference's formats, bit for bit.  The k-means codebook builders
+// (k256, global log-k-means) are not provided: their payloads still run.
+#pragma once
+
+#include "structural/bitbsr.hpp"
+#include "structural/gpu_convert.cuh"
+#include "structural/operators/bitbsr_spmv_8x4_dispatch.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace structural {
+
+// ---- 16-bit encodings (value_compression.hpp:105-198) -------------------------
+
+inline std::uint32_t float_bits(float f) {
+    std::uint32_t u = 0;
+    std::memcpy(&u, &f, 4);
+    return u;
+}
+
+inline float bits_float(std::uint32_t u) {
+    float f = 0.0f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// bf16: round to nearest, ties to even, on the upper half of the fp32 bits.
+inline std::uint16_t float_to_bf16_bits(float value) {
+    const std::uint32_t u = float_bits(value);
+    return static_cast<std::uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+inline float bf16_bits_to_float(std::uint16_t bits) { return bits_float(static_cast<std::uint32_t>(bits) << 16); }
+
+// fp16 (IEEE binary16), round to nearest, ties to even; overflow -> inf,
+// NaN -> quiet NaN with the sign kept, values below half the smallest
+// subnormal -> signed zero.
+inline std::uint16_t float_to_fp16_bits(float value) {
+    const std::uint32_t u = float_bits(value);
+    const std::uint16_t sign = static_cast<std::uint16_t>((u >> 16) & 0x8000u);
+    const int e8 = static_cast<int>((u >> 23) & 0xFFu);
+    const std::uint32_t m23 = u & 0x7FFFFFu;
+    if (e8 == 0xFF) return static_cast<std::uint16_t>(sign | (m23 ? 0x7E00u : 0x7C00u));
+    int e5 = e8 - 112;  // rebias 127 -> 15
+    if (e5 >= 31) return static_cast<std::uint16_t>(sign | 0x7C00u);
+    // round the significand (with its hidden bit) right by `drop` bits
+    auto round_shift = [](std::uint32_t v, int drop) {
+        const std::uint32_t keep = v >> drop;
+        const std::uint32_t rest = v & ((1u << drop) - 1u);
+        const std::uint32_t half = 1u << (drop - 1);
+        return keep + ((rest > half || (rest == half && (keep & 1u))) ? 1u : 0u);
+    };
+    if (e5 <= 0) {  // subnormal result (or zero)
+        if (e5 < -10) return sign;
+        return static_cast<std::uint16_t>(sign | round_shift(m23 | 0x800000u, 14 - e5));
+    }
+    std::uint32_t m10 = round_shift(m23, 13);
+    if (m10 == 0x400u) {  // the rounding carried into the exponent
+        m10 = 0;
+        if (++e5 >= 31) return static_cast<std::uint16_t>(sign | 0x7C00u);
+    }
+    return static_cast<std::uint16_t>(sign | (static_cast<std::uint32_t>(e5) << 10) | m10);
+}
+
+// ---- value sets --------------------------------------------------------------
+
+// Ascending distinct values, stopping once unique_cap + 1 are found.
+template <typename T>
+std::vector<T> sorted_unique_values(const std::vector<T>& values, int unique_cap) {
+    std::vector<T> s(values);
+    std::sort(s.begin(), s.end());
+    std::vector<T> out;
+    for (const T v : s) {
+        if (!out.empty() && out.back() == v) continue;
+        out.push_back(v);
+        if (static_cast<int>(out.size()) > unique_cap) break;
+    }
+    return out;
+}
+
+struct DeviceExactValueHistogram {
+    Offset nnz = 0;
+    Offset num_blocks = 0;
+    std::size_t raw_payload_bytes = 0;
+    int unique_count = 0;
+    bool unique_overflow = false;
+    bool all_one = false;
+    bool const_c = false;
+    bool sign2 = false;
+    bool sign2_scale = false;
+    std::size_t const_c_payload_bytes = 0;
+    std::size_t sign2_payload_bytes = 0;
+    std::size_t sign2_scale_payload_bytes = 0;
+    std::size_t dict2_payload_bytes = 0;
+    std::size_t dict4_payload_bytes = 0;
+    std::size_t dict16_payload_bytes = 0;
+    std::size_t dict256_u8_payload_bytes = 0;
+    std::size_t dict65536_u16_payload_bytes = 0;
+};
+
+// Distinct-value statistics of a device BitBSR matrix and each lossless
+// codec's payload size.  unique_count counts up to 65537 (then
+// unique_overflow is set).
+template <typename T>
+DeviceExactValueHistogram build_device_exact_value_histogram(const DeviceBitBsrMatrix<T>& bitbsr,
+                                                             float* device_ms = nullptr) {
+    gpu_detail::CudaEventTimer timer(device_ms);
+    DeviceExactValueHistogram h;
+    h.nnz = bitbsr.nnz;
+    h.num_blocks = bitbsr.num_blocks;
+    h.raw_payload_bytes = static_cast<std::size_t>(bitbsr.nnz) * sizeof(T);
+    h.sign2_payload_bytes = static_cast<std::size_t>(bitbsr.num_blocks) * 4;
+    h.const_c_payload_bytes = bitbsr.nnz > 0 ? sizeof(T) : 0;
+    h.sign2_scale_payload_bytes = bitbsr.nnz > 0 ? h.sign2_payload_bytes + sizeof(T) : 0;
+    if (bitbsr.nnz > 0) {
+        std::vector<T> values(static_cast<size_t>(bitbsr.nnz));
+        thrust::copy(bitbsr.values.begin(), bitbsr.values.end(), values.begin());
+        const auto u = sorted_unique_values(values, 65536);
+        h.unique_count = static_cast<int>(u.size());
+        h.unique_overflow = u.size() > 65536;
+        if (u.size() == 1) {
+            h.const_c = true;
+            h.all_one = u[0] == T(1);
+        } else if (u.size() == 2) {
+            h.sign2 = u[0] == T(-1) && u[1] == T(1);
+            h.sign2_scale = u[0] != T(0) && u[0] == -u[1];
+        }
+    }
+    auto dict_bytes = [&](int words) {
+        return static_cast<std::size_t>(bitbsr.num_blocks) * words * 4 +
+               static_cast<std::size_t>(h.unique_count) * sizeof(T);
+    };
+    h.dict2_payload_bytes = dict_bytes(1);
+    h.dict4_payload_bytes = dict_bytes(2);
+    h.dict16_payload_bytes = dict_bytes(4);
+    h.dict256_u8_payload_bytes = dict_bytes(8);
+    h.dict65536_u16_payload_bytes = dict_bytes(16);
+    gpu_detail::finish(timer, device_ms);
+    return h;
+}
+
+// The smallest exact codec whose payload beats the raw values
+// (select_auto_lossless_value_codec, main_gpu_spmv.cu:127-174), as the
+// operator's codec kind.
+inline BitBsrValueCodecKind8x4 select_auto_lossless_value_codec(const DeviceExactValueHistogram& h) {
+    using K = BitBsrValueCodecKind8x4;
+    if (h.nnz == 0) return K::Raw;
+    auto saves = [&](std::size_t bytes) { return bytes < h.raw_payload_bytes; };
+    if (h.all_one && saves(0)) return K::ImplicitOne;
+    if (h.const_c && saves(h.const_c_payload_bytes)) return K::ConstC;
+    if (h.sign2 && saves(h.sign2_payload_bytes)) return K::Sign2;
+    if (h.sign2_scale && saves(h.sign2_scale_payload_bytes)) return K::Sign2Scale;
+    if (h.unique_count <= 2 && saves(h.dict2_payload_bytes)) return K::Dict2;
+    if (h.unique_count <= 4 && saves(h.dict4_payload_bytes)) return K::Unique4;
+    if (h.unique_count <= 16 && saves(h.dict16_payload_bytes)) return K::Unique16;
+    if (h.unique_count <= 256 && saves(h.dict256_u8_payload_bytes)) return K::Dict256U8;
+    if (!h.unique_overflow && h.unique_count <= 65536 && saves(h.dict65536_u16_payload_bytes))
+        return K::Dict65536U16;
+    return K::Raw;
+}
+
+// ---- per-cell walk ---------------------------------------------------------------
+
+namespace codec_detail {
+// f(block, bit, value_index) for every stored cell, blocks in order, bits ascending
+template <typename T, typename F>
+void for_each_cell(const BitBsrMatrix<T>& m, F&& f) {
+    for (Offset b = 0; b < m.num_blocks(); ++b) {
+        const std::uint32_t bm = m.bitmap_words[b];
+        Offset k = m.block_val_ptr[b];
+        for (int bit = 0; bit < 32; ++bit)
+            if (bm & (1u << bit)) f(b, bit, k++);
+    }
+}
+}  // namespace codec_detail
+
+// ---- constant and sign codecs --------------------------------------------------
+
+template <typename T>
+T build_const_c_value(const BitBsrMatrix<T>& bitbsr) {
+    bitbsr.validate();
+    if (bitbsr.values.empty()) throw std::runtime_error("const_c value codec requires at least one value");
+    for (const T v : bitbsr.values)
+        if (v != bitbsr.values.front())
+            throw std::runtime_error("const_c value codec requires every stored value to equal C");
+    return bitbsr.values.front();
+}
+
+template <typename T>
+void validate_implicit_one_values(const std::vector<T>& values) {
+    for (const T v : values)
+        if (v != T(1)) throw std::runtime_error("all_one value codec requires every stored value to be 1");
+}
+
+template <typename T>
+struct Sign2ScaleTile32ValueCodec {
+    T scale = T{1};
+    std::vector<std::uint32_t> sign_masks;
+    std::size_t payload_bytes() const { return sign_masks.size() * 4 + sizeof(T); }
+};
+
+// One word per block: cell bit set where the value is +1 (else it must be -1).
+template <typename T>
+std::vector<std::uint32_t> build_sign2_tile32_masks(const BitBsrMatrix<T>& bitbsr) {
+    bitbsr.validate();
+    std::vector<std::uint32_t> masks(static_cast<size_t>(bitbsr.num_blocks()), 0);
+    codec_detail::for_each_cell(bitbsr, [&](Offset b, int bit, Offset k) {
+        const T v = bitbsr.values[k];
+        if (v == T(1)) masks[b] |= 1u << bit;
+        else if (v != T(-1)) throw std::runtime_error("sign2 value codec requires values in {-1, +1}");
+    });
+    return masks;
+}
+
+template <typename T>
+Sign2ScaleTile32ValueCodec<T> build_sign2_scale_tile32_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    bitbsr.validate();
+    const auto u = sorted_unique_values(bitbsr.values, 2);
+    if (u.size() != 2) throw std::runtime_error("sign2_scale value codec requires exactly two values");
+    if (u[0] == T(0) || u[0] != -u[1]) throw std::runtime_error("sign2_scale value codec requires values in {-C, +C}");
+    Sign2ScaleTile32ValueCodec<T> c;
+    c.scale = u[1];
+    c.sign_masks.assign(static_cast<size_t>(bitbsr.num_blocks()), 0);
+    codec_detail::for_each_cell(bitbsr, [&](Offset b, int bit, Offset k) {
+        if (bitbsr.values[k] == u[1]) c.sign_masks[b] |= 1u << bit;
+    });
+    return c;
+}
+
+// ---- tile codes ------------------------------------------------------------------
+
+template <int BitsPerCode, typename T>
+std::vector<std::uint32_t> build_tile_code_words_from_value_ids(const BitBsrMatrix<T>& bitbsr,
+                                                                const std::vector<std::uint32_t>& value_ids) {
+    static_assert(BitsPerCode == 1 || BitsPerCode == 2 || BitsPerCode == 4 || BitsPerCode == 8 ||
+                      BitsPerCode == 16,
+                  "tile codec supports 1, 2, 4, 8, or 16 bits per 8x4 cell");
+    bitbsr.validate();
+    if (value_ids.size() != bitbsr.values.size()) throw std::runtime_error("tile value codec id count mismatch");
+    constexpr int kWords = BitsPerCode;  // 32 cells x BitsPerCode bits = BitsPerCode words
+    constexpr int kPerWord = 32 / BitsPerCode;
+    std::vector<std::uint32_t> words(static_cast<size_t>(bitbsr.num_blocks()) * kWords, 0);
+    codec_detail::for_each_cell(bitbsr, [&](Offset b, int bit, Offset k) {
+        const std::uint32_t id = value_ids[static_cast<size_t>(k)];
+        if (BitsPerCode < 32 && id >= (1u << BitsPerCode))
+            throw std::runtime_error("tile value codec id does not fit in tile field");
+        words[static_cast<size_t>(b) * kWords + bit / kPerWord] |= id << ((bit % kPerWord) * BitsPerCode);
+    });
+    return words;
+}
+
+template <int BitsPerCode, typename T>
+struct TileCodeValueCodec {
+    std::vector<T> codebook;
+    std::vector<std::uint32_t> value_ids;
+    std::vector<std::uint32_t> tile_code_words;
+    bool exact = true;
+    std::size_t payload_bytes() const { return tile_code_words.size() * 4 + codebook.size() * sizeof(T); }
+};
+
+// Exact dictionary: codebook = ascending distinct values, id = rank.
+template <int BitsPerCode, typename T>
+TileCodeValueCodec<BitsPerCode, T> build_exact_tile_code_value_codec(const BitBsrMatrix<T>& bitbsr,
+                                                                     int max_codebook_size, const char* name) {
+    TileCodeValueCodec<BitsPerCode, T> c;
+    c.codebook = sorted_unique_values(bitbsr.values, max_codebook_size);
+    if (static_cast<int>(c.codebook.size()) > max_codebook_size)
+        throw std::runtime_error(std::string(name) + " value codec requires fewer distinct values");
+    std::unordered_map<T, std::uint32_t> rank;
+    for (size_t i = 0; i < c.codebook.size(); ++i) rank.emplace(c.codebook[i], static_cast<std::uint32_t>(i));
+    c.value_ids.resize(bitbsr.values.size());
+    for (size_t i = 0; i < bitbsr.values.size(); ++i) {
+        const auto it = rank.find(bitbsr.values[i]);
+        if (it == rank.end()) throw std::runtime_error(std::string(name) + " exact value was not found in codebook");
+        c.value_ids[i] = it->second;
+    }
+    c.tile_code_words = build_tile_code_words_from_value_ids<BitsPerCode>(bitbsr, c.value_ids);
+    return c;
+}
+
+template <typename T> struct Dict2Tile32ValueCodec : TileCodeValueCodec<1, T> {};
+template <typename T> struct Unique4Tile64ValueCodec : TileCodeValueCodec<2, T> {};
+template <typename T> struct Unique16Tile128ValueCodec : TileCodeValueCodec<4, T> {};
+template <typename T> struct Dict256Tile256ValueCodec : TileCodeValueCodec<8, T> {};
+template <typename T> struct Dict65536Tile512ValueCodec : TileCodeValueCodec<16, T> {};
+
+namespace codec_detail {
+template <typename Out, int Bits, typename T>
+Out named_tile_codec(const BitBsrMatrix<T>& m, int cap, const char* name) {
+    Out out;
+    static_cast<TileCodeValueCodec<Bits, T>&>(out) = build_exact_tile_code_value_codec<Bits>(m, cap, name);
+    return out;
+}
+}  // namespace codec_detail
+
+template <typename T>
+Dict2Tile32ValueCodec<T> build_dict2_tile32_value_codec(const BitBsrMatrix<T>& m) {
+    return codec_detail::named_tile_codec<Dict2Tile32ValueCodec<T>, 1>(m, 2, "dict2_tile32");
+}
+template <typename T>
+Unique4Tile64ValueCodec<T> build_unique4_tile64_value_codec(const BitBsrMatrix<T>& m) {
+    return codec_detail::named_tile_codec<Unique4Tile64ValueCodec<T>, 2>(m, 4, "unique4_tile64");
+}
+template <typename T>
+Unique16Tile128ValueCodec<T> build_unique16_tile128_value_codec(const BitBsrMatrix<T>& m) {
+    return codec_detail::named_tile_codec<Unique16Tile128ValueCodec<T>, 4>(m, 16, "unique16_tile128");
+}
+template <typename T>
+Dict256Tile256ValueCodec<T> build_dict256_tile256_value_codec(const BitBsrMatrix<T>& m) {
+    return codec_detail::named_tile_codec<Dict256Tile256ValueCodec<T>, 8>(m, 256, "dict256_tile256");
+}
+template <typename T>
+Dict65536Tile512ValueCodec<T> build_dict65536_tile512_value_codec(const BitBsrMatrix<T>& m) {
+    return codec_detail::named_tile_codec<Dict65536Tile512ValueCodec<T>, 16>(m, 65536, "dict65536_tile512");
+}
+
+// ---- 16-bit values -----------------------------------------------------------------
+
+struct Round16NnzValueCodec {
+    std::vector<std::uint16_t> values16;
+    std::size_t payload_bytes() const { return values16.size() * 2; }
+};
+
+struct Round16Tile512ValueCodec {
+    std::vector<std::uint32_t> tile_code_words;
+    std::size_t payload_bytes() const { return tile_code_words.size() * 4; }
+};
+
+// encode_bits(value) -> 16 bits (float_to_bf16_bits / float_to_fp16_bits), per nnz
+template <typename T, typename EncodeBitsFn>
+Round16NnzValueCodec build_round16_nnz_value_codec(const BitBsrMatrix<T>& bitbsr, EncodeBitsFn encode_bits) {
+    bitbsr.validate();
+    Round16NnzValueCodec c;
+    c.values16.reserve(bitbsr.values.size());
+    for (const T v : bitbsr.values) c.values16.push_back(static_cast<std::uint16_t>(encode_bits(v)));
+    return c;
+}
+
+// the same 16 bits per cell, two cells per word, 16 words per block
+template <typename T, typename EncodeBitsFn>
+Round16Tile512ValueCodec build_round16_tile512_value_codec(const BitBsrMatrix<T>& bitbsr, EncodeBitsFn encode_bits) {
+    bitbsr.validate();
+    Round16Tile512ValueCodec c;
+    c.tile_code_words.assign(static_cast<size_t>(bitbsr.num_blocks()) * 16, 0);
+    codec_detail::for_each_cell(bitbsr, [&](Offset b, int bit, Offset k) {
+        const std::uint32_t v = static_cast<std::uint16_t>(encode_bits(bitbsr.values[k]));
+        c.tile_code_words[static_cast<size_t>(b) * 16 + bit / 2] |= v << ((bit % 2) * 16);
+    });
+    return c;
+}
+
+// ---- block floating point --------------------------------------------------------
+
+struct Bfp8BlkScaleValueCodec {
+    std::vector<signed char> int8_values;
+    std::vector<std::uint16_t> block_scale_bf16;
+    std::size_t payload_bytes() const { return int8_values.size() + block_scale_bf16.size() * 2; }
+};
+
+struct Bfp4BlkScaleValueCodec {
+    Offset nnz = 0;
+    std::vector<std::uint8_t> packed_int4;
+    std::vector<std::uint16_t> block_scale_bf16;
+    std::size_t payload_bytes() const { return packed_int4.size() + block_scale_bf16.size() * 2; }
+};
+
+namespace codec_detail {
+// Per block: scale = bf16(float(max|v| / qmax)) (1 when the block is all
+// zero), q = clamp(lround(v / scale), -qmax, qmax); emit(k, q) per value.
+template <typename T, typename Emit>
+void block_quantize(const BitBsrMatrix<T>& m, double qmax, std::vector<std::uint16_t>& scales, Emit&& emit) {
+    scales.assign(static_cast<size_t>(m.num_blocks()), 0);
+    for (Offset b = 0; b < m.num_blocks(); ++b) {
+        double mx = 0.0;
+        for (Offset k = m.block_val_ptr[b]; k < m.block_val_ptr[b + 1]; ++k)
+            mx = std::max(mx, std::abs(static_cast<double>(m.values[k])));
+        float s = static_cast<float>(mx / qmax);
+        if (s == 0.0f) s = 1.0f;
+        scales[b] = float_to_bf16_bits(s);
+        const double d = static_cast<double>(bf16_bits_to_float(scales[b]));
+        const long lim = static_cast<long>(qmax);
+        for (Offset k = m.block_val_ptr[b]; k < m.block_val_ptr[b + 1]; ++k)
+            emit(k, std::max(-lim, std::min(lim, std::lround(static_cast<double>(m.values[k]) / d))));
+    }
+}
+}  // namespace codec_detail
+
+template <typename T>
+Bfp8BlkScaleValueCodec build_bfp8_blkscale_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    bitbsr.validate();
+    Bfp8BlkScaleValueCodec c;
+    c.int8_values.assign(bitbsr.values.size(), 0);
+    codec_detail::block_quantize(bitbsr, 127.0, c.block_scale_bf16,
+                                 [&](Offset k, long q) { c.int8_values[k] = static_cast<signed char>(q); });
+    return c;
+}
+
+// two signed 4-bit mantissas per byte: even nnz position in the low nibble
+template <typename T>
+Bfp4BlkScaleValueCodec build_bfp4_blkscale_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    bitbsr.validate();
+    Bfp4BlkScaleValueCodec c;
+    c.nnz = bitbsr.nnz();
+    c.packed_int4.assign(static_cast<size_t>((bitbsr.nnz() + 1) / 2), 0);
+    codec_detail::block_quantize(bitbsr, 7.0, c.block_scale_bf16, [&](Offset k, long q) {
+        const std::uint8_t nib = static_cast<std::uint8_t>(q & 0xF);
+        std::uint8_t& byte = c.packed_int4[static_cast<size_t>(k >> 1)];
+        byte = (k & 1) ? static_cast<std::uint8_t>((byte & 0x0F) | (nib << 4))
+                       : static_cast<std::uint8_t>((byte & 0xF0) | nib);
+    });
+    return c;
+}
+
+}  // namespace structural

@@ -5,6 +5,7 @@
 // operators, the hybrid/joint launchers, and the device pipeline handle.
 // Built and run by tests/test_gpu_shim.py (needs a GPU).
 #include "structural/csr_bitbsr_hybrid.cuh"
+#include "structural/gpu_value_codecs.cuh"
 
 #include <cuda_fp16.h>
 
@@ -326,6 +327,115 @@ void test_hybrid_launchers_and_plan() {
     close(expected, host(dy), 1e-12);
 }
 
+// ---- family codec builders vs the reference builders' payloads -------------------
+#include "codec_golden.inc"
+
+// the matrices of oracle/ref_codec_golden.cu (same formulas)
+double golden_value(int kind, int r, int c) {
+    const int h = (r * 131 + c * 71) % 97;
+    switch (kind) {
+        case 0: return (h % 3 == 0) ? -1.5 : (h % 3 == 1 ? 0.5 : 2.0);
+        case 1: return (h % 2) ? -1.5 : 2.0;
+        case 2: return (h % 2) ? 1.0 : -1.0;
+        case 3: return (h % 2) ? 0.75 : -0.75;
+        case 4: return 3.25;
+        default: {
+            const double m = (h - 48) / 7.0;
+            return m * std::pow(10.0, (r + c) % 7 - 3);
+        }
+    }
+}
+
+structural::BitBsrMatrix<double> golden_bitbsr(int kind, structural::DeviceBitBsrMatrix<double>* dev_out = nullptr) {
+    CsrMatrix<double> a;
+    a.rows = 37;
+    a.cols = 53;
+    a.row_ptr.push_back(0);
+    for (int r = 0; r < a.rows; ++r) {
+        for (int c = 0; c < a.cols; ++c)
+            if ((r * 7 + c * 13 + r * c) % 11 < 4) {
+                a.col_idx.push_back(c);
+                a.values.push_back(golden_value(kind, r, c));
+            }
+        a.row_ptr.push_back(static_cast<int>(a.col_idx.size()));
+    }
+    structural::GpuBitBsrWorkspace<double> ws;
+    auto dev = structural::convert_to_bitbsr_gpu_warp_direct_8x4_device(a, ws);
+    auto h = dev.to_host();
+    if (dev_out) *dev_out = std::move(dev);
+    return h;
+}
+
+template <typename A, typename B>
+void same(const std::vector<A>& got, const B* want, size_t n, const char* what) {
+    if (got.size() != n) {
+        std::fprintf(stderr, "%s: %zu values, golden %zu\n", what, got.size(), n);
+        std::exit(1);
+    }
+    for (size_t i = 0; i < n; ++i)
+        if (!(got[i] == static_cast<A>(want[i]))) {
+            std::fprintf(stderr, "%s: value %zu differs from the reference builder\n", what, i);
+            std::exit(1);
+        }
+}
+
+template <typename Codec>
+void same_tile(const Codec& c, const double* cb, size_t ncb, const uint32_t* w, size_t nw, const char* what) {
+    same(c.codebook, cb, ncb, what);
+    same(c.tile_code_words, w, nw, what);
+}
+
+void test_family_builders() {
+    using namespace structural;
+    const auto b0 = golden_bitbsr(0);
+    same_tile(build_unique4_tile64_value_codec(b0), g_unique4_codebook, g_unique4_codebook_n, g_unique4_words,
+              g_unique4_words_n, "unique4");
+    same_tile(build_unique16_tile128_value_codec(b0), g_unique16_codebook, g_unique16_codebook_n, g_unique16_words,
+              g_unique16_words_n, "unique16");
+    same_tile(build_dict256_tile256_value_codec(b0), g_dict256_codebook, g_dict256_codebook_n, g_dict256_words,
+              g_dict256_words_n, "dict256");
+    same_tile(build_dict65536_tile512_value_codec(b0), g_dict65536_codebook, g_dict65536_codebook_n,
+              g_dict65536_words, g_dict65536_words_n, "dict65536");
+    same_tile(build_dict2_tile32_value_codec(golden_bitbsr(1)), g_dict2_codebook, g_dict2_codebook_n, g_dict2_words,
+              g_dict2_words_n, "dict2");
+    same(build_sign2_tile32_masks(golden_bitbsr(2)), g_sign2_masks, g_sign2_masks_n, "sign2");
+    const auto s3 = build_sign2_scale_tile32_value_codec(golden_bitbsr(3));
+    CHECK(s3.scale == g_sign2s_scale[0]);
+    same(s3.sign_masks, g_sign2s_masks, g_sign2s_masks_n, "sign2_scale");
+    CHECK(build_const_c_value(golden_bitbsr(4)) == g_const_c[0]);
+    const auto b5 = golden_bitbsr(5);
+    const auto q8 = build_bfp8_blkscale_value_codec(b5);
+    same(std::vector<int>(q8.int8_values.begin(), q8.int8_values.end()), g_bfp8_q, g_bfp8_q_n, "bfp8 q");
+    same(q8.block_scale_bf16, g_bfp8_scale, g_bfp8_scale_n, "bfp8 scale");
+    const auto q4 = build_bfp4_blkscale_value_codec(b5);
+    same(q4.packed_int4, g_bfp4_packed, g_bfp4_packed_n, "bfp4 packed");
+    same(q4.block_scale_bf16, g_bfp4_scale, g_bfp4_scale_n, "bfp4 scale");
+    const auto bf = [](double v) { return float_to_bf16_bits(static_cast<float>(v)); };
+    const auto hf = [](double v) { return float_to_fp16_bits(static_cast<float>(v)); };
+    same(build_round16_nnz_value_codec(b5, bf).values16, g_bf16_nnz, g_bf16_nnz_n, "bf16 nnz");
+    same(build_round16_nnz_value_codec(b5, hf).values16, g_fp16_nnz, g_fp16_nnz_n, "fp16 nnz");
+    same(build_round16_tile512_value_codec(b5, bf).tile_code_words, g_bf16_tile512, g_bf16_tile512_n, "bf16 tile512");
+
+    // histogram and the auto_lossless choice (main_gpu_spmv.cu:127-174)
+    using K = BitBsrValueCodecKind8x4;
+    const int kinds[] = {4, 2, 3, 1, 0, 5};
+    const K want[] = {K::ConstC, K::Sign2, K::Sign2Scale, K::Dict2, K::Unique4, K::Raw};
+    for (int i = 0; i < 6; ++i) {
+        DeviceBitBsrMatrix<double> dev;
+        golden_bitbsr(kinds[i], &dev);
+        const auto h = build_device_exact_value_histogram(dev);
+        CHECK(select_auto_lossless_value_codec(h) == want[i]);
+    }
+    // an all-one matrix
+    auto ones = golden_bitbsr(4);
+    CsrMatrix<double> one = kat_9x4404();
+    for (auto& v : one.values) v = 1.0;
+    structural::GpuBitBsrWorkspace<double> ws;
+    const auto d1 = convert_to_bitbsr_gpu_warp_direct_8x4_device(one, ws);
+    CHECK(select_auto_lossless_value_codec(build_device_exact_value_histogram(d1)) == K::ImplicitOne);
+    (void)ones;
+}
+
 }  // namespace
 
 int main() {
@@ -337,6 +447,7 @@ int main() {
     test_converter_and_work_items();
     test_bitbsr_only_operators();
     test_family_value_codecs();
+    test_family_builders();
     test_hybrid_launchers_and_plan();
     std::printf("shim tests passed\n");
     return 0;

@@ -27,7 +27,8 @@ def _stale():
     if not os.path.exists(BIN):
         return True
     t = os.path.getmtime(BIN)
-    deps = [SRC, os.path.join(LIBDIR, "libcove_b200.so")]
+    deps = [SRC, os.path.join(LIBDIR, "libcove_b200.so"),
+            os.path.join(ROOT, "tests", "cpp", "codec_golden.inc")]
     inc = os.path.join(ROOT, "cove-spmv_b200", "include", "structural")
     for dp, _, fs in os.walk(inc):
         deps += [os.path.join(dp, f) for f in fs]
