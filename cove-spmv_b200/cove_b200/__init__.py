@@ -114,6 +114,11 @@ class CgResult(C.Structure):
                 ("rs_final", C.c_double), ("ms_total", C.c_double), ("ms_spmv", C.c_double)]
 
 
+class IrResult(C.Structure):
+    _fields_ = [("outer", C.c_int32), ("inner_total", C.c_int32), ("final_relres", C.c_double),
+                ("reached", C.c_int32), ("ms_total", C.c_double)]
+
+
 class MmMatrix(C.Structure):
     _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("nnz", C.c_int64),
                 ("row_ptr", C.POINTER(C.c_int64)), ("col_idx", C.POINTER(C.c_int32)),
@@ -134,7 +139,7 @@ EXPORTED = [
     "cove_lb_layout_count", "cove_lb_layout_fill",
     "cove_hybrid_spmv", "cove_spmv", "cove_spmv_route", "cove_spmv_host",
     "cove_spmv_launches", "cove_compare_vectors", "cove_canonical_x", "cove_cg_solve",
-    "cove_mm_read", "cove_mm_free",
+    "cove_mm_read", "cove_mm_free", "cove_ir_solve", "cove_fcg_solve", "cove_dist_mp_solve",
     "cove_cg_solve_noalloc",
     "cove_dist_halo_plan", "cove_dist_id_bytes", "cove_dist_make_id", "cove_dist_create", "cove_dist_destroy",
     "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv", "cove_dist_spmv_launches",
@@ -187,6 +192,9 @@ def _setup(L):
     L.cove_canonical_x.argtypes = [vp, i64, i32, vp]
     L.cove_cg_solve.argtypes = [vp, vp, vp, i32, C.POINTER(CgResult), vp]
     L.cove_mm_read.argtypes = [C.c_char_p, i32, C.POINTER(MmMatrix)]
+    L.cove_ir_solve.argtypes = [vp, i32, vp, vp, C.c_double, i32, i32, C.POINTER(IrResult), vp]
+    L.cove_fcg_solve.argtypes = [vp, i32, vp, vp, C.c_double, i32, i32, C.POINTER(IrResult), vp]
+    L.cove_dist_mp_solve.argtypes = [vp, i32, i32, vp, vp, C.c_double, i32, i32, C.POINTER(IrResult), vp]
     L.cove_mm_free.restype = None
     L.cove_mm_free.argtypes = [C.POINTER(MmMatrix)]
     L.cove_cg_solve_noalloc.argtypes = [vp, vp, vp, i32, C.POINTER(CgResult), vp]
@@ -385,6 +393,15 @@ class Plan:
     def launches(self, route=None) -> int:
         return int(lib().cove_spmv_launches(self._h, self.info.dispatched_route if route is None
                                             else route))
+
+    def mp_solve(self, b, x, inner_route, tol=1e-10, k_inner=20, max_outer=50, flexible=False,
+                 stream=None) -> IrResult:
+        """Mixed-precision iterative refinement (flexible=False) or flexible CG."""
+        res = IrResult()
+        fn = lib().cove_fcg_solve if flexible else lib().cove_ir_solve
+        check(fn(self._h, inner_route, _dptr(b), _dptr(x), tol, k_inner, max_outer, C.byref(res),
+                 _stream_handle(stream)))
+        return res
 
     def cg(self, b, x, iters, stream=None) -> CgResult:
         res = CgResult()

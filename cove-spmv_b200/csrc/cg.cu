@@ -18,6 +18,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <cmath>
 #include <chrono>
 #include <mutex>
 #include <thread>
@@ -100,6 +101,106 @@ __global__ void cg_p_kernel(int64_t n, const double* __restrict__ scal, int rs_s
         p[i] = r[i] + beta * p[i];
 }
 
+
+// ---- mixed-precision solver kernels (IR / flexible CG) --------------------------
+// Scalar slots: [0], [1] inner r.r (alternating), [2] p.Ap, [3] outer r.r,
+// [4] ||b||^2, [6] inner stop flag, [7] inner iterations run, [8] r.z,
+// [9] rn.zn, [10] rn.z, [11] outer p.Ap.
+
+// Inner bounded CG step (bench_cg_solve.cu:311-330): stop for good once
+// p.Ap is not positive; else d += alpha p, ri -= alpha Ap and the ri.ri
+// partials.  Every CTA takes the same decision from the same scalars.
+__global__ void ir_update_kernel(int64_t n, double* __restrict__ scal, int rs_slot,
+                                 const double* __restrict__ p, const double* __restrict__ ap,
+                                 double* __restrict__ d, double* __restrict__ ri,
+                                 double* __restrict__ partial) {
+    const double pap = scal[2];
+    const bool stop = scal[6] != 0.0 || !(pap > 0.0);
+    const double alpha = stop ? 0.0 : scal[rs_slot] / pap;
+    double s = 0.0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        if (!stop) {
+            d[i] += alpha * p[i];
+            ri[i] -= alpha * ap[i];
+        }
+        s += ri[i] * ri[i];
+    }
+    __shared__ double sh[kThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < kThreads / 32; ++w) t += sh[w];
+        partial[blockIdx.x] = t;
+        if (blockIdx.x == 0) {
+            scal[6] = stop ? 1.0 : 0.0;
+            if (!stop) scal[7] += 1.0;
+        }
+    }
+}
+
+// p = ri + (rs'/rs) p unless the inner solve has stopped
+__global__ void ir_p_kernel(int64_t n, const double* __restrict__ scal, int rs_slot, int new_slot,
+                            const double* __restrict__ ri, double* __restrict__ p) {
+    if (scal[6] != 0.0) return;
+    const double rs = scal[rs_slot];
+    const double beta = rs != 0.0 ? scal[new_slot] / rs : 0.0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        p[i] = ri[i] + beta * p[i];
+}
+
+// y = a + s * b   (s = +1 / -1)
+__global__ void axpy_kernel(int64_t n, const double* __restrict__ a, double s,
+                            const double* __restrict__ b, double* __restrict__ y) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] = a[i] + s * b[i];
+}
+
+// flexible CG outer step: alpha = rz / pAp (0 if pAp <= 0), x += alpha p,
+// rn = r - alpha Ap, rn.rn partials
+__global__ void fcg_update_kernel(int64_t n, const double* __restrict__ scal,
+                                  const double* __restrict__ p, const double* __restrict__ ap,
+                                  const double* __restrict__ r, double* __restrict__ x,
+                                  double* __restrict__ rn, double* __restrict__ partial) {
+    const double pap = scal[11];
+    const double alpha = pap > 0.0 ? scal[8] / pap : 0.0;
+    double s = 0.0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        x[i] += alpha * p[i];
+        const double v = r[i] - alpha * ap[i];
+        rn[i] = v;
+        s += v * v;
+    }
+    __shared__ double sh[kThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < kThreads / 32; ++w) t += sh[w];
+        partial[blockIdx.x] = t;
+    }
+}
+
+// flexible Polak-Ribiere: beta = max(0, (rn.zn - rn.z) / rz); p = zn + beta p;
+// then rz = rn.zn (bench_cg_solve.cu:430-436)
+__global__ void fcg_p_kernel(int64_t n, double* __restrict__ scal, const double* __restrict__ zn,
+                             double* __restrict__ p) {
+    double beta = (scal[9] - scal[10]) / scal[8];
+    if (!(beta > 0.0)) beta = 0.0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        p[i] = zn[i] + beta * p[i];
+}
+
+__global__ void fcg_rz_kernel(double* __restrict__ scal) { scal[8] = scal[9]; }
 
 // NCCL is resolved at run time: a process that already holds libnccl.so.2
 // (PyTorch loads its own) keeps using that copy, and the library itself
@@ -273,12 +374,15 @@ void allreduce_scalar(cove_dist* d, double* v, cudaStream_t s) {
     if (r == ncclInProgress) wait_comm_ready(d->comm, d->timeout_ms);
 }
 
+// The route a plan runs for `route` (< 0: its dispatched route).
+int route_of(const cove_plan* P, int route) { return route < 0 ? P->dispatched_route : route; }
+
 // y_local = A_local x_window over the rank's plans (consecutive row blocks)
 float spmv_plans(const std::vector<cove_plan*>& plans, const double* xw, double* y,
-                 cudaStream_t s) {
+                 cudaStream_t s, int route = -1) {
     int64_t off = 0;
     for (const cove_plan* P : plans) {
-        launch_hybrid_spmv(P->shape(), P->route_values(P->dispatched_route), xw, y + off, s);
+        launch_hybrid_spmv(P->shape(), P->route_values(route_of(P, route)), xw, y + off, s);
         off += P->rows;
     }
     return 0.0f;
@@ -287,10 +391,10 @@ float spmv_plans(const std::vector<cove_plan*>& plans, const double* xw, double*
 // y_local = A_local x_window on a partition: the halo runs on the comm
 // stream while the block rows that read only own columns are computed; the
 // rest follow once it has landed, then any overflow pass.
-void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s) {
+void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s, int route = -1) {
     if (!d->overlap) {
         halo(d, xw, s);
-        spmv_plans(d->plans, xw, y, s);
+        spmv_plans(d->plans, xw, y, s, route);
         return;
     }
     CUDA_OK(cudaEventRecord(d->x_ready, s));
@@ -303,7 +407,7 @@ void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s) {
         for (size_t i = 0; i < d->plans.size(); ++i) {
             const cove_plan* P = d->plans[i];
             const KernelShape k = P->shape();
-            const RouteValues rv = P->route_values(P->dispatched_route);
+            const RouteValues rv = P->route_values(route_of(P, route));
             for (const auto& r : d->ranges[i]) {
                 if (r.halo != (pass == 1)) continue;
                 KernelShape kr = k;
@@ -318,7 +422,7 @@ void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s) {
     int64_t off = 0;
     for (const cove_plan* P : d->plans) {
         const KernelShape k = P->shape();
-        const RouteValues rv = P->route_values(P->dispatched_route);
+        const RouteValues rv = P->route_values(route_of(P, route));
         if (hybrid_spmv_launch_count(k, rv) > 1) {
             KernelShape ko = k;
             ko.part = 2;
@@ -445,10 +549,219 @@ void cg_run(cove_dist* d, const std::vector<cove_plan*>& plans, int64_t n_local,
     }
 }
 
+// ---- mixed-precision iterative refinement and flexible CG ------------------------
+// (bench_cg_solve.cu:280-448).  The outer level uses an exact (lossless)
+// route, the inner bounded CG a cheaper one; both run on one plan or on a
+// row-block partition (halo + allreduce as in cg_run).  Inner alpha, beta and
+// the breakdown stop stay on the device; the host reads one residual norm per
+// outer step.
+
+struct MpSolver {
+    cove_dist* d = nullptr;
+    std::vector<cove_plan*> plans;
+    int64_t n = 0, p_off = 0, wl = 0;
+    int exact_route = COVE_ROUTE_HYBRID, inner_route = COVE_ROUTE_HYBRID;
+    cudaStream_t s = nullptr;
+    DevBuf xw, pw, r, dvec, ri, ap, z, zn, rn, partial, scal;
+    int ug = 1;
+
+    double* S() { return scal.as<double>(); }
+    double* p() { return pw.as<double>() + p_off; }
+    double* x() { return xw.as<double>() + p_off; }
+
+    void setup() {
+        alloc_n<double>(xw, wl);
+        alloc_n<double>(pw, wl);
+        for (DevBuf* b : {&r, &dvec, &ri, &ap, &z, &zn, &rn}) alloc_n<double>(*b, n);
+        alloc_n<double>(partial, kDotCtas);
+        alloc_n<double>(scal, 16);
+        CUDA_OK(cudaMemsetAsync(xw.p, 0, static_cast<size_t>(wl) * 8, s));
+        CUDA_OK(cudaMemsetAsync(pw.p, 0, static_cast<size_t>(wl) * 8, s));
+        CUDA_OK(cudaMemsetAsync(scal.p, 0, 16 * 8, s));
+        ug = static_cast<int>(std::min<int64_t>(grid_for(n, kThreads), kDotCtas));
+    }
+    void matvec(int route, double* window, double* y) {
+        if (d) {
+            spmv_dist(d, window, y, s, route);
+        } else {
+            spmv_plans(plans, window, y, s, route);
+        }
+    }
+    void dot_to(const double* a, const double* b, int slot) {
+        dot(n, a, b, partial.as<double>(), S() + slot, s);
+        allreduce_scalar(d, S() + slot, s);
+    }
+    double read(int slot) {
+        double v = 0.0;
+        CUDA_LAUNCH_OK();
+        wait_stream(d, s);
+        CUDA_OK(cudaMemcpy(&v, S() + slot, 8, cudaMemcpyDeviceToHost));
+        return v;
+    }
+    // out ~= A^-1 rhs: k_inner steps of CG on the inner route, from out = 0
+    void inner(const double* rhs, double* out, int k_inner) {
+        CUDA_OK(cudaMemsetAsync(out, 0, static_cast<size_t>(n) * 8, s));
+        CUDA_OK(cudaMemcpyAsync(ri.p, rhs, static_cast<size_t>(n) * 8, cudaMemcpyDeviceToDevice, s));
+        CUDA_OK(cudaMemcpyAsync(p(), rhs, static_cast<size_t>(n) * 8, cudaMemcpyDeviceToDevice, s));
+        CUDA_OK(cudaMemsetAsync(S() + 6, 0, 8, s));  // not stopped
+        dot_to(ri.as<double>(), ri.as<double>(), 0);
+        for (int j = 0; j < k_inner; ++j) {
+            const int cur = j & 1, nxt = cur ^ 1;
+            matvec(inner_route, pw.as<double>(), ap.as<double>());
+            dot_to(p(), ap.as<double>(), 2);
+            ir_update_kernel<<<kDotCtas, kThreads, 0, s>>>(n, S(), cur, p(), ap.as<double>(), out,
+                                                         ri.as<double>(), partial.as<double>());
+            dot_final_kernel<<<1, kThreads, 0, s>>>(partial.as<double>(), kDotCtas, S() + nxt);
+            allreduce_scalar(d, S() + nxt, s);
+            ir_p_kernel<<<ug, kThreads, 0, s>>>(n, S(), cur, nxt, ri.as<double>(), p());
+        }
+        CUDA_LAUNCH_OK();
+    }
+    // ||b - A_exact x||^2 into `res` (the outer residual) and slot 3
+    void exact_residual(const double* b, double* res) {
+        matvec(exact_route, xw.as<double>(), ap.as<double>());
+        axpy_kernel<<<ug, kThreads, 0, s>>>(n, b, -1.0, ap.as<double>(), res);
+        dot_to(res, res, 3);
+    }
+};
+
+void mp_solve(MpSolver& m, bool flexible, const double* b, double* x_out, double tol, int k_inner,
+              int max_outer, cove_ir_result* res) {
+    m.setup();
+    cudaEvent_t e0, e1;
+    CUDA_OK(cudaEventCreate(&e0));
+    CUDA_OK(cudaEventCreate(&e1));
+    m.dot_to(b, b, 4);
+    const double bnorm = std::sqrt(m.read(4));
+    const double denom = bnorm > 0.0 ? bnorm : 1.0;
+    CUDA_OK(cudaEventRecord(e0, m.s));
+    int outer = 0;
+    double* r = m.r.as<double>();
+    if (!flexible) {
+        // iterative refinement: r = b; repeat {d = inner(r); x += d; r = b - A x}
+        CUDA_OK(cudaMemcpyAsync(r, b, static_cast<size_t>(m.n) * 8, cudaMemcpyDeviceToDevice, m.s));
+        m.dot_to(r, r, 3);
+        for (outer = 0; outer < max_outer; ++outer) {
+            if (std::sqrt(m.read(3)) / denom < tol) break;
+            m.inner(r, m.dvec.as<double>(), k_inner);
+            axpy_kernel<<<m.ug, kThreads, 0, m.s>>>(m.n, m.x(), 1.0, m.dvec.as<double>(), m.x());
+            m.exact_residual(b, r);
+        }
+    } else {
+        // flexible CG: z = M r, p = z; per step exact Ap, x += a p, rn = r - a Ap,
+        // zn = M rn, beta = max(0, (rn.zn - rn.z) / r.z), p = zn + beta p
+        double* z = m.z.as<double>();
+        double* zn = m.zn.as<double>();
+        double* rn = m.rn.as<double>();
+        CUDA_OK(cudaMemcpyAsync(r, b, static_cast<size_t>(m.n) * 8, cudaMemcpyDeviceToDevice, m.s));
+        m.inner(r, z, k_inner);
+        CUDA_OK(cudaMemcpyAsync(m.p(), z, static_cast<size_t>(m.n) * 8, cudaMemcpyDeviceToDevice, m.s));
+        m.dot_to(r, z, 8);
+        for (outer = 0; outer < max_outer; ++outer) {
+            m.matvec(m.exact_route, m.pw.as<double>(), m.ap.as<double>());
+            m.dot_to(m.p(), m.ap.as<double>(), 11);
+            fcg_update_kernel<<<kDotCtas, kThreads, 0, m.s>>>(m.n, m.S(), m.p(), m.ap.as<double>(), r,
+                                                             m.x(), rn, m.partial.as<double>());
+            dot_final_kernel<<<1, kThreads, 0, m.s>>>(m.partial.as<double>(), kDotCtas, m.S() + 3);
+            allreduce_scalar(m.d, m.S() + 3, m.s);
+            const double pap = m.read(11);
+            if (!(pap > 0.0)) break;
+            if (std::sqrt(m.read(3)) / denom < tol) {
+                ++outer;
+                break;
+            }
+            // the p window is the inner solve's work vector: keep p in dvec meanwhile
+            CUDA_OK(cudaMemcpyAsync(m.dvec.p, m.p(), static_cast<size_t>(m.n) * 8,
+                                    cudaMemcpyDeviceToDevice, m.s));
+            m.inner(rn, zn, k_inner);
+            CUDA_OK(cudaMemcpyAsync(m.p(), m.dvec.p, static_cast<size_t>(m.n) * 8,
+                                    cudaMemcpyDeviceToDevice, m.s));
+            m.dot_to(rn, zn, 9);
+            m.dot_to(rn, z, 10);
+            fcg_p_kernel<<<m.ug, kThreads, 0, m.s>>>(m.n, m.S(), zn, m.p());
+            fcg_rz_kernel<<<1, 1, 0, m.s>>>(m.S());
+            std::swap(r, rn);
+            std::swap(z, zn);
+        }
+        // the true residual with the exact operator
+        m.exact_residual(b, m.rn.as<double>());
+    }
+    CUDA_OK(cudaEventRecord(e1, m.s));
+    const double rs = m.read(3);
+    float ms = 0.0f;
+    CUDA_OK(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    CUDA_OK(cudaMemcpyAsync(x_out, m.x(), static_cast<size_t>(m.n) * 8, cudaMemcpyDeviceToDevice, m.s));
+    const double inner_total = m.read(7);
+    if (res) {
+        res->outer = outer;
+        res->inner_total = static_cast<int32_t>(inner_total);
+        res->final_relres = std::sqrt(rs) / denom;
+        res->reached = res->final_relres <= tol ? 1 : 0;
+        res->ms_total = ms;
+    }
+}
+
+// exact = the lossless hybrid when the plan keeps it, else a lossless dispatched route
+int exact_route_of(const std::vector<cove_plan*>& plans) {
+    const cove_plan* P = plans.front();
+    if (P->has_route(COVE_ROUTE_HYBRID)) return COVE_ROUTE_HYBRID;
+    if (P->dispatched_route == COVE_ROUTE_DICT_U8 || P->dispatched_route == COVE_ROUTE_DICT_U16)
+        return P->dispatched_route;
+    COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "the plan holds no lossless route for the outer solve");
+}
+
+void check_mp(const std::vector<cove_plan*>& plans, int inner_route, double tol, int k_inner, int max_outer) {
+    if (plans.empty()) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "no plan");
+    for (const cove_plan* P : plans) {
+        if (P->dtype != COVE_F64) COVE_THROW(COVE_ERR_UNSUPPORTED, "the mixed-precision solvers run in fp64");
+        if (!P->has_route(inner_route)) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "the plan does not hold the inner route");
+        if (hybrid_spmv_launch_count(P->shape(), P->route_values(inner_route)) < 1 && P->nbr > 0)
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "inner route not runnable");
+    }
+    if (!(tol > 0.0) || k_inner < 1 || max_outer < 0)
+        COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "tol must be positive, k_inner >= 1, max_outer >= 0");
+}
+
 }  // namespace
 }  // namespace cove
 
 extern "C" {
+
+cove_status cove_ir_solve(const cove_plan* P, int32_t inner_route, const void* b, void* x, double tol,
+                          int32_t k_inner, int32_t max_outer, cove_ir_result* result, void* stream) {
+    return guarded([&] {
+        if (!P || !b || !x) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        if (P->rows != P->cols) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "the solvers need a square matrix");
+        MpSolver m;
+        m.plans = {const_cast<cove_plan*>(P)};
+        check_mp(m.plans, inner_route, tol, k_inner, max_outer);
+        m.n = P->rows;
+        m.wl = P->cols;
+        m.exact_route = exact_route_of(m.plans);
+        m.inner_route = inner_route;
+        m.s = static_cast<cudaStream_t>(stream);
+        mp_solve(m, false, static_cast<const double*>(b), static_cast<double*>(x), tol, k_inner, max_outer, result);
+    });
+}
+
+cove_status cove_fcg_solve(const cove_plan* P, int32_t inner_route, const void* b, void* x, double tol,
+                           int32_t k_inner, int32_t max_outer, cove_ir_result* result, void* stream) {
+    return guarded([&] {
+        if (!P || !b || !x) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        if (P->rows != P->cols) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "the solvers need a square matrix");
+        MpSolver m;
+        m.plans = {const_cast<cove_plan*>(P)};
+        check_mp(m.plans, inner_route, tol, k_inner, max_outer);
+        m.n = P->rows;
+        m.wl = P->cols;
+        m.exact_route = exact_route_of(m.plans);
+        m.inner_route = inner_route;
+        m.s = static_cast<cudaStream_t>(stream);
+        mp_solve(m, true, static_cast<const double*>(b), static_cast<double*>(x), tol, k_inner, max_outer, result);
+    });
+}
 
 cove_status cove_cg_solve(const cove_plan* P, const void* b, void* x, int32_t iters,
                           cove_cg_result* result, void* stream) {
@@ -618,6 +931,26 @@ int32_t cove_dist_spmv_launches(const cove_dist* d) {
         n += full - (k.nbr > 0 ? 1 : 0);                              // the overflow pass
     }
     return n;
+}
+
+cove_status cove_dist_mp_solve(cove_dist* d, int32_t flexible, int32_t inner_route, const void* b_local,
+                               void* x_local, double tol, int32_t k_inner, int32_t max_outer,
+                               cove_ir_result* result, void* stream) {
+    return guarded([&] {
+        if (!d || !b_local || !x_local) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
+        MpSolver m;
+        m.d = d;
+        m.plans = d->plans;
+        check_mp(m.plans, inner_route, tol, k_inner, max_outer);
+        m.n = d->row_end - d->row_begin;
+        m.p_off = d->row_begin - d->wb;
+        m.wl = d->wl;
+        m.exact_route = exact_route_of(m.plans);
+        m.inner_route = inner_route;
+        m.s = static_cast<cudaStream_t>(stream);
+        mp_solve(m, flexible != 0, static_cast<const double*>(b_local), static_cast<double*>(x_local), tol,
+                 k_inner, max_outer, result);
+    });
 }
 
 cove_status cove_dist_cg_solve(cove_dist* d, const void* b_local, void* x_local, int32_t iters,

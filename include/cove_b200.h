@@ -396,6 +396,37 @@ typedef struct {
 COVE_API cove_status cove_cg_solve(const cove_plan* plan, const void* b, void* x, int32_t iters,
                           cove_cg_result* result, void* stream);
 
+/* ---- mixed-precision solvers (bench_cg_solve.cu:280-448) --------------- */
+
+typedef struct {
+    int32_t outer;          /* outer iterations run */
+    int32_t inner_total;    /* inner CG iterations run, all outer steps */
+    double final_relres;    /* ||b - A x|| / ||b|| with the exact (lossless) route */
+    int32_t reached;        /* final_relres <= tol */
+    double ms_total;        /* device time of the solve (CUDA events) */
+} cove_ir_result;
+
+/*
+ * Iterative refinement (run_ir, bench_cg_solve.cu:280-351): x0 = 0; until
+ * ||r|| / ||b|| < tol or max_outer steps: d = k_inner steps of CG on
+ * A d = r with the plan's `inner_route` (stopping for good when p.Ap is not
+ * positive), x += d, r = b - A x with the exact route (the lossless hybrid
+ * if the plan keeps it, else its lossless dictionary route).  Single GPU;
+ * fp64 plans; b, x device vectors of length rows (rows == cols).
+ */
+COVE_API cove_status cove_ir_solve(const cove_plan* plan, int32_t inner_route, const void* b, void* x,
+                                   double tol, int32_t k_inner, int32_t max_outer,
+                                   cove_ir_result* result, void* stream);
+
+/*
+ * Flexible preconditioned CG (run_fcg, bench_cg_solve.cu:355-448): one outer
+ * CG on the exact route, preconditioned by z = (k_inner inner CG steps on
+ * `inner_route`) r, Polak-Ribiere beta = max(0, (r'.z' - r'.z) / r.z).
+ */
+COVE_API cove_status cove_fcg_solve(const cove_plan* plan, int32_t inner_route, const void* b, void* x,
+                                    double tol, int32_t k_inner, int32_t max_outer,
+                                    cove_ir_result* result, void* stream);
+
 /*
  * CG that allocates no device memory.  It has no counterpart in the
  * reference.
@@ -465,6 +496,12 @@ COVE_API cove_status cove_dist_halo(cove_dist* d, void* x_window, void* stream);
  * result->ms_spmv times the distributed SpMV (halo exchange included). */
 COVE_API cove_status cove_dist_cg_solve(cove_dist* d, const void* b_local, void* x_local, int32_t iters,
                                cove_cg_result* result, void* stream);
+
+/* The mixed-precision solvers on the partition (flexible = 0: iterative
+ * refinement, 1: flexible CG); b and x are the local row blocks. */
+COVE_API cove_status cove_dist_mp_solve(cove_dist* d, int32_t flexible, int32_t inner_route,
+                                        const void* b_local, void* x_local, double tol, int32_t k_inner,
+                                        int32_t max_outer, cove_ir_result* result, void* stream);
 
 /* Distributed SpMV: y_local = A_local x_window after the halo exchange of
  * x_window.  The exchange runs on a second stream while the block rows that
