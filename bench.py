@@ -305,6 +305,27 @@ def run_fem(args):
             e2e_ms.append((time.perf_counter() - t0) * 1e3)
 
     e2e_median = float(np.median(e2e_ms))
+    # vendor library context: cuSPARSE CSR SpMV (through torch) of the same matrix
+    vendor_ms = None
+    try:
+        A_csr = torch.sparse_csr_tensor(torch.from_numpy(rp.astype(np.int64)), torch.from_numpy(ci.astype(np.int64)),
+                                        torch.from_numpy(v), size=(rows, wl), device=dev)
+        xv = xw.view(-1, 1)
+        for _ in range(3):
+            A_csr.matmul(xv)
+        vt = []
+        for _ in range(10):
+            flush.zero_()
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record()
+            A_csr.matmul(xv)
+            c1.record()
+            torch.cuda.synchronize()
+            vt.append(c0.elapsed_time(c1))
+        vendor_ms = float(np.median(vt))
+        del A_csr
+    except Exception:
+        vendor_ms = None
     # the host link on its own: plain pinned copies of the same x and y bytes
     copy_ms = {}
     for name, dst, src in (("h2d", xd2, xh), ("d2h", yh_t, y)):
@@ -369,6 +390,7 @@ def run_fem(args):
                        "plan_build_s": round(build_s, 3), "kernel_slots": info.kernel_slots,
                        "e2e_ms_mean": round(e2e_all, 4), "e2e_ms_median_rank0": round(e2e_median, 4),
                        "host_copy_ms_rank0": {k: round(v, 4) for k, v in copy_ms.items()},
+                       "cusparse_csr_ms_rank0": round(vendor_ms, 5) if vendor_ms else None,
                        "parity_rel_vs_cpu": rel_all},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
