@@ -264,6 +264,22 @@ def _dptr(t):
     return C.c_void_p(t.data_ptr()) if t is not None else None
 
 
+def _vec(t, n, dtype, name):
+    """Device pointer of a contiguous CUDA vector of at least n `dtype` entries;
+    the C ABI takes bare pointers, so a wrong element type would be read as
+    the plan's type."""
+    import torch
+
+    want = torch.float64 if dtype == np.float64 else torch.float32
+    if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+        raise CoveError(1, f"{name} must be a CUDA tensor")
+    if t.dtype != want:
+        raise CoveError(1, f"{name} is {t.dtype}, the plan computes in {want}")
+    if not t.is_contiguous() or t.numel() < n:
+        raise CoveError(1, f"{name} must be contiguous with at least {n} entries")
+    return C.c_void_p(t.data_ptr())
+
+
 def default_opts(**kw) -> PlanOpts:
     o = PlanOpts()
     lib().cove_plan_opts_default(C.byref(o))
@@ -375,10 +391,12 @@ class Plan:
 
     def spmv(self, x, y, route=None, stream=None):
         """y = A x on device tensors (dispatched route unless `route` given)."""
+        xp = _vec(x, self.info.cols, self.dtype, "x")
+        yp = _vec(y, self.info.rows, self.dtype, "y")
         if route is None:
-            check(lib().cove_spmv(self._h, _dptr(x), _dptr(y), _stream_handle(stream)))
+            check(lib().cove_spmv(self._h, xp, yp, _stream_handle(stream)))
         else:
-            check(lib().cove_spmv_route(self._h, route, _dptr(x), _dptr(y), _stream_handle(stream)))
+            check(lib().cove_spmv_route(self._h, route, xp, yp, _stream_handle(stream)))
         return y
 
     def spmv_host(self, x_host: np.ndarray, y_host: np.ndarray | None = None, stream=None):
@@ -399,14 +417,16 @@ class Plan:
         """Mixed-precision iterative refinement (flexible=False) or flexible CG."""
         res = IrResult()
         fn = lib().cove_fcg_solve if flexible else lib().cove_ir_solve
-        check(fn(self._h, inner_route, _dptr(b), _dptr(x), tol, k_inner, max_outer, C.byref(res),
-                 _stream_handle(stream)))
+        n = self.info.rows
+        check(fn(self._h, inner_route, _vec(b, n, self.dtype, "b"), _vec(x, n, self.dtype, "x"), tol,
+                 k_inner, max_outer, C.byref(res), _stream_handle(stream)))
         return res
 
     def cg(self, b, x, iters, stream=None) -> CgResult:
         res = CgResult()
-        check(lib().cove_cg_solve(self._h, _dptr(b), _dptr(x), iters, C.byref(res),
-                                  _stream_handle(stream)))
+        n = self.info.rows
+        check(lib().cove_cg_solve(self._h, _vec(b, n, self.dtype, "b"), _vec(x, n, self.dtype, "x"),
+                                  iters, C.byref(res), _stream_handle(stream)))
         return res
 
 

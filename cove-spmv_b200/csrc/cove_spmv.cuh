@@ -56,8 +56,23 @@ int launch_hybrid_spmv(const KernelShape& k, const RouteValues& v, const void* x
                        cudaStream_t s);
 int hybrid_spmv_launch_count(const KernelShape& k, const RouteValues& v);
 
+// Residual rows as a lane-per-row launch would see them: entries of the rows
+// of at most kProfileTau entries (`light_nnz`), those of them whose column
+// lies 0-2 columns right of the same-position entry of the next row
+// (`diag_nnz`: neighbouring lanes then read neighbouring x), and the number of
+// longer rows (`heavy_rows`), which that launch hands to warp chunks.
+constexpr int kProfileTau = 32;
+constexpr int kProfileHeavyAvg = 128;  // mean heavy-row length at which warp chunks pay
+struct ResidualProfile {
+    int64_t light_nnz = 0, diag_nnz = 0, heavy_rows = 0;
+};
+
 // Choose lanes per block row from the average kept blocks per block row and
-// residual entries per row; 0 selects the lane-per-row kernel (short rows).
-int choose_slots(int64_t nbr, int64_t kept_blocks, int64_t rows, int64_t residual_nnz);
+// residual entries per row; 0 selects the lane-per-row kernel.  With a
+// profile, one lane per row is taken for few kept blocks when the light rows
+// are short (or short-ish and diagonal) and the heavy rows, if they matter,
+// are long; without one, only for short residual rows throughout.
+int choose_slots(int64_t nbr, int64_t kept_blocks, int64_t rows, int64_t residual_nnz,
+                 const ResidualProfile* prof = nullptr);
 
 }  // namespace cove

@@ -26,6 +26,61 @@ __global__ void heavy_count_kernel(int32_t nbr, const int32_t* __restrict__ kbrp
     out[br] = c > limit ? (c - limit + piece - 1) / piece : 0;
 }
 
+// ResidualProfile counts (grid-stride over rows, warp sums, three atomics a warp).
+__global__ void residual_profile_kernel(int32_t rows, const int32_t* __restrict__ rp,
+                                        const int32_t* __restrict__ ci,
+                                        unsigned long long* __restrict__ out) {
+    unsigned long long light = 0, diag = 0, heavy = 0;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < rows; r += stride) {
+        const int32_t b = rp[r], nb = rp[r + 1];
+        const int32_t len = nb - b;
+        if (len > kProfileTau) {
+            ++heavy;
+            continue;
+        }
+        light += static_cast<unsigned long long>(len);
+        if (r + 1 < rows) {
+            const int32_t m = min(len, rp[r + 2] - nb);
+            for (int32_t k = 0; k < m; ++k) {
+                const int32_t d = ci[nb + k] - ci[b + k];
+                diag += (d >= 0 && d <= 2) ? 1ull : 0ull;
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        light += __shfl_xor_sync(0xffffffffu, light, o);
+        diag += __shfl_xor_sync(0xffffffffu, diag, o);
+        heavy += __shfl_xor_sync(0xffffffffu, heavy, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        atomicAdd(out, light);
+        atomicAdd(out + 1, diag);
+        atomicAdd(out + 2, heavy);
+    }
+}
+
+ResidualProfile residual_profile(const SplitParts& sp, int32_t rows, cudaStream_t s) {
+    ResidualProfile p;
+    if (rows <= 0) return p;
+    DevBuf acc;
+    alloc_n<unsigned long long>(acc, 3);
+    CUDA_OK(cudaMemsetAsync(acc.p, 0, 3 * sizeof(unsigned long long), s));
+    const int grid = static_cast<int>(std::min<int64_t>(grid_for(rows, kThreads), 148 * 8));
+    residual_profile_kernel<<<grid, kThreads, 0, s>>>(rows, sp.res_row_ptr.as<int32_t>(),
+                                                      sp.res_col.as<int32_t>(),
+                                                      acc.as<unsigned long long>());
+    CUDA_LAUNCH_OK();
+    unsigned long long h[3];
+    CUDA_OK(cudaMemcpyAsync(h, acc.p, sizeof(h), cudaMemcpyDeviceToHost, s));
+    CUDA_OK(cudaStreamSynchronize(s));
+    p.light_nnz = static_cast<int64_t>(h[0]);
+    p.diag_nnz = static_cast<int64_t>(h[1]);
+    p.heavy_rows = static_cast<int64_t>(h[2]);
+    return p;
+}
+
 __global__ void heavy_fill_kernel(int32_t nbr, const int32_t* __restrict__ kbrp, int limit,
                                   int piece, const int64_t* __restrict__ off,
                                   int32_t* __restrict__ hbr, int32_t* __restrict__ hb0,
@@ -323,7 +378,8 @@ void build_plan_typed(cove_plan* P, const cove_csr_desc& d, cudaStream_t s) {
                  P->chunks, s);
 
     // kernel work split
-    P->slots = choose_slots(P->nbr, P->sp.kept_blocks, P->rows, P->sp.residual_nnz);
+    const ResidualProfile prof = residual_profile(P->sp, P->rows, s);
+    P->slots = choose_slots(P->nbr, P->sp.kept_blocks, P->rows, P->sp.residual_nnz, &prof);
     const double avg_blocks = P->nbr > 0 ? static_cast<double>(P->sp.kept_blocks) / P->nbr : 0.0;
     // a block row's blocks beyond the limit go to 256-block overflow pieces;
     // a lane-per-row launch walks blocks serially, so its limit is lower

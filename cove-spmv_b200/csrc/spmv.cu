@@ -673,11 +673,23 @@ int hybrid_spmv_launch_count(const KernelShape& k, const RouteValues& v) {
     return n;
 }
 
-int choose_slots(int64_t nbr, int64_t kept_blocks, int64_t rows, int64_t residual_nnz) {
+int choose_slots(int64_t nbr, int64_t kept_blocks, int64_t rows, int64_t residual_nnz,
+                 const ResidualProfile* prof) {
     const double kb = nbr > 0 ? static_cast<double>(kept_blocks) / static_cast<double>(nbr) : 0.0;
     const double rr = rows > 0 ? static_cast<double>(residual_nnz) / static_cast<double>(rows) : 0.0;
     if (kb >= 8.0) return 4;
-    if (kb < 6.0 && rr < 6.0) return 0;
+    if (prof == nullptr) {
+        if (kb < 6.0 && rr < 6.0) return 0;
+    } else if (kb < 6.0 && rows > 0) {
+        // one lane per row: its light rows stay in the lanes, the longer rows go
+        // to warp chunks, which pay only when those rows are long
+        const int64_t heavy_nnz = residual_nnz - prof->light_nnz;
+        const bool heavy_ok = heavy_nnz * 10 <= residual_nnz ||
+                              heavy_nnz >= static_cast<int64_t>(kProfileHeavyAvg) * prof->heavy_rows;
+        const double lr = static_cast<double>(prof->light_nnz) / static_cast<double>(rows);
+        const bool diagonal = prof->diag_nnz * 2 >= prof->light_nnz;
+        if (heavy_ok && (lr < 12.0 || (diagonal && lr < 24.0))) return 0;
+    }
     if (rr >= 24.0) return 4;
     if (kb >= 1.5 || rr >= 2.5) return 2;
     return 1;

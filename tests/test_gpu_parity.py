@@ -242,7 +242,7 @@ def test_routes_spmv_and_gate(ref_cases, codec):
 
 @pytest.mark.parametrize("codec", ["auto", "bfp8", "bfp8_outlier"])
 def test_blocksparse_outlier_config_scaled(codec):
-    """Config 4's matrix family at n = 2^16 (same block / entry densities,
+    """The block-sparse outlier matrix family at n = 2^16 (same block / entry densities,
     bf16-representable values in [-8, 8] with 0.1 % outliers of 1e5-1e6):
     position and value streams bit-exact, route choice and gate as the
     oracle decides them, and the dispatched SpMV within its route's bound."""
@@ -398,6 +398,63 @@ def test_lane_per_row_kernel_with_overflow_pieces():
     assert np.abs(y - ref).max() <= 1e-12 * np.abs(ref).max()
 
 
+def _slot_matrix(kind):
+    import scipy.sparse as sp
+
+    rng = np.random.default_rng(21)
+    n = 1 << 16
+    if kind.startswith("random"):  # k random columns a row, no 8x4 structure
+        k = int(kind[6:])
+        rows = np.repeat(np.arange(n), k)
+        A = sp.csr_matrix((rng.uniform(-1, 1, n * k), (rows, rng.integers(0, n, n * k))), shape=(n, n))
+    elif kind == "banded":  # 24 scattered diagonals: neighbouring rows read neighbouring x
+        offs = [0, 1, -1, 3, -3, 7, -7, 9, -9, 20, -20, 33, -33, 64, -64, 77, 200, -200, 513, -513,
+                1000, -1000, 4096, -4096]
+        A = sp.diags([rng.uniform(-1, 1, n - abs(o)) for o in offs], offs, shape=(n, n), format="csr")
+    else:  # power law: 400 rows of 400 entries hold most of the residual, the rest 2 a row
+        heavy = rng.choice(n, 400, replace=False)
+        lens = np.full(n, 2)
+        lens[heavy] = 400
+        rows = np.repeat(np.arange(n), lens)
+        A = sp.csr_matrix((rng.uniform(-1, 1, rows.size), (rows, rng.integers(0, n, rows.size))), shape=(n, n))
+    A.sum_duplicates()
+    A.sort_indices()
+    return A
+
+
+@pytest.mark.parametrize("kind,slots", [("random8", 0), ("banded", 0), ("powerlaw", 0), ("random16", 2),
+                                        ("random40", 4)])
+def test_slot_rule_from_residual_profile(kind, slots):
+    """The kernel choice follows the residual rows' shape: short light rows, a
+    diagonal structure or long heavy rows take one lane per row; longer
+    random rows take 2 or 4 lanes per block row.  Every choice stays exact."""
+    A = _slot_matrix(kind)
+    n = A.shape[0]
+    p = plan_for(n, n, A.indptr.astype(np.int64), A.indices.astype(np.int32), A.data,
+                 value_codec="original", gate_enable=0)
+    assert p.info.kernel_slots == slots
+    x = cb.synth_vector("uniform_pm1", n, seed=3)
+    y = gpu_spmv(p, x)
+    ref = A @ x
+    assert np.abs(y - ref).max() <= 1e-12 * np.abs(ref).max()
+
+
+def test_spmv_rejects_mismatched_vectors():
+    """The C ABI takes bare pointers; the Python plan checks element type,
+    device and length before the call."""
+    import torch
+
+    rows, cols, rp, ci, v = cb.synth_lapl2d(32, 32)
+    p = plan_for(rows, cols, rp, ci, v.astype(np.float32), value_codec="original")
+    y = torch.zeros(rows, dtype=torch.float32, device="cuda")
+    with pytest.raises(cb.CoveError, match="plan computes in"):
+        p.spmv(torch.zeros(cols, dtype=torch.float64, device="cuda"), y)
+    with pytest.raises(cb.CoveError, match="at least"):
+        p.spmv(torch.zeros(cols - 1, dtype=torch.float32, device="cuda"), y)
+    with pytest.raises(cb.CoveError, match="CUDA tensor"):
+        p.spmv(torch.zeros(cols, dtype=torch.float32), y)
+
+
 def test_spmv_host_matches_device():
     rows, cols, rp, ci, v = cb.synth_fem27(12, 10, 9, 3, seed=5)
     p = plan_for(rows, cols, rp, ci, v, value_codec="auto")
@@ -445,7 +502,8 @@ def test_spmv_host_sliced_overlap_matches_device(long_row):
 
 @pytest.mark.parametrize("cfg", ["lapl2d_512", "fem27_64", "rmat_22"])
 def test_full_size_configs(cfg):
-    """BASELINE configs 1-3 at full size: streams bit-exact, routes, SpMV."""
+    """2D Laplacian 512^2, FEM 27-point 64^3 and R-MAT 2^22 at full size:
+    streams bit-exact, routes, SpMV."""
     rows, cols, rp, ci, v, x = cb.workload(cfg)
     opts = dict(value_codec="auto", long_row_split=256)
     p = plan_for(rows, cols, rp, ci, v, **opts)
