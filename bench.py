@@ -13,6 +13,9 @@ x-halo exchange (one node plane to each neighbour) followed by the local
 SpMV.  `value` is the whole-job GFLOP/s (2 nnz_total / t).
 
 --workload lapl3d_cg runs the 3D 7-point Laplacian CG (strong scaling).
+--workload lapl2d_512 / rmat_22 run those single matrices (2D 5-point
+Laplacian 512^2 fp64; R-MAT 2^22 nodes fp32, x ~ U[0,1)) through the same
+step; with N > 1 every rank runs its own replica (no collective).
 
 Timing: W warm-up steps, then K steps bracketed by barrier + synchronize;
 each step's SpMV is timed with CUDA events on the launching stream and the
@@ -144,12 +147,17 @@ def run_reference_arm(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    part = fem_partition(0, 1)
     import cove_b200 as cb
 
-    rows, n, rp, ci, v = cb.synth_fem27_rows(part["nx"], part["ny"], part["nz"], part["dof"],
-                                             FEM["seed"], part["row_begin"], part["row_end"], 0)
-    x = cb.synth_vector("uniform_pm1", n, seed=FEM["seed"])
+    if args.workload in ("lapl2d_512", "rmat_22"):
+        rows, n, rp, ci, v, x = cb.workload(args.workload)
+        wname = f"{args.workload} (rows={rows}, nnz={ci.size})"
+    else:
+        part = fem_partition(0, 1)
+        rows, n, rp, ci, v = cb.synth_fem27_rows(part["nx"], part["ny"], part["nz"], part["dof"],
+                                                 FEM["seed"], part["row_begin"], part["row_end"], 0)
+        x = cb.synth_vector("uniform_pm1", n, seed=FEM["seed"])
+        wname = "fem27_64^3x3 (n=786432, nnz=61731000)"
     nnz = int(ci.size)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
@@ -178,12 +186,11 @@ def run_reference_arm(args):
         "impl": "reference", "metric": "spmv_gflops", "value": round(gflops, 3),
         "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "fem27_64^3x3 (n=786432, nnz=61731000)",
-                   "sample": "one full SpMV of the 1-GPU slab per step"},
+        "vs_baseline": None, "dtype": "f64" if v.dtype == np.float64 else "f32", "data": "synthetic",
+        "config": {"workload": wname, "sample": "one full SpMV of the 1-GPU matrix per step"},
         "cpu_baseline": {"value": round(gflops, 3), "unit": "GFLOP/s", "cores": cores,
                          "kind": kind,
-                         "sample": "structural::spmv_csr on the fem27 64^3x3 matrix, one SpMV per step"},
+                         "sample": f"structural::spmv_csr on {wname}, one SpMV per step"},
         "e2e": {"value": round(gflops, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -204,13 +211,20 @@ def run_fem(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    part = fem_partition(rank, world)
-    rows, n, rp, ci, v = cb.synth_fem27_rows(part["nx"], part["ny"], part["nz"], part["dof"],
-                                             FEM["seed"], part["row_begin"], part["row_end"],
-                                             part["window_begin"])
-    wl = part["window_len"]
-    xg = cb.synth_vector("uniform_pm1", n, seed=FEM["seed"])
-    x_window = xg[part["window_begin"]: part["window_begin"] + wl].copy()
+    fem = args.workload == "fem27"
+    if fem:
+        part = fem_partition(rank, world)
+        rows, n, rp, ci, v = cb.synth_fem27_rows(part["nx"], part["ny"], part["nz"], part["dof"],
+                                                 FEM["seed"], part["row_begin"], part["row_end"],
+                                                 part["window_begin"])
+        wl = part["window_len"]
+        xg = cb.synth_vector("uniform_pm1", n, seed=FEM["seed"])
+        x_window = xg[part["window_begin"]: part["window_begin"] + wl].copy()
+    else:  # one named matrix, a replica per rank
+        rows, n, rp, ci, v, x_window = cb.workload(args.workload)
+        wl = n
+    vt = torch.float64 if v.dtype == np.float64 else torch.float32
+    esz = v.itemsize
     csr = cb.DeviceCsr.from_numpy(rows, wl, rp, ci, v, device=dev)
     t0 = time.perf_counter()
     plan = cb.Plan(csr, value_codec=args.codec, long_row_split=256)
@@ -222,9 +236,9 @@ def run_fem(args):
 
     stream = torch.cuda.current_stream()
     xw = torch.from_numpy(x_window).to(dev)
-    y = torch.empty(rows, dtype=torch.float64, device=dev)
+    y = torch.empty(rows, dtype=vt, device=dev)
     D = None
-    if world > 1:
+    if world > 1 and fem:
         import ctypes as C
 
         idb = cb.lib().cove_dist_id_bytes()
@@ -286,8 +300,8 @@ def run_fem(args):
 
     # end to end through the public C ABI with host buffers (pinned)
     xh = torch.from_numpy(x_window).pin_memory()
-    yh_t = torch.empty(rows, dtype=torch.float64).pin_memory()
-    xd2 = torch.empty(wl, dtype=torch.float64, device=dev)
+    yh_t = torch.empty(rows, dtype=vt).pin_memory()
+    xd2 = torch.empty(wl, dtype=vt, device=dev)
     e2e_ms = []
     for i in range(args.warmup + args.steps):
         torch.cuda.synchronize()
@@ -363,7 +377,7 @@ def run_fem(args):
             try:
                 with open(prof) as f:
                     t = json.load(f)
-                traffic = t.get("fem27_64", {}).get(cb.ROUTE_NAMES[route])
+                traffic = t.get("fem27_64" if fem else args.workload, {}).get(cb.ROUTE_NAMES[route])
             except Exception:
                 traffic = None
         # the reference's CPU SpMV on the same matrix, bounded sample
@@ -377,16 +391,21 @@ def run_fem(args):
             "metric": "spmv_gflops", "value": round(gflops, 3), "unit": "GFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_all, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f64" if route in (0, 1, 2) else "f32 accumulate, f64 in/out",
+            "vs_baseline": None,
+            "dtype": ("f64" if esz == 8 else "f32") if route in (0, 1, 2)
+                     else f"f32 accumulate, {'f64' if esz == 8 else 'f32'} in/out",
             "data": "synthetic",
-            "config": {"workload": f"fem27 {FEM['nx']}x{FEM['ny']}x{FEM['nz'] * world} nodes x3 dof"
-                                   f" ({'z-slab per rank, ' if world > 1 else ''}nnz={int(nnz_total)})",
+            "config": {"workload": (f"fem27 {FEM['nx']}x{FEM['ny']}x{FEM['nz'] * world} nodes x3 dof"
+                                    f" ({'z-slab per rank, ' if world > 1 else ''}nnz={int(nnz_total)})")
+                                   if fem else f"{args.workload} (rows={rows}, nnz={nnz_local}"
+                                               f"{', a replica per rank' if world > 1 else ''})",
                        "route": cb.ROUTE_NAMES[route], "requested_codec": args.codec,
                        "dispatched_route": cb.ROUTE_NAMES[info.dispatched_route],
                        "joint_route": cb.ROUTE_NAMES[info.joint_route],
                        "gate_rel_err": info.joint_rel_err, "gate_pass": bool(info.gate_pass),
                        "l2": "flushed between steps (256 MiB write, outside the timed events)",
-                       "parallelism": f"row-block z-slabs x{world}, NCCL halo" if world > 1 else "1 GPU",
+                       "parallelism": ("1 GPU" if world == 1 else f"row-block z-slabs x{world}, NCCL halo"
+                                       if fem else f"{world} independent replicas"),
                        "plan_build_s": round(build_s, 3), "kernel_slots": info.kernel_slots,
                        "e2e_ms_mean": round(e2e_all, 4), "e2e_ms_median_rank0": round(e2e_median, 4),
                        "host_copy_ms_rank0": {k: round(v, 4) for k, v in copy_ms.items()},
@@ -397,7 +416,7 @@ def run_fem(args):
                          "algorithmic_bytes": alg_bytes, "traffic": traffic},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gflops, 3), "unit": "GFLOP/s",
-                    "h2d_bytes_per_step": wl * 8, "d2h_bytes_per_step": rows * 8},
+                    "h2d_bytes_per_step": wl * esz, "d2h_bytes_per_step": rows * esz},
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
         }
@@ -551,7 +570,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="fem27", choices=["fem27", "lapl3d_cg"])
+    ap.add_argument("--workload", default="fem27", choices=["fem27", "lapl3d_cg", "lapl2d_512", "rmat_22"])
     ap.add_argument("--grid", type=int, default=0, help="lapl3d_cg: grid edge (default 768)")
     ap.add_argument("--cg-iters", type=int, default=50)
     ap.add_argument("--codec", default="auto")

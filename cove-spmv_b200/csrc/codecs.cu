@@ -191,6 +191,9 @@ __global__ void dict_insert_kernel(int64_t nk, int64_t n, const T* __restrict__ 
             return;
         }
         if (cur == 0ULL) {
+            // past the limit the answer is "too many values": stop claiming slots,
+            // or the threads in flight would fill the table and probe all of it
+            if (*overflow) return;
             const unsigned long long prev = atomicCAS(&keys[h], 0ULL, static_cast<unsigned long long>(key));
             if (prev == 0ULL) {
                 const unsigned int c = atomicAdd(count, 1u);
@@ -203,6 +206,7 @@ __global__ void dict_insert_kernel(int64_t nk, int64_t n, const T* __restrict__ 
                 return;
             }
         }
+        if ((probe & 63) == 63 && *overflow) return;
         h = (h + 1) & (kTableSize - 1);
     }
     *overflow = 1;

@@ -32,34 +32,96 @@ __device__ __forceinline__ unsigned group_mask(int lane) { return 0xFFu << (lane
 
 // ---------------------------------------------------------------------------
 // validation: monotonic row_ptr, columns in range, strictly increasing
-// columns among the nonzero entries of each row
+// columns among the nonzero entries of each row.  Error bits: 1 row_ptr,
+// 2 column range, 4 column order; the host reports them in that priority,
+// the reference's order (csr.hpp:23-49 checks every row_ptr step, then every
+// column's range; the converter then meets duplicates, convert.hpp:145-149).
+// Bit 8 is no error: some row's columns decrease across a stored zero, so
+// the converter may not binary-search rows for column ranges.
 // ---------------------------------------------------------------------------
 
+constexpr int kValidateLong = 256;  // longer rows are cut into units of kValidateSeg entries
+constexpr int kValidateSeg = 2048;
+
 template <typename T, typename RP>
-__global__ void validate_csr_kernel(int32_t rows, int32_t cols, const RP* __restrict__ rp,
+__global__ void validate_csr_kernel(int32_t rows, int32_t cols, int64_t nnz, const RP* __restrict__ rp,
                                     const int32_t* __restrict__ ci, const T* __restrict__ v,
-                                    int* __restrict__ err) {
+                                    int* __restrict__ err, int32_t* __restrict__ unit_row,
+                                    int32_t* __restrict__ unit_seg, int64_t unit_cap,
+                                    unsigned long long* __restrict__ n_units) {
     const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     const int64_t b = static_cast<int64_t>(rp[r]);
     const int64_t e = static_cast<int64_t>(rp[r + 1]);
-    if (b > e) {
+    // rp[0] = 0 and rp[rows] = nnz are checked on the host, so an offset
+    // outside [0, nnz] means row_ptr is not monotonic
+    if (b > e || b < 0 || e > nnz) {
         atomicOr(err, 1);
         return;
     }
+    if (e - b > kValidateLong) {
+        // with monotonic offsets the units number at most
+        // nnz / kValidateSeg + nnz / kValidateLong; more means another row
+        // fails the check above
+        const int64_t nseg = (e - b + kValidateSeg - 1) / kValidateSeg;
+        const int64_t k0 = static_cast<int64_t>(atomicAdd(n_units, static_cast<unsigned long long>(nseg)));
+        for (int64_t k = 0; k < nseg && k0 + k < unit_cap; ++k) {
+            unit_row[k0 + k] = static_cast<int32_t>(r);
+            unit_seg[k0 + k] = static_cast<int32_t>(k);
+        }
+        return;
+    }
     int prev = -1;
+    int prev_any = INT_MIN;
+    int bits = 0;
     for (int64_t p = b; p < e; ++p) {
         const int c = ci[p];
         if (c < 0 || c >= cols) {
-            atomicOr(err, 2);
-            return;
+            bits |= 2;
+            break;
         }
+        if (c < prev_any) bits |= 8;
+        prev_any = c;
         if (is_zero(v[p])) continue;
-        if (c <= prev) {
-            atomicOr(err, 4);
-            return;
-        }
+        if (c <= prev) bits |= 4;
         prev = c;
+    }
+    if (bits) atomicOr(err, bits);
+}
+
+// One warp per unit (kValidateSeg entries of a long row), a lane per entry:
+// each entry is checked against the entry before it and, if nonzero, against
+// the previous nonzero entry of the row (found by walking back over zeros;
+// the walks of a row add up to at most its zero count).
+template <typename T, typename RP>
+__global__ void validate_long_rows_kernel(int32_t cols, const RP* __restrict__ rp,
+                                          const int32_t* __restrict__ ci, const T* __restrict__ v,
+                                          const int32_t* __restrict__ unit_row,
+                                          const int32_t* __restrict__ unit_seg, int64_t unit_cap,
+                                          const unsigned long long* __restrict__ n_units,
+                                          int* __restrict__ err) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    const int64_t nu = min(static_cast<int64_t>(*n_units), unit_cap);
+    for (int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < nu; u += nw) {
+        const int32_t r = unit_row[u];
+        const int64_t rb = static_cast<int64_t>(rp[r]);
+        const int64_t re = static_cast<int64_t>(rp[r + 1]);
+        const int64_t b = rb + static_cast<int64_t>(unit_seg[u]) * kValidateSeg;
+        const int64_t e = b + kValidateSeg < re ? b + kValidateSeg : re;
+        int bits = 0;
+        for (int64_t p = b + lane; p < e; p += 32) {
+            const int c = ci[p];
+            if (c < 0 || c >= cols) bits |= 2;
+            if (p > rb && c < ci[p - 1]) bits |= 8;
+            if (!is_zero(v[p])) {
+                int64_t q = p - 1;
+                while (q >= rb && is_zero(v[q])) --q;
+                if (q >= rb && c <= ci[q]) bits |= 4;
+            }
+        }
+        bits = __reduce_or_sync(0xffffffffu, bits);
+        if (lane == 0 && bits) atomicOr(err, bits);
     }
 }
 
@@ -75,21 +137,110 @@ struct RowCursor {
     }
 };
 
+// Pieces: a block row with more than kPieceEntries CSR entries is cut into
+// column ranges [c0, c1) on block boundaries, taken from its longest row at
+// evenly spaced positions, and each piece is walked by its own 8-lane group
+// (a single group over an R-MAT hub row would walk ~10^5 blocks serially).
+// The ranges need every row's columns non-decreasing, stored zeros included;
+// otherwise each block row is one piece.
+constexpr int kPieceEntries = 1024;
+
+template <typename RP>
+__global__ void piece_count_kernel(int32_t rows, int32_t nbr, const RP* __restrict__ rp, int split,
+                                   int32_t* __restrict__ np) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (br >= nbr) return;
+    const int64_t r0 = br * kBlockRows;
+    const int64_t r1 = r0 + kBlockRows < rows ? r0 + kBlockRows : rows;
+    const int64_t e = static_cast<int64_t>(rp[r1]) - static_cast<int64_t>(rp[r0]);
+    np[br] = (split && e > kPieceEntries) ? static_cast<int32_t>((e + kPieceEntries - 1) / kPieceEntries) : 1;
+}
+
+template <typename RP>
+__global__ void piece_bounds_kernel(int32_t rows, int32_t nbr, const RP* __restrict__ rp,
+                                    const int32_t* __restrict__ ci, const int64_t* __restrict__ first,
+                                    int32_t* __restrict__ pbr, int32_t* __restrict__ pc0,
+                                    int32_t* __restrict__ pc1) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (br >= nbr) return;
+    const int64_t o = first[br];
+    const int64_t n = first[br + 1] - o;
+    if (n == 1) {
+        pbr[o] = static_cast<int32_t>(br);
+        pc0[o] = 0;
+        pc1[o] = INT_MAX;
+        return;
+    }
+    const int64_t r0 = br * kBlockRows;
+    const int64_t r1 = r0 + kBlockRows < rows ? r0 + kBlockRows : rows;
+    int64_t lb = 0, len = -1;
+    for (int64_t r = r0; r < r1; ++r) {
+        const int64_t b = static_cast<int64_t>(rp[r]);
+        const int64_t l = static_cast<int64_t>(rp[r + 1]) - b;
+        if (l > len) {
+            len = l;
+            lb = b;
+        }
+    }
+    // n <= ceil(8 len / kPieceEntries) <= len, so every sampled position is in the row
+    int32_t prev = 0;
+    for (int64_t k = 0; k < n; ++k) {
+        int32_t end = INT_MAX;
+        if (k + 1 < n) {
+            end = ci[lb + (k + 1) * len / n] & ~(kBlockCols - 1);
+            if (end < prev) end = prev;
+        }
+        pbr[o + k] = static_cast<int32_t>(br);
+        pc0[o + k] = prev;
+        pc1[o + k] = end;
+        prev = end;
+    }
+}
+
+// First position in [lo, hi) whose column is >= c (columns non-decreasing).
+__device__ __forceinline__ int64_t lower_bound_col(const int32_t* __restrict__ ci, int64_t lo, int64_t hi,
+                                                   int32_t c) {
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (ci[mid] < c) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// This lane's CSR range inside piece j (its row of the piece's block row).
+template <typename RP>
+__device__ __forceinline__ void piece_row_range(int32_t rows, const RP* __restrict__ rp,
+                                                const int32_t* __restrict__ ci, int32_t br, int32_t c0,
+                                                int32_t c1, int l8, int64_t* b, int64_t* e) {
+    const int64_t row = static_cast<int64_t>(br) * kBlockRows + l8;
+    int64_t lo = 0, hi = 0;
+    if (row < rows) {
+        lo = static_cast<int64_t>(rp[row]);
+        hi = static_cast<int64_t>(rp[row + 1]);
+        if (c0 > 0) lo = lower_bound_col(ci, lo, hi, c0);
+        if (c1 != INT_MAX) hi = lower_bound_col(ci, lo, hi, c1);
+    }
+    *b = lo;
+    *e = hi;
+}
+
 template <typename T, typename RP>
-__global__ void full_count_kernel(int32_t rows, int32_t nbr, const RP* __restrict__ rp,
+__global__ void full_count_kernel(int32_t rows, int64_t npieces, const RP* __restrict__ rp,
                                   const int32_t* __restrict__ ci, const T* __restrict__ v,
+                                  const int32_t* __restrict__ pbr, const int32_t* __restrict__ pc0,
+                                  const int32_t* __restrict__ pc1,
                                   int32_t* __restrict__ block_counts,
                                   int32_t* __restrict__ nnz_counts) {
     const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int64_t br = gt >> 3;
+    const int64_t j = gt >> 3;
     const int lane = threadIdx.x & 31;
     const int l8 = lane & 7;
     const unsigned gm = group_mask(lane);
-    if (br >= nbr) return;  // whole group leaves together
-    const int64_t row = br * kBlockRows + l8;
-    const bool active = row < rows;
-    RowCursor<T, RP> cur{active ? static_cast<int64_t>(rp[row]) : 0,
-                         active ? static_cast<int64_t>(rp[row + 1]) : 0};
+    if (j >= npieces) return;  // whole group leaves together
+    int64_t b, e;
+    piece_row_range(rows, rp, ci, pbr[j], pc0[j], pc1[j], l8, &b, &e);
+    RowCursor<T, RP> cur{b, e};
     cur.skip_zeros(v);
     int nblocks = 0;
     int nnz = 0;
@@ -106,31 +257,32 @@ __global__ void full_count_kernel(int32_t rows, int32_t nbr, const RP* __restric
     }
     const int total = __reduce_add_sync(gm, nnz);
     if (l8 == 0) {
-        block_counts[br] = nblocks;
-        nnz_counts[br] = total;
+        block_counts[j] = nblocks;
+        nnz_counts[j] = total;
     }
 }
 
 template <typename T, typename RP>
-__global__ void full_fill_kernel(int32_t rows, int32_t nbr, const RP* __restrict__ rp,
+__global__ void full_fill_kernel(int32_t rows, int64_t npieces, const RP* __restrict__ rp,
                                  const int32_t* __restrict__ ci, const T* __restrict__ v,
-                                 const int32_t* __restrict__ block_row_ptr,
-                                 const int32_t* __restrict__ block_row_val_ptr,
+                                 const int32_t* __restrict__ pbr, const int32_t* __restrict__ pc0,
+                                 const int32_t* __restrict__ pc1,
+                                 const int32_t* __restrict__ piece_block_off,
+                                 const int32_t* __restrict__ piece_val_off,
                                  int32_t* __restrict__ block_col_idx,
                                  uint32_t* __restrict__ bitmap, T* __restrict__ values) {
     const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int64_t br = gt >> 3;
+    const int64_t j = gt >> 3;
     const int lane = threadIdx.x & 31;
     const int l8 = lane & 7;
     const unsigned gm = group_mask(lane);
-    if (br >= nbr) return;
-    const int64_t row = br * kBlockRows + l8;
-    const bool active = row < rows;
-    RowCursor<T, RP> cur{active ? static_cast<int64_t>(rp[row]) : 0,
-                         active ? static_cast<int64_t>(rp[row + 1]) : 0};
+    if (j >= npieces) return;
+    int64_t b, e;
+    piece_row_range(rows, rp, ci, pbr[j], pc0[j], pc1[j], l8, &b, &e);
+    RowCursor<T, RP> cur{b, e};
     cur.skip_zeros(v);
-    int64_t block_id = block_row_ptr[br];
-    int64_t value_pos = block_row_val_ptr[br];
+    int64_t block_id = piece_block_off[j];
+    int64_t value_pos = piece_val_off[j];
     while (true) {
         const int cand = cur.pos < cur.end ? (ci[cur.pos] >> 2) : INT_MAX;
         const int bc = __reduce_min_sync(gm, cand);
@@ -446,7 +598,7 @@ int32_t checked_i32(int64_t v, const char* what) {
 // ---------------------------------------------------------------------------
 
 template <typename T>
-void validate_csr(const cove_csr_desc& d, cudaStream_t s) {
+bool validate_csr(const cove_csr_desc& d, cudaStream_t s) {
     if (d.rows < 0 || d.cols < 0 || d.nnz < 0) {
         COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "CSR dimensions must be non-negative");
     }
@@ -472,17 +624,35 @@ void validate_csr(const cove_csr_desc& d, cudaStream_t s) {
     }
     if (first != 0) COVE_THROW(COVE_ERR_INVALID_INPUT, "CSR row_ptr must start at zero");
     if (last != d.nnz) COVE_THROW(COVE_ERR_INVALID_INPUT, "CSR row_ptr.back must equal nnz");
-    if (d.rows == 0) return;
-    DevBuf err;
+    if (d.rows == 0) return true;
+    DevBuf err, units, urow, useg;
     err.alloc(sizeof(int));
+    alloc_n<unsigned long long>(units, 1);
+    const int64_t unit_cap = d.nnz / kValidateSeg + d.nnz / kValidateLong + 1;
+    alloc_n<int32_t>(urow, unit_cap);
+    alloc_n<int32_t>(useg, unit_cap);
     CUDA_OK(cudaMemsetAsync(err.p, 0, sizeof(int), s));
+    CUDA_OK(cudaMemsetAsync(units.p, 0, sizeof(unsigned long long), s));
     const T* v = static_cast<const T*>(d.values);
+    const int long_grid = 148 * 8;
     if (d.row_ptr_i32) {
+        const int32_t* rp = static_cast<const int32_t*>(d.row_ptr);
         validate_csr_kernel<T, int32_t><<<grid_for(d.rows, kThreads), kThreads, 0, s>>>(
-            d.rows, d.cols, static_cast<const int32_t*>(d.row_ptr), d.col_idx, v, err.as<int>());
+            d.rows, d.cols, d.nnz, rp, d.col_idx, v, err.as<int>(), urow.as<int32_t>(), useg.as<int32_t>(),
+            unit_cap, units.as<unsigned long long>());
+        CUDA_LAUNCH_OK();
+        validate_long_rows_kernel<T, int32_t><<<long_grid, kThreads, 0, s>>>(
+            d.cols, rp, d.col_idx, v, urow.as<int32_t>(), useg.as<int32_t>(), unit_cap,
+            units.as<unsigned long long>(), err.as<int>());
     } else {
+        const int64_t* rp = static_cast<const int64_t*>(d.row_ptr);
         validate_csr_kernel<T, int64_t><<<grid_for(d.rows, kThreads), kThreads, 0, s>>>(
-            d.rows, d.cols, static_cast<const int64_t*>(d.row_ptr), d.col_idx, v, err.as<int>());
+            d.rows, d.cols, d.nnz, rp, d.col_idx, v, err.as<int>(), urow.as<int32_t>(), useg.as<int32_t>(),
+            unit_cap, units.as<unsigned long long>());
+        CUDA_LAUNCH_OK();
+        validate_long_rows_kernel<T, int64_t><<<long_grid, kThreads, 0, s>>>(
+            d.cols, rp, d.col_idx, v, urow.as<int32_t>(), useg.as<int32_t>(), unit_cap,
+            units.as<unsigned long long>(), err.as<int>());
     }
     CUDA_LAUNCH_OK();
     int h = 0;
@@ -495,72 +665,147 @@ void validate_csr(const cove_csr_desc& d, cudaStream_t s) {
                    "CSR columns must be strictly increasing within a row "
                    "(duplicate CSR entry maps to the same BitBSR bit)");
     }
+    return (h & 8) == 0;
 }
 
-template <typename T>
-void bitbsr_count(const cove_csr_desc& d, int32_t* brp, int32_t* brvp, int64_t* num_blocks,
-                  int64_t* nnz, cudaStream_t s) {
+namespace {
+
+__global__ void piece_rows_kernel(int32_t nbr, const int64_t* __restrict__ first,
+                                  const int32_t* __restrict__ boff, const int32_t* __restrict__ voff,
+                                  int32_t* __restrict__ brp, int32_t* __restrict__ brvp) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (br > nbr) return;
+    const int64_t j = first[br];
+    brp[br] = boff[j];
+    brvp[br] = voff[j];
+}
+
+// Pieces of the block rows with their block / nnz counts and offsets.
+struct PieceCounts {
+    int64_t n = 0, num_blocks = 0, nnz = 0;
+    DevBuf first;       // int64 nbr+1: first piece of each block row
+    DevBuf br, c0, c1;  // int32 n
+    DevBuf boff, voff;  // int32 n+1: exclusive scans of the block / nnz counts
+};
+
+template <typename T, typename RP>
+void count_pieces(const cove_csr_desc& d, const RP* rp, bool split, PieceCounts& p, cudaStream_t s) {
     const int32_t nbr = (d.rows + kBlockRows - 1) / kBlockRows;
+    DevBuf np;
+    alloc_n<int32_t>(np, nbr);
+    alloc_n<int64_t>(p.first, nbr + 1);
+    piece_count_kernel<RP><<<grid_for(nbr, kThreads), kThreads, 0, s>>>(d.rows, nbr, rp, split ? 1 : 0,
+                                                                         np.as<int32_t>());
+    CUDA_LAUNCH_OK();
+    p.n = exclusive_scan_total<int32_t, int64_t>(np.as<int32_t>(), p.first.as<int64_t>(), nbr, s);
+    alloc_n<int32_t>(p.br, p.n);
+    alloc_n<int32_t>(p.c0, p.n);
+    alloc_n<int32_t>(p.c1, p.n);
+    piece_bounds_kernel<RP><<<grid_for(nbr, kThreads), kThreads, 0, s>>>(
+        d.rows, nbr, rp, d.col_idx, p.first.as<int64_t>(), p.br.as<int32_t>(), p.c0.as<int32_t>(),
+        p.c1.as<int32_t>());
+    CUDA_LAUNCH_OK();
     DevBuf counts, nnzc;
-    alloc_n<int32_t>(counts, nbr);
-    alloc_n<int32_t>(nnzc, nbr);
-    const T* v = static_cast<const T*>(d.values);
-    const int grid = grid_for(static_cast<int64_t>(nbr) * 8, kThreads);
-    if (nbr > 0) {
-        if (d.row_ptr_i32) {
-            full_count_kernel<T, int32_t><<<grid, kThreads, 0, s>>>(
-                d.rows, nbr, static_cast<const int32_t*>(d.row_ptr), d.col_idx, v,
-                counts.as<int32_t>(), nnzc.as<int32_t>());
-        } else {
-            full_count_kernel<T, int64_t><<<grid, kThreads, 0, s>>>(
-                d.rows, nbr, static_cast<const int64_t*>(d.row_ptr), d.col_idx, v,
-                counts.as<int32_t>(), nnzc.as<int32_t>());
-        }
-        CUDA_LAUNCH_OK();
-    }
+    alloc_n<int32_t>(counts, p.n);
+    alloc_n<int32_t>(nnzc, p.n);
+    full_count_kernel<T, RP><<<grid_for(p.n * 8, kThreads), kThreads, 0, s>>>(
+        d.rows, p.n, rp, d.col_idx, static_cast<const T*>(d.values), p.br.as<int32_t>(),
+        p.c0.as<int32_t>(), p.c1.as<int32_t>(), counts.as<int32_t>(), nnzc.as<int32_t>());
+    CUDA_LAUNCH_OK();
+    alloc_n<int32_t>(p.boff, p.n + 1);
+    alloc_n<int32_t>(p.voff, p.n + 1);
     // the scans carry int64 totals, so an int32 overflow is detected
-    *num_blocks = checked_i32(exclusive_scan_total<int32_t, int32_t>(counts.as<int32_t>(), brp, nbr, s),
-                              "BitBSR block count");
-    *nnz = checked_i32(exclusive_scan_total<int32_t, int32_t>(nnzc.as<int32_t>(), brvp, nbr, s),
-                       "BitBSR nnz");
+    p.num_blocks = checked_i32(exclusive_scan_total<int32_t, int32_t>(counts.as<int32_t>(), p.boff.as<int32_t>(),
+                                                                      p.n, s),
+                               "BitBSR block count");
+    p.nnz = checked_i32(exclusive_scan_total<int32_t, int32_t>(nnzc.as<int32_t>(), p.voff.as<int32_t>(), p.n, s),
+                        "BitBSR nnz");
 }
 
 template <typename T>
-void bitbsr_fill(const cove_csr_desc& d, const int32_t* brp, const int32_t* brvp, int32_t* col,
-                 uint32_t* bitmap, T* values, cudaStream_t s) {
-    const int32_t nbr = (d.rows + kBlockRows - 1) / kBlockRows;
-    if (nbr == 0 || d.nnz == 0) return;
+void count_pieces(const cove_csr_desc& d, bool split, PieceCounts& p, cudaStream_t s) {
+    if (d.row_ptr_i32) count_pieces<T, int32_t>(d, static_cast<const int32_t*>(d.row_ptr), split, p, s);
+    else count_pieces<T, int64_t>(d, static_cast<const int64_t*>(d.row_ptr), split, p, s);
+}
+
+template <typename T>
+void fill_pieces(const cove_csr_desc& d, const PieceCounts& p, int32_t* col, uint32_t* bitmap, T* values,
+                 cudaStream_t s) {
+    if (p.num_blocks == 0) return;
     const T* v = static_cast<const T*>(d.values);
-    const int grid = grid_for(static_cast<int64_t>(nbr) * 8, kThreads);
+    const int grid = grid_for(p.n * 8, kThreads);
     if (d.row_ptr_i32) {
         full_fill_kernel<T, int32_t><<<grid, kThreads, 0, s>>>(
-            d.rows, nbr, static_cast<const int32_t*>(d.row_ptr), d.col_idx, v, brp, brvp, col,
-            bitmap, values);
+            d.rows, p.n, static_cast<const int32_t*>(d.row_ptr), d.col_idx, v, p.br.as<int32_t>(),
+            p.c0.as<int32_t>(), p.c1.as<int32_t>(), p.boff.as<int32_t>(), p.voff.as<int32_t>(), col, bitmap,
+            values);
     } else {
         full_fill_kernel<T, int64_t><<<grid, kThreads, 0, s>>>(
-            d.rows, nbr, static_cast<const int64_t*>(d.row_ptr), d.col_idx, v, brp, brvp, col,
-            bitmap, values);
+            d.rows, p.n, static_cast<const int64_t*>(d.row_ptr), d.col_idx, v, p.br.as<int32_t>(),
+            p.c0.as<int32_t>(), p.c1.as<int32_t>(), p.boff.as<int32_t>(), p.voff.as<int32_t>(), col, bitmap,
+            values);
     }
     CUDA_LAUNCH_OK();
 }
 
+}  // namespace
+
 template <typename T>
-void build_full_bitbsr(const cove_csr_desc& d, FullBitBsr& out, cudaStream_t s) {
+void bitbsr_count(const cove_csr_desc& d, bool split, int32_t* brp, int32_t* brvp, int64_t* num_blocks,
+                  int64_t* nnz, cudaStream_t s) {
+    const int32_t nbr = (d.rows + kBlockRows - 1) / kBlockRows;
+    if (nbr == 0) {
+        CUDA_OK(cudaMemsetAsync(brp, 0, sizeof(int32_t), s));
+        CUDA_OK(cudaMemsetAsync(brvp, 0, sizeof(int32_t), s));
+        *num_blocks = 0;
+        *nnz = 0;
+        return;
+    }
+    PieceCounts p;
+    count_pieces<T>(d, split, p, s);
+    piece_rows_kernel<<<grid_for(static_cast<int64_t>(nbr) + 1, kThreads), kThreads, 0, s>>>(
+        nbr, p.first.as<int64_t>(), p.boff.as<int32_t>(), p.voff.as<int32_t>(), brp, brvp);
+    CUDA_LAUNCH_OK();
+    *num_blocks = p.num_blocks;
+    *nnz = p.nnz;
+}
+
+template <typename T>
+void bitbsr_fill(const cove_csr_desc& d, bool split, int32_t* col, uint32_t* bitmap, T* values,
+                 cudaStream_t s) {
+    const int32_t nbr = (d.rows + kBlockRows - 1) / kBlockRows;
+    if (nbr == 0 || d.nnz == 0) return;
+    PieceCounts p;  // the pieces' offsets are recounted: they are not the caller's per-block-row ones
+    count_pieces<T>(d, split, p, s);
+    fill_pieces<T>(d, p, col, bitmap, values, s);
+}
+
+template <typename T>
+void build_full_bitbsr(const cove_csr_desc& d, bool split, FullBitBsr& out, cudaStream_t s) {
     out.rows = d.rows;
     out.cols = d.cols;
     out.nbr = (d.rows + kBlockRows - 1) / kBlockRows;
     alloc_n<int32_t>(out.block_row_ptr, out.nbr + 1);
     alloc_n<int32_t>(out.block_row_val_ptr, out.nbr + 1);
-    bitbsr_count<T>(d, out.block_row_ptr.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(),
-                    &out.num_blocks, &out.nnz, s);
+    if (out.nbr == 0) {
+        CUDA_OK(cudaMemsetAsync(out.block_row_ptr.p, 0, sizeof(int32_t), s));
+        CUDA_OK(cudaMemsetAsync(out.block_row_val_ptr.p, 0, sizeof(int32_t), s));
+        out.num_blocks = 0;
+        out.nnz = 0;
+        return;
+    }
+    PieceCounts p;
+    count_pieces<T>(d, split, p, s);
+    piece_rows_kernel<<<grid_for(static_cast<int64_t>(out.nbr) + 1, kThreads), kThreads, 0, s>>>(
+        out.nbr, p.first.as<int64_t>(), p.boff.as<int32_t>(), p.voff.as<int32_t>(),
+        out.block_row_ptr.as<int32_t>(), out.block_row_val_ptr.as<int32_t>());
+    CUDA_LAUNCH_OK();
+    out.num_blocks = p.num_blocks;
+    out.nnz = p.nnz;
     alloc_n<int32_t>(out.block_col_idx, out.num_blocks);
     alloc_n<uint32_t>(out.bitmap, out.num_blocks);
     alloc_n<T>(out.values, out.nnz);
-    if (out.num_blocks > 0) {
-        bitbsr_fill<T>(d, out.block_row_ptr.as<int32_t>(), out.block_row_val_ptr.as<int32_t>(),
-                       out.block_col_idx.as<int32_t>(), out.bitmap.as<uint32_t>(),
-                       out.values.as<T>(), s);
-    }
+    fill_pieces<T>(d, p, out.block_col_idx.as<int32_t>(), out.bitmap.as<uint32_t>(), out.values.as<T>(), s);
 }
 
 void pack_words(int64_t nb, const int32_t* col, const uint32_t* bitmap, uint64_t* words,
@@ -749,16 +994,14 @@ void build_chunks(const int32_t* res_rp, int32_t rows, int tau, int chunk_nnz, C
     }
 }
 
-template void validate_csr<double>(const cove_csr_desc&, cudaStream_t);
-template void validate_csr<float>(const cove_csr_desc&, cudaStream_t);
-template void build_full_bitbsr<double>(const cove_csr_desc&, FullBitBsr&, cudaStream_t);
-template void build_full_bitbsr<float>(const cove_csr_desc&, FullBitBsr&, cudaStream_t);
-template void bitbsr_count<double>(const cove_csr_desc&, int32_t*, int32_t*, int64_t*, int64_t*, cudaStream_t);
-template void bitbsr_count<float>(const cove_csr_desc&, int32_t*, int32_t*, int64_t*, int64_t*, cudaStream_t);
-template void bitbsr_fill<double>(const cove_csr_desc&, const int32_t*, const int32_t*, int32_t*, uint32_t*,
-                                  double*, cudaStream_t);
-template void bitbsr_fill<float>(const cove_csr_desc&, const int32_t*, const int32_t*, int32_t*, uint32_t*,
-                                 float*, cudaStream_t);
+template bool validate_csr<double>(const cove_csr_desc&, cudaStream_t);
+template bool validate_csr<float>(const cove_csr_desc&, cudaStream_t);
+template void build_full_bitbsr<double>(const cove_csr_desc&, bool, FullBitBsr&, cudaStream_t);
+template void build_full_bitbsr<float>(const cove_csr_desc&, bool, FullBitBsr&, cudaStream_t);
+template void bitbsr_count<double>(const cove_csr_desc&, bool, int32_t*, int32_t*, int64_t*, int64_t*, cudaStream_t);
+template void bitbsr_count<float>(const cove_csr_desc&, bool, int32_t*, int32_t*, int64_t*, int64_t*, cudaStream_t);
+template void bitbsr_fill<double>(const cove_csr_desc&, bool, int32_t*, uint32_t*, double*, cudaStream_t);
+template void bitbsr_fill<float>(const cove_csr_desc&, bool, int32_t*, uint32_t*, float*, cudaStream_t);
 template void build_split<double>(const FullBitBsr&, const cove_plan_opts&, SplitParts&, cudaStream_t);
 template void build_split<float>(const FullBitBsr&, const cove_plan_opts&, SplitParts&, cudaStream_t);
 

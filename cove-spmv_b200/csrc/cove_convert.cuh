@@ -47,15 +47,19 @@ struct Chunks {
     DevBuf row, pbegin, pcount;  // int32 each
 };
 
+// Throws on invalid CSR; returns whether every row's columns are
+// non-decreasing with stored zeros included (the converter may then cut
+// long block rows into column-range pieces).
 template <typename T>
-void validate_csr(const cove_csr_desc& d, cudaStream_t s);
-// caller-buffer steps (the reference's step-by-step device API)
+bool validate_csr(const cove_csr_desc& d, cudaStream_t s);
+// caller-buffer steps (the reference's step-by-step device API); `split`
+// is validate_csr's answer
 template <typename T>
-void bitbsr_count(const cove_csr_desc& d, int32_t* brp, int32_t* brvp, int64_t* num_blocks,
+void bitbsr_count(const cove_csr_desc& d, bool split, int32_t* brp, int32_t* brvp, int64_t* num_blocks,
                   int64_t* nnz, cudaStream_t s);
 template <typename T>
-void bitbsr_fill(const cove_csr_desc& d, const int32_t* brp, const int32_t* brvp, int32_t* col,
-                 uint32_t* bitmap, T* values, cudaStream_t s);
+void bitbsr_fill(const cove_csr_desc& d, bool split, int32_t* col, uint32_t* bitmap, T* values,
+                 cudaStream_t s);
 void pack_words(int64_t nb, const int32_t* col, const uint32_t* bitmap, uint64_t* words,
                 cudaStream_t s);
 int64_t lb_count(int32_t nbr, const int32_t* brp, int chunk, int split, int style,
@@ -64,7 +68,7 @@ void lb_fill(int32_t nbr, const int32_t* brp, const int32_t* brvp, const uint32_
              const int32_t* item_rp, int chunk, int split, int style, uint64_t* words,
              WorkItem* items, cudaStream_t s);
 template <typename T>
-void build_full_bitbsr(const cove_csr_desc& d, FullBitBsr& out, cudaStream_t s);
+void build_full_bitbsr(const cove_csr_desc& d, bool split, FullBitBsr& out, cudaStream_t s);
 unsigned long long move_mask_for(const cove_plan_opts& o);
 template <typename T>
 void build_split(const FullBitBsr& f, const cove_plan_opts& o, SplitParts& out, cudaStream_t s);

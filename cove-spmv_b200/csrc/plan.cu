@@ -368,8 +368,8 @@ namespace {
 template <typename T>
 void build_plan_typed(cove_plan* P, const cove_csr_desc& d, cudaStream_t s) {
     const cove_plan_opts& o = P->opts;
-    validate_csr<T>(d, s);
-    build_full_bitbsr<T>(d, P->full, s);
+    const bool split = validate_csr<T>(d, s);
+    build_full_bitbsr<T>(d, split, P->full, s);
     P->nnz = P->full.nnz;
     P->nbr = P->full.nbr;
     build_split<T>(P->full, o, P->sp, s);
@@ -787,11 +787,9 @@ cove_status cove_bitbsr8x4_count(const cove_csr_desc* csr, int32_t* brp, int32_t
         if (!csr || !brp || !brvp || !num_blocks || !nnz) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         if (csr->dtype == COVE_F64) {
-            validate_csr<double>(*csr, s);
-            bitbsr_count<double>(*csr, brp, brvp, num_blocks, nnz, s);
+            bitbsr_count<double>(*csr, validate_csr<double>(*csr, s), brp, brvp, num_blocks, nnz, s);
         } else if (csr->dtype == COVE_F32) {
-            validate_csr<float>(*csr, s);
-            bitbsr_count<float>(*csr, brp, brvp, num_blocks, nnz, s);
+            bitbsr_count<float>(*csr, validate_csr<float>(*csr, s), brp, brvp, num_blocks, nnz, s);
         } else {
             COVE_THROW(COVE_ERR_UNSUPPORTED, "dtype must be float64 or float32");
         }
@@ -804,8 +802,15 @@ cove_status cove_bitbsr8x4_fill(const cove_csr_desc* csr, const int32_t* brp, co
         if (!csr || !brp || !brvp) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null argument");
         if (csr->nnz > 0 && (!col || !bitmap || !values)) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null output");
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        if (csr->dtype == COVE_F64) bitbsr_fill<double>(*csr, brp, brvp, col, bitmap, static_cast<double*>(values), s);
-        else bitbsr_fill<float>(*csr, brp, brvp, col, bitmap, static_cast<float*>(values), s);
+        // the fill re-validates: it walks the CSR on its own and needs the
+        // column-order answer for its pieces
+        if (csr->dtype == COVE_F64) {
+            bitbsr_fill<double>(*csr, validate_csr<double>(*csr, s), col, bitmap, static_cast<double*>(values), s);
+        } else if (csr->dtype == COVE_F32) {
+            bitbsr_fill<float>(*csr, validate_csr<float>(*csr, s), col, bitmap, static_cast<float*>(values), s);
+        } else {
+            COVE_THROW(COVE_ERR_UNSUPPORTED, "dtype must be float64 or float32");
+        }
     });
 }
 

@@ -546,7 +546,20 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
         const int pb = k.chunk_pbegin[c];
         const int pn = k.chunk_pcount[c];
         Acc sum = Acc(0);
-        for (int q = lane; q < pn; q += 32) sum += dec.res_val(pb + q) * dec.xv(x, k.res_col[pb + q]);
+        // four independent column -> x chains in flight per lane
+        constexpr int U = 4;
+        int q = lane;
+        for (; q + 32 * (U - 1) < pn; q += 32 * U) {
+            int col[U];
+            Acc val[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) col[u] = __ldg(k.res_col + pb + q + 32 * u);
+#pragma unroll
+            for (int u = 0; u < U; ++u) val[u] = dec.res_val(pb + q + 32 * u);
+#pragma unroll
+            for (int u = 0; u < U; ++u) sum += val[u] * dec.xv(x, col[u]);
+        }
+        for (; q < pn; q += 32) sum += dec.res_val(pb + q) * dec.xv(x, k.res_col[pb + q]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         if (lane == 0) atomicAdd(&y[row], static_cast<T>(sum));

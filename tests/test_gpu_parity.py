@@ -337,10 +337,112 @@ def test_edge_cases():
         (np.array([0, 2, 2, 3]), np.array([1, 0, 2], np.int32), "strictly increasing"),
         (np.array([0, 2, 2, 3]), np.array([1, 1, 2], np.int32), "strictly increasing"),
         (np.array([0, 2, 2, 3]), np.array([0, 9, 2], np.int32), "out of range"),
+        # an offset above nnz is a non-monotonic row_ptr; the row is not read
+        (np.array([0, 5000, 1, 3]), np.array([0, 1, 2], np.int32), "monotonic"),
+        # an order error before a range error in one row: the range error is reported
+        (np.array([0, 3, 3, 3]), np.array([1, 0, 9], np.int32), "out of range"),
     ]
     for rp_b, ci_b, msg in bad:
         with pytest.raises(cb.CoveError, match=msg):
             plan_for(3, 4, rp_b, ci_b, np.ones(3))
+
+
+def _heavy_rows_csr(seed=31):
+    """64 x 200000 with three 6000-entry rows (two in one block row), 300-entry
+    rows and 7-entry rows; 5 % stored zeros, columns in order."""
+    rng = np.random.default_rng(seed)
+    rows, cols = 64, 200000
+    lists = [np.unique(rng.integers(0, cols, 6000 if r in (3, 17, 18) else (300 if r % 5 == 0 else 7)))
+             for r in range(rows)]
+    rp = np.zeros(rows + 1, np.int64)
+    rp[1:] = np.cumsum([len(c) for c in lists])
+    ci = np.concatenate(lists).astype(np.int32)
+    v = rng.standard_normal(ci.size)
+    v[rng.random(ci.size) < 0.05] = 0.0
+    return rows, cols, rp, ci, v
+
+
+def _step_api_full(rows, cols, rp, ci, v):
+    """cove_bitbsr8x4_count + cove_bitbsr8x4_fill into caller buffers."""
+    import ctypes as C
+
+    import torch
+
+    csr = cb.DeviceCsr.from_numpy(rows, cols, rp, ci, v)
+    d = csr.desc()
+    nbr = (rows + 7) // 8
+    brp = torch.empty(nbr + 1, dtype=torch.int32, device="cuda")
+    brvp = torch.empty(nbr + 1, dtype=torch.int32, device="cuda")
+    nb, nz = C.c_int64(), C.c_int64()
+    L = cb.lib()
+    cb.check(L.cove_bitbsr8x4_count(C.byref(d), C.c_void_p(brp.data_ptr()), C.c_void_p(brvp.data_ptr()),
+                                    C.byref(nb), C.byref(nz), None))
+    col = torch.empty(max(nb.value, 1), dtype=torch.int32, device="cuda")
+    bm = torch.empty(max(nb.value, 1), dtype=torch.int32, device="cuda")
+    vals = torch.empty(max(nz.value, 1), dtype=csr.values.dtype, device="cuda")
+    cb.check(L.cove_bitbsr8x4_fill(C.byref(d), C.c_void_p(brp.data_ptr()), C.c_void_p(brvp.data_ptr()),
+                                   C.c_void_p(col.data_ptr()), C.c_void_p(bm.data_ptr()),
+                                   C.c_void_p(vals.data_ptr()), None))
+    torch.cuda.synchronize()
+    return (brp.cpu().numpy(), brvp.cpu().numpy(), col.cpu().numpy()[: nb.value],
+            bm.cpu().numpy().view(np.uint32)[: nb.value], vals.cpu().numpy()[: nz.value])
+
+
+@pytest.mark.parametrize("zeros", ["in_order", "out_of_order"])
+def test_heavy_block_rows_convert_in_pieces(zeros):
+    """Block rows with more than 1024 CSR entries are converted as
+    column-range pieces (each row binary-searched for the range); with a
+    stored zero out of column order the converter keeps one piece per block
+    row.  Both give the reference converter's streams bit for bit, through
+    the plan and through the step-by-step count / fill calls."""
+    rows, cols, rp, ci, v = _heavy_rows_csr()
+    if zeros == "out_of_order":
+        q = rp[17] + 10  # a stored zero whose column goes back: valid CSR, zeros are ignored
+        v[q] = 0.0
+        ci[q] = ci[rp[17]]
+    b = O.convert_to_bitbsr(rows, cols, rp, ci, v)
+    p = plan_for(rows, cols, rp, ci, v, keep_full_bitbsr=1, value_codec="original")
+    assert np.array_equal(p.stream("full_block_row_ptr"), b.block_row_ptr)
+    assert np.array_equal(p.stream("full_block_col_idx"), b.block_col_idx)
+    assert np.array_equal(p.stream("full_bitmap"), b.bitmap_words)
+    assert np.array_equal(p.stream("full_values"), b.values)
+    assert np.array_equal(p.stream("full_block_row_val_ptr"), b.block_val_ptr[b.block_row_ptr])
+    brp, brvp, col, bm, vals = _step_api_full(rows, cols, rp, ci, v)
+    assert np.array_equal(brp, b.block_row_ptr) and np.array_equal(brvp, b.block_val_ptr[b.block_row_ptr])
+    assert np.array_equal(col, b.block_col_idx) and np.array_equal(bm, b.bitmap_words)
+    assert np.array_equal(vals, b.values)
+    x = cb.synth_vector("uniform_pm1", cols, seed=9)
+    y = gpu_spmv(p, x)
+    assert O.compare_vectors(O.spmv_csr(rows, rp, ci, v, x), y)[2] <= 1e-12
+
+
+def test_long_row_validation_follows_the_reference_priority():
+    """Rows longer than 256 entries are validated in 2048-entry units, a lane
+    per entry.  As in the reference (every column's range is checked before
+    the converter meets a duplicate), a range error anywhere outranks an
+    order error."""
+    rows, cols, rp, ci, v = _heavy_rows_csr(seed=5)
+    v[:] = 1.0
+    r = 3  # a 6000-entry row
+    dup = ci.copy()
+    dup[rp[r] + 100] = dup[rp[r] + 99]  # duplicate at entry 100 ...
+    with pytest.raises(cb.CoveError, match="strictly increasing"):
+        plan_for(rows, cols, rp, dup, v)
+    dup[rp[r] + 5000] = cols + 5  # ... and out of range at entry 5000, in another unit
+    with pytest.raises(cb.CoveError, match="out of range"):
+        plan_for(rows, cols, rp, dup, v)
+    oor = ci.copy()
+    oor[rp[r] + 4000] = -1
+    with pytest.raises(cb.CoveError, match="out of range"):
+        plan_for(rows, cols, rp, oor, v)
+    z = v.copy()  # a zero between two equal columns is fine; the equal nonzeros are not
+    eq = ci.copy()
+    eq[rp[r] + 301] = eq[rp[r] + 300]
+    z[rp[r] + 300] = 0.0
+    plan_for(rows, cols, rp, eq, z)
+    z[rp[r] + 300] = 1.0
+    with pytest.raises(cb.CoveError, match="strictly increasing"):
+        plan_for(rows, cols, rp, eq, z)
 
 
 def test_long_rows_and_heavy_block_rows_overflow_path():
