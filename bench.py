@@ -564,16 +564,201 @@ def run_lapl3d_cg(args):
     return 0
 
 
+BLOCKSPARSE = dict(n=1 << 21, p_block=2e-3, p_entry=0.6, outlier_fraction=1e-3, seed=3)
+SHARD_NNZ_TARGET = 1_800_000_000  # expected nnz per plan (int32 offsets, with margin)
+
+
+def blocksparse_shards(rank, world, n):
+    """Rows [row_begin, row_end) of rank (whole 8-row block rows) and its shards."""
+    bs = BLOCKSPARSE
+    nbr = (n + 7) // 8
+    cuts = [round(r * nbr / world) * 8 for r in range(world + 1)]
+    rb, re = cuts[rank], min(cuts[rank + 1], n)
+    per_row = ((n + 3) // 4) * bs["p_block"] * 4 * bs["p_entry"]
+    k = max(1, int(np.ceil((re - rb) * per_row / SHARD_NNZ_TARGET)))
+    sb = [rb + round(i * (re - rb) / (8 * k)) * 8 for i in range(k)] + [re]
+    return rb, re, [(sb[i], sb[i + 1]) for i in range(k) if sb[i + 1] > sb[i]]
+
+
+def run_blocksparse(args):
+    """Random 8x4 block-sparse n = 2^21 with outliers (5.3e9 nnz): row blocks
+    of int32-safe plans generated in HBM; with N > 1 the rows are split across
+    the ranks and each rank receives the other ranks' x rows (weak in rows,
+    every rank reads all of x)."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    import cove_b200 as cb
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=dev)
+    bs = BLOCKSPARSE
+    n = args.bs_n or bs["n"]
+    gen = (bs["p_block"], bs["p_entry"], bs["outlier_fraction"], bs["seed"])
+    codec = args.codec or "bfp8_outlier"
+    rb, re, shards = blocksparse_shards(rank, world, n)
+    stream = torch.cuda.current_stream()
+    sh = C.c_void_p(stream.cuda_stream)
+    L = cb.lib()
+    plans = []
+    t0 = time.perf_counter()
+    for (sb, se) in shards:
+        rp, ci, v = cb.synth_blocksparse_device(n, sb, se, *gen, device=dev, stream=stream)
+        plans.append(cb.Plan(cb.DeviceCsr(se - sb, n, rp, ci, v), value_codec=codec, keep_lossless=1,
+                             stream=stream))
+        del rp, ci, v
+        torch.cuda.empty_cache()
+    build_s = time.perf_counter() - t0
+    nnz_local = sum(int(p.info.nnz) for p in plans)
+    route = plans[0].info.dispatched_route
+    x_host = cb.synth_vector("normal", n, seed=bs["seed"])
+    xd = torch.from_numpy(x_host).to(dev)
+    y = torch.empty(re - rb, dtype=torch.float64, device=dev)
+
+    idbuf = np.zeros(L.cove_dist_id_bytes(), np.uint8)
+    if rank == 0:
+        cb.check(L.cove_dist_make_id(idbuf.ctypes.data_as(C.c_void_p)))
+    if world > 1:
+        obj = [idbuf.tobytes()]
+        dist.broadcast_object_list(obj, src=0)
+        idbuf = np.frombuffer(obj[0], np.uint8).copy()
+    D = C.c_void_p()
+    arr = (C.c_void_p * len(plans))(*[p.handle.value for p in plans])
+    cb.check(L.cove_dist_create(rank, world, idbuf.ctypes.data_as(C.c_void_p), arr, len(plans), n, rb, re,
+                                0, n, 300000, C.byref(D)))
+
+    def step(xbuf, ybuf):
+        cb.check(L.cove_dist_spmv(D, C.c_void_p(xbuf.data_ptr()), C.c_void_p(ybuf.data_ptr()), sh))
+
+    # parity on 16 block rows of this rank, regenerated on the host
+    step(xd, y)
+    torch.cuda.synchronize()
+    yh = y.cpu().numpy()
+    nbr_local = (re - rb + 7) // 8
+    worst = 0.0
+    ymax = 0.0
+    for q in np.linspace(0, nbr_local - 1, 16).astype(np.int64):
+        r0 = rb + int(q) * 8
+        r1 = min(r0 + 8, re)
+        srp, sci, sv = cb.synth_blocksparse_rows(n, r0, r1, *gen)
+        for i in range(r1 - r0):
+            ref = float(np.dot(sv[srp[i]:srp[i + 1]], x_host[sci[srp[i]:srp[i + 1]]]))
+            worst = max(worst, abs(ref - yh[r0 - rb + i]))
+            ymax = max(ymax, abs(ref))
+    rel = worst / max(ymax, 1e-300)
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        step(xd, y)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    clk = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk.start()
+    time.sleep(0.3)
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step(xd, y)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clk.stop()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    launches = int(L.cove_dist_spmv_launches(D))
+
+    # end to end: pinned host x in, y out, every step
+    xh = torch.from_numpy(x_host).pin_memory()
+    yh_t = torch.empty(re - rb, dtype=torch.float64).pin_memory()
+    xd2 = torch.empty(n, dtype=torch.float64, device=dev)
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t1 = time.perf_counter()
+        xd2.copy_(xh, non_blocking=True)
+        step(xd2, y)
+        yh_t.copy_(y, non_blocking=True)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            e2e.append((time.perf_counter() - t1) * 1e3)
+    tot = torch.tensor([ms, float(np.mean(e2e)), float(nnz_local), rel], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = tot.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = tot.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms_all, e2e_all, rel_all, nnz_total = float(mx[0]), float(mx[1]), float(mx[3]), float(sm[2])
+    else:
+        ms_all, e2e_all, rel_all, nnz_total = ms, float(np.mean(e2e)), rel, float(nnz_local)
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        alg = sum(int(p.info.algorithmic_bytes[p.info.dispatched_route]) for p in plans)
+        achieved = alg / (ms * 1e-3) / 1e9
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            # bounded sample: the first 32,768 rows (~8e7 nnz) through the reference's spmv_csr
+            srp, sci, sv = cb.synth_blocksparse_rows(n, 0, min(n, 32768), *gen)
+            cms, cores, kind = cpu_reference_time(len(srp) - 1, n, srp, sci, sv, x_host, 5)
+            cpu = {"value": round(2.0 * len(sv) / (cms * 1e-3) / 1e9, 3), "unit": "GFLOP/s", "cores": cores,
+                   "kind": kind, "sample": f"best of 5 SpMVs of rows [0, {len(srp) - 1}) ({len(sv)} nnz)"}
+        line = {
+            "metric": "spmv_gflops", "value": round(2.0 * nnz_total / (ms_all * 1e-3) / 1e9, 3),
+            "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_all, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64" if route in (0, 1, 2) else "f32 accumulate, f64 in/out",
+            "data": "synthetic",
+            "config": {"workload": f"block-sparse 8x4 n={n} (p_block {bs['p_block']}, p_entry {bs['p_entry']},"
+                                   f" {bs['outlier_fraction']:g} outliers; nnz={int(nnz_total)})",
+                       "requested_codec": codec, "route": cb.ROUTE_NAMES[route],
+                       "joint_route": cb.ROUTE_NAMES[plans[0].info.joint_route],
+                       "gate_rel_err": plans[0].info.joint_rel_err, "gate_pass": bool(plans[0].info.gate_pass),
+                       "plans_per_rank": len(plans), "plan_build_s": round(build_s, 2),
+                       "l2": "flushed between steps (256 MiB write, outside the timed events)",
+                       "parallelism": "1 GPU" if world == 1 else f"row blocks x{world}, x rows exchanged by NCCL",
+                       "parity_rel_sampled_rows": rel_all},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "algorithmic_bytes": alg,
+                         "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(2.0 * nnz_total / (e2e_all * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
+                    "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": (re - rb) * 8},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    L.cove_dist_destroy(D)
+    for p in plans:
+        p.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="fem27", choices=["fem27", "lapl3d_cg", "lapl2d_512", "rmat_22"])
+    ap.add_argument("--workload", default="fem27",
+                    choices=["fem27", "lapl3d_cg", "lapl2d_512", "rmat_22", "blocksparse"])
+    ap.add_argument("--bs-n", type=int, default=0, help="blocksparse: n (default 2^21)")
     ap.add_argument("--grid", type=int, default=0, help="lapl3d_cg: grid edge (default 768)")
     ap.add_argument("--cg-iters", type=int, default=50)
-    ap.add_argument("--codec", default="auto")
+    ap.add_argument("--codec", default=None, help="value codec (default auto; blocksparse: bfp8_outlier)")
     ap.add_argument("--route", default=None,
                     help="time this route instead of the dispatched one (analysis only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -582,6 +767,10 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload == "blocksparse":
+        return run_blocksparse(args)
+    if args.codec is None:
+        args.codec = "auto"
     if args.workload == "lapl3d_cg":
         return run_lapl3d_cg(args)
     return run_fem(args)

@@ -145,7 +145,8 @@ EXPORTED = [
     "cove_dist_halo", "cove_dist_cg_solve", "cove_dist_spmv", "cove_dist_spmv_launches",
     "cove_rng_u64", "cove_rng_uniform01", "cove_synth_lapl2d", "cove_synth_lapl3d",
     "cove_synth_fem27", "cove_synth_fem27_rows", "cove_synth_rmat", "cove_synth_blocksparse", "cove_synth_vector",
-    "cove_synth_lapl3d_device", "cove_synth_vector_device",
+    "cove_synth_lapl3d_device", "cove_synth_vector_device", "cove_synth_blocksparse_rows",
+    "cove_synth_blocksparse_device",
 ]
 
 _lib = None
@@ -226,6 +227,11 @@ def _setup(L):
     L.cove_synth_rmat.argtypes = [i32, i32, f64, f64, f64, u64, vp, vp, vp]
     L.cove_synth_blocksparse.restype = i64
     L.cove_synth_blocksparse.argtypes = [i32, f64, f64, f64, u64, vp, vp, vp]
+    L.cove_synth_blocksparse_rows.restype = i64
+    L.cove_synth_blocksparse_rows.argtypes = [i32, f64, f64, f64, u64, i64, i64, vp, vp, vp]
+    L.cove_synth_blocksparse_device.restype = C.c_int
+    L.cove_synth_blocksparse_device.argtypes = [i32, f64, f64, f64, u64, i64, i64, vp, vp, vp,
+                                                C.POINTER(C.c_int64), vp]
     L.cove_synth_vector.argtypes = [i32, u64, u64, i64, i32, vp]
     L.cove_synth_lapl3d_device.restype = C.c_int
     L.cove_synth_lapl3d_device.argtypes = [i32, i32, i32, i64, i64, i64, vp, vp, vp,
@@ -514,6 +520,35 @@ def synth_blocksparse(n, p_block=2e-3, p_entry=0.6, outlier_fraction=1e-3, seed=
     rp, ci, v = _two_call(lib().cove_synth_blocksparse, n,
                           (n, p_block, p_entry, outlier_fraction, seed), np.float64)
     return n, n, rp, ci, v
+
+
+def synth_blocksparse_rows(n, row_begin, row_end, p_block=2e-3, p_entry=0.6, outlier_fraction=1e-3, seed=3):
+    """Rows [row_begin, row_end) of synth_blocksparse(n): (row_ptr relative, cols, values)."""
+    if lib().cove_synth_blocksparse_rows(n, p_block, p_entry, outlier_fraction, seed, row_begin, row_end,
+                                         None, None, None) < 0:
+        raise CoveError(1, "row range must cover whole 8-row block rows of [0, n)")
+    rp, ci, v = _two_call(lib().cove_synth_blocksparse_rows, row_end - row_begin,
+                          (n, p_block, p_entry, outlier_fraction, seed, row_begin, row_end), np.float64)
+    return rp, ci, v
+
+
+def synth_blocksparse_device(n, row_begin, row_end, p_block=2e-3, p_entry=0.6, outlier_fraction=1e-3,
+                             seed=3, device="cuda", stream=None):
+    """The same rows generated in HBM: (row_ptr int32 relative, cols int32, values f64) tensors."""
+    import torch
+
+    L = lib()
+    nnz = C.c_int64(0)
+    check(L.cove_synth_blocksparse_device(n, p_block, p_entry, outlier_fraction, seed, row_begin, row_end,
+                                          None, None, None, C.byref(nnz), _stream_handle(stream)))
+    rows = row_end - row_begin
+    rp = torch.empty(rows + 1, dtype=torch.int32, device=device)
+    ci = torch.empty(max(nnz.value, 1), dtype=torch.int32, device=device)
+    v = torch.empty(max(nnz.value, 1), dtype=torch.float64, device=device)
+    check(L.cove_synth_blocksparse_device(n, p_block, p_entry, outlier_fraction, seed, row_begin, row_end,
+                                          C.c_void_p(rp.data_ptr()), C.c_void_p(ci.data_ptr()),
+                                          C.c_void_p(v.data_ptr()), C.byref(nnz), _stream_handle(stream)))
+    return rp, ci[: nnz.value], v[: nnz.value]
 
 
 def read_matrix_market(path, dtype=np.float64):

@@ -388,9 +388,10 @@ float spmv_plans(const std::vector<cove_plan*>& plans, const double* xw, double*
     return 0.0f;
 }
 
-// y_local = A_local x_window on a partition: the halo runs on the comm
-// stream while the block rows that read only own columns are computed; the
-// rest follow once it has landed, then any overflow pass.
+// y_local = A_local x_window on a partition: the block rows that read only
+// own columns are launched first, so the GPU computes them while the host
+// enqueues the halo on the (highest-priority) comm stream; the rest follow
+// once it has landed, then any overflow pass.
 void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s, int route = -1) {
     if (!d->overlap) {
         halo(d, xw, s);
@@ -398,11 +399,13 @@ void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s, int route = 
         return;
     }
     CUDA_OK(cudaEventRecord(d->x_ready, s));
-    CUDA_OK(cudaStreamWaitEvent(d->s_comm, d->x_ready, 0));
-    halo(d, xw, d->s_comm);
-    CUDA_OK(cudaEventRecord(d->halo_done, d->s_comm));
     for (int pass = 0; pass < 2; ++pass) {
-        if (pass == 1) CUDA_OK(cudaStreamWaitEvent(s, d->halo_done, 0));
+        if (pass == 1) {
+            CUDA_OK(cudaStreamWaitEvent(d->s_comm, d->x_ready, 0));
+            halo(d, xw, d->s_comm);
+            CUDA_OK(cudaEventRecord(d->halo_done, d->s_comm));
+            CUDA_OK(cudaStreamWaitEvent(s, d->halo_done, 0));
+        }
         int64_t off = 0;
         for (size_t i = 0; i < d->plans.size(); ++i) {
             const cove_plan* P = d->plans[i];
@@ -462,7 +465,11 @@ void plan_overlap(cove_dist* d) {
         d->ranges.clear();
         return;
     }
-    CUDA_OK(cudaStreamCreateWithFlags(&d->s_comm, cudaStreamNonBlocking));
+    // NCCL's kernel on this stream should not queue behind the interior
+    // pass's remaining CTAs
+    int least = 0, greatest = 0;
+    CUDA_OK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+    CUDA_OK(cudaStreamCreateWithPriority(&d->s_comm, cudaStreamNonBlocking, greatest));
     CUDA_OK(cudaEventCreateWithFlags(&d->x_ready, cudaEventDisableTiming));
     CUDA_OK(cudaEventCreateWithFlags(&d->halo_done, cudaEventDisableTiming));
     d->overlap = true;

@@ -102,6 +102,96 @@ __global__ void vector_kernel(int32_t kind, uint64_t key, int64_t begin, int64_t
     out[t] = kind == 0 ? 2.0 * u - 1.0 : u;
 }
 
+// ---- 8x4 block-sparse rows (the host generator's draws, on the device) ----------
+// One warp per block row scans the block columns (a lane per column, a
+// Bernoulli draw each); a present block's 32 cells are one lane each.
+
+struct BlockSparseKeys {
+    uint64_t kb, ke, kv, ko, ks, km;
+};
+
+__host__ __device__ inline BlockSparseKeys blocksparse_keys(uint64_t seed) {
+    return {stream_key(seed, 0), stream_key(seed, 1), stream_key(seed, 2),
+            stream_key(seed, 3), stream_key(seed, 4), stream_key(seed, 5)};
+}
+
+// The value of cell `cell` (block * 32 + bit).  The outlier magnitude is a
+// separate multiply and add on the device too (the host compiler does not
+// contract it), so both give the same double.
+__device__ inline double blocksparse_value_dev(const BlockSparseKeys& k, double outlier_fraction, uint64_t cell) {
+    if (u01_key(k.ko, cell) < outlier_fraction) {
+        const double sgn = u01_key(k.ks, cell) < 0.5 ? -1.0 : 1.0;
+        return sgn * __dadd_rn(1e5, __dmul_rn(9e5, u01_key(k.km, cell)));
+    }
+    for (int t = 0; t < 8; ++t) {
+        const float f = static_cast<float>(__dadd_rn(__dmul_rn(16.0, u01_key(k.kv, cell * 8 + t)), -8.0));
+        const uint32_t bits = __float_as_uint(f);
+        const uint32_t r = ((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16) << 16;  // bf16, ties to even
+        if (__uint_as_float(r) != 0.0f) return static_cast<double>(__uint_as_float(r));
+    }
+    return 1.0;
+}
+
+__global__ void blocksparse_count_kernel(int32_t n, int64_t nbc, double p_block, double p_entry,
+                                         BlockSparseKeys k, int64_t br0, int64_t nbr_local,
+                                         int64_t row_begin, int32_t* __restrict__ cnt) {
+    const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= nbr_local) return;  // whole warp
+    const int64_t br = br0 + w;
+    int c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t bc = lane; bc < nbc; bc += 32) {
+        const uint64_t blk = static_cast<uint64_t>(br * nbc + bc);
+        if (u01_key(k.kb, blk) < p_block) {
+#pragma unroll
+            for (int lr = 0; lr < 8; ++lr)
+#pragma unroll
+                for (int lc = 0; lc < 4; ++lc)
+                    c[lr] += (bc * 4 + lc < n && u01_key(k.ke, blk * 32 + lr * 4 + lc) < p_entry) ? 1 : 0;
+        }
+    }
+#pragma unroll
+    for (int lr = 0; lr < 8; ++lr) {
+        const int t = __reduce_add_sync(0xffffffffu, c[lr]);
+        const int64_t row = br * 8 + lr;
+        if (lane == 0 && row < n) cnt[row - row_begin] = t;
+    }
+}
+
+__global__ void blocksparse_fill_kernel(int32_t n, int64_t nbc, double p_block, double p_entry,
+                                        double outlier_fraction, BlockSparseKeys k, int64_t br0,
+                                        int64_t nbr_local, int64_t row_begin,
+                                        const int32_t* __restrict__ rp, int32_t* __restrict__ ci,
+                                        double* __restrict__ v) {
+    const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= nbr_local) return;
+    const int64_t br = br0 + w;
+    const int lr = lane >> 2, lc = lane & 3;
+    // lane i < 8 carries row i's next write position
+    int32_t pos = (lane < 8 && br * 8 + lane < n) ? rp[br * 8 + lane - row_begin] : 0;
+    for (int64_t base = 0; base < nbc; base += 32) {
+        const int64_t bc = base + lane;
+        const bool present = bc < nbc && u01_key(k.kb, static_cast<uint64_t>(br * nbc + bc)) < p_block;
+        unsigned pb = __ballot_sync(0xffffffffu, present);
+        while (pb) {
+            const int src = __ffs(pb) - 1;
+            pb &= pb - 1;
+            const int64_t pbc = base + src;
+            const uint64_t blk = static_cast<uint64_t>(br * nbc + pbc);
+            const bool cell = pbc * 4 + lc < n && br * 8 + lr < n && u01_key(k.ke, blk * 32 + lane) < p_entry;
+            const unsigned cb = __ballot_sync(0xffffffffu, cell);
+            const int32_t row_pos = __shfl_sync(0xffffffffu, pos, lr);
+            if (cell) {
+                const int32_t p = row_pos + __popc(cb & (0xFu << (4 * lr)) & ((1u << lane) - 1u));
+                ci[p] = static_cast<int32_t>(pbc * 4 + lc);
+                v[p] = blocksparse_value_dev(k, outlier_fraction, blk * 32 + lane);
+            }
+            if (lane < 8) pos += __popc(cb & (0xFu << (4 * lane)));
+        }
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -337,7 +427,15 @@ int64_t cove_synth_rmat(int32_t scale, int32_t edge_factor, double a, double b, 
 
 int64_t cove_synth_blocksparse(int32_t n, double p_block, double p_entry, double outlier_fraction,
                                uint64_t seed, int64_t* rp, int32_t* ci, double* v) {
-    const int64_t nbr = (n + 7) / 8, nbc = (n + 3) / 4;
+    return cove_synth_blocksparse_rows(n, p_block, p_entry, outlier_fraction, seed, 0, n, rp, ci, v);
+}
+
+int64_t cove_synth_blocksparse_rows(int32_t n, double p_block, double p_entry, double outlier_fraction,
+                                    uint64_t seed, int64_t rb, int64_t re, int64_t* rp, int32_t* ci,
+                                    double* v) {
+    if (n < 0 || rb < 0 || re < rb || re > n || rb % 8 != 0 || (re % 8 != 0 && re != n)) return -1;
+    const int64_t nbc = (n + 3) / 4;
+    const int64_t br0 = rb / 8, br1 = (re + 7) / 8;
     const uint64_t kb = stream_key(seed, 0), ke = stream_key(seed, 1), kv = stream_key(seed, 2);
     const uint64_t ko = stream_key(seed, 3), ks = stream_key(seed, 4), km = stream_key(seed, 5);
     auto present_blocks = [&](int64_t br, std::vector<int32_t>& out) {
@@ -360,12 +458,13 @@ int64_t cove_synth_blocksparse(int32_t n, double p_block, double p_entry, double
         }
         return 1.0;
     };
-    std::vector<int64_t> rowcnt(n, 0);
+    const int64_t rows = re - rb;
+    std::vector<int64_t> rowcnt(rows, 0);
 #pragma omp parallel
     {
         std::vector<int32_t> blocks;
 #pragma omp for schedule(dynamic, 16)
-        for (int64_t br = 0; br < nbr; ++br) {
+        for (int64_t br = br0; br < br1; ++br) {
             present_blocks(br, blocks);
             for (int lr = 0; lr < 8; ++lr) {
                 const int64_t row = br * 8 + lr;
@@ -374,25 +473,25 @@ int64_t cove_synth_blocksparse(int32_t n, double p_block, double p_entry, double
                 for (int32_t bc : blocks)
                     for (int lc = 0; lc < 4; ++lc)
                         if (bc * 4 + lc < n && cell_present(br * nbc + bc, lr * 4 + lc)) ++cnt;
-                rowcnt[row] = cnt;
+                rowcnt[row - rb] = cnt;
             }
         }
     }
     int64_t nnz = 0;
-    for (int64_t r = 0; r < n; ++r) nnz += rowcnt[r];
+    for (int64_t r = 0; r < rows; ++r) nnz += rowcnt[r];
     if (!rp) return nnz;
     rp[0] = 0;
-    for (int64_t r = 0; r < n; ++r) rp[r + 1] = rp[r] + rowcnt[r];
+    for (int64_t r = 0; r < rows; ++r) rp[r + 1] = rp[r] + rowcnt[r];
 #pragma omp parallel
     {
         std::vector<int32_t> blocks;
 #pragma omp for schedule(dynamic, 16)
-        for (int64_t br = 0; br < nbr; ++br) {
+        for (int64_t br = br0; br < br1; ++br) {
             present_blocks(br, blocks);
             for (int lr = 0; lr < 8; ++lr) {
                 const int64_t row = br * 8 + lr;
                 if (row >= n) break;
-                int64_t p = rp[row];
+                int64_t p = rp[row - rb];
                 for (int32_t bc : blocks)
                     for (int lc = 0; lc < 4; ++lc) {
                         const int64_t blk = br * nbc + bc;
@@ -454,6 +553,52 @@ int cove_synth_lapl3d_device(int32_t nx, int32_t ny, int32_t nz, int64_t rb, int
         if (rows > 0) {
             lapl3d_fill_kernel<<<cove::grid_for(rows, 256), 256, 0, s>>>(nx, ny, nz, rb, rows, shift,
                                                                          dst, ci, v);
+            CUDA_LAUNCH_OK();
+        }
+        CUDA_OK(cudaStreamSynchronize(s));
+    });
+}
+
+int cove_synth_blocksparse_device(int32_t n, double p_block, double p_entry, double outlier_fraction,
+                                  uint64_t seed, int64_t rb, int64_t re, int32_t* rp, int32_t* ci,
+                                  double* v, int64_t* nnz_out, void* stream) {
+    return cove::guarded([&] {
+        if (n < 0 || rb < 0 || re < rb || re > n) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "bad row range");
+        if (rb % 8 != 0 || (re % 8 != 0 && re != n)) {
+            COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "row range must cover whole 8-row block rows");
+        }
+        const int64_t rows = re - rb;
+        const int64_t nbc = (static_cast<int64_t>(n) + 3) / 4;
+        const int64_t br0 = rb / 8, nbr_local = (re + 7) / 8 - br0;
+        const BlockSparseKeys k = blocksparse_keys(seed);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        cove::DevBuf cnt;
+        cove::alloc_n<int32_t>(cnt, rows);
+        const int grid = cove::grid_for(nbr_local * 32, 256);
+        if (rows > 0) {
+            blocksparse_count_kernel<<<grid, 256, 0, s>>>(n, nbc, p_block, p_entry, k, br0, nbr_local, rb,
+                                                          cnt.as<int32_t>());
+            CUDA_LAUNCH_OK();
+        }
+        cove::DevBuf tmp;
+        if (!rp) {
+            cove::alloc_n<int64_t>(tmp, rows + 1);
+            const int64_t nnz = cove::exclusive_scan_total<int32_t, int64_t>(cnt.as<int32_t>(), tmp.as<int64_t>(),
+                                                                            rows, s);
+            if (nnz_out) *nnz_out = nnz;
+            return;
+        }
+        // count into an int64 scan first: a block of more than INT32_MAX entries is refused
+        // before any int32 offset is written
+        cove::alloc_n<int64_t>(tmp, rows + 1);
+        const int64_t nnz = cove::exclusive_scan_total<int32_t, int64_t>(cnt.as<int32_t>(), tmp.as<int64_t>(), rows, s);
+        if (nnz > INT32_MAX) COVE_THROW(COVE_ERR_OVERFLOW, "row block exceeds int32 nnz");
+        cove::exclusive_scan_total<int32_t, int32_t>(cnt.as<int32_t>(), rp, rows, s);
+        if (nnz_out) *nnz_out = nnz;
+        if (rows > 0 && nnz > 0) {
+            if (!ci || !v) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "null col_idx/values");
+            blocksparse_fill_kernel<<<grid, 256, 0, s>>>(n, nbc, p_block, p_entry, outlier_fraction, k, br0,
+                                                         nbr_local, rb, rp, ci, v);
             CUDA_LAUNCH_OK();
         }
         CUDA_OK(cudaStreamSynchronize(s));

@@ -63,6 +63,14 @@ COVE_API int64_t cove_synth_blocksparse(int32_t n, double p_block, double p_entr
                                double outlier_fraction, uint64_t seed, int64_t* row_ptr,
                                int32_t* col_idx, double* values);
 
+/* Rows [row_begin, row_end) of the same matrix (row_ptr relative, rows + 1
+ * entries; global columns).  row_begin a multiple of 8, row_end a multiple
+ * of 8 or n.  Returns nnz (-1 for a bad range); null row_ptr counts only. */
+COVE_API int64_t cove_synth_blocksparse_rows(int32_t n, double p_block, double p_entry,
+                                    double outlier_fraction, uint64_t seed, int64_t row_begin,
+                                    int64_t row_end, int64_t* row_ptr, int32_t* col_idx,
+                                    double* values);
+
 /* Vectors.  kind 0: U[-1,1]; 1: U[0,1]; 2: N(0,1).  dtype 0 double, 1 float. */
 COVE_API void cove_synth_vector(int32_t kind, uint64_t seed, uint64_t stream, int64_t n, int32_t dtype,
                        void* out);
@@ -74,6 +82,16 @@ COVE_API void cove_synth_vector(int32_t kind, uint64_t seed, uint64_t stream, in
 COVE_API int cove_synth_lapl3d_device(int32_t nx, int32_t ny, int32_t nz, int64_t row_begin,
                              int64_t row_end, int64_t col_shift, int32_t* row_ptr,
                              int32_t* col_idx, double* values, int64_t* nnz_out, void* stream);
+
+/* Device generator of the block-sparse rows [row_begin, row_end) (same
+ * matrix and range rules as cove_synth_blocksparse_rows) into device
+ * buffers: int32 row_ptr relative to row_begin, global columns.  Returns the
+ * status (COVE_ERR_OVERFLOW above INT32_MAX entries); nnz through *nnz_out;
+ * null row_ptr counts only. */
+COVE_API int cove_synth_blocksparse_device(int32_t n, double p_block, double p_entry,
+                                  double outlier_fraction, uint64_t seed, int64_t row_begin,
+                                  int64_t row_end, int32_t* row_ptr, int32_t* col_idx,
+                                  double* values, int64_t* nnz_out, void* stream);
 
 /* Device U[-1,1] (kind 0) / U[0,1] (kind 1) vector of global indices
  * [begin, begin + n), double. */
