@@ -152,6 +152,15 @@ def run_reference_arm(args):
     if args.workload in ("lapl2d_512", "rmat_22"):
         rows, n, rp, ci, v, x = cb.workload(args.workload)
         wname = f"{args.workload} (rows={rows}, nnz={ci.size})"
+    elif args.workload == "blocksparse":
+        # 5.3e9 nnz do not fit host memory: a bounded sample of its first rows
+        bs = BLOCKSPARSE
+        n = args.bs_n or bs["n"]
+        rp, ci, v = cb.synth_blocksparse_rows(n, 0, min(n, 32768), bs["p_block"], bs["p_entry"],
+                                              bs["outlier_fraction"], bs["seed"])
+        rows = len(rp) - 1
+        x = cb.synth_vector("normal", n, seed=bs["seed"])
+        wname = f"block-sparse 8x4 n={n}, rows [0, {rows}) ({ci.size} nnz)"
     else:
         part = fem_partition(0, 1)
         rows, n, rp, ci, v = cb.synth_fem27_rows(part["nx"], part["ny"], part["nz"], part["dof"],

@@ -373,6 +373,16 @@ void build_plan_typed(cove_plan* P, const cove_csr_desc& d, cudaStream_t s) {
     P->nnz = P->full.nnz;
     P->nbr = P->full.nbr;
     build_split<T>(P->full, o, P->sp, s);
+    // only the counts of the full BitBSR are needed past the split; its
+    // arrays go before the codecs allocate theirs
+    P->has_full = o.keep_full_bitbsr != 0;
+    if (!P->has_full) {
+        P->full.block_col_idx.release();
+        P->full.bitmap.release();
+        P->full.values.release();
+        P->full.block_row_ptr.release();
+        P->full.block_row_val_ptr.release();
+    }
     build_layout(P->sp, P->nbr, o, P->lay, s);
     build_chunks(P->sp.res_row_ptr.as<int32_t>(), P->rows, o.long_row_split, kLongChunkNnz,
                  P->chunks, s);
@@ -477,16 +487,6 @@ void build_plan_typed(cove_plan* P, const cove_csr_desc& d, cudaStream_t s) {
         P->gate_evaluated = true;
         P->gate_pass = P->joint_rel >= 0.0 && P->joint_rel <= o.gate_tolerance;
         if (!P->gate_pass) P->dispatched_route = COVE_ROUTE_HYBRID;
-    }
-    if (!o.keep_full_bitbsr) {
-        P->full.block_col_idx.release();
-        P->full.bitmap.release();
-        P->full.values.release();
-        P->full.block_row_ptr.release();
-        P->full.block_row_val_ptr.release();
-        P->has_full = false;
-    } else {
-        P->has_full = true;
     }
     if (!o.keep_lossless && P->dispatched_route != COVE_ROUTE_HYBRID) {
         P->sp.kept_values.release();
