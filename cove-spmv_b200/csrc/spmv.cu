@@ -38,6 +38,13 @@ __device__ __forceinline__ float bf16_to_float(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }
 
+// float(q) for |q| < 2^22 with an integer add and a float subtract instead of
+// the int -> float conversion unit (its throughput bounds the BFP decoders):
+// adding q to the bit pattern of 1.5 * 2^23 adds q to its value, exactly.
+__device__ __forceinline__ float small_int_to_float(int q) {
+    return __int_as_float(0x4B400000 + q) - 12582912.0f;
+}
+
 // The four x values of a block column, as the accumulator type.  With
 // `vec` (x 16-byte aligned, cols a multiple of 4) they come from 16-byte
 // read-only vector loads; otherwise only the cells present in `nib`.
@@ -151,7 +158,7 @@ struct Bfp8Dec {
     }
     __device__ __forceinline__ float block_ctx(int64_t b) const { return bf16_to_float(scale[b]); }
     __device__ __forceinline__ float decode(V raw, float sc, int) const {
-        return static_cast<float>(raw) * sc;
+        return small_int_to_float(raw) * sc;
     }
     __device__ __forceinline__ float res_val(int64_t p) const { return bf16_to_float(res[p]); }
     __device__ __forceinline__ float xv(const T* __restrict__ x, int64_t c) const {
@@ -285,7 +292,7 @@ struct Bfp4Dec {
         prefetch_l2(packed + (a >> 1), ((b + 1) >> 1) - (a >> 1));
     }
     __device__ __forceinline__ float block_ctx(int64_t b) const { return bf16_to_float(scale[b]); }
-    __device__ __forceinline__ float decode(V raw, float sc, int) const { return static_cast<float>(raw) * sc; }
+    __device__ __forceinline__ float decode(V raw, float sc, int) const { return small_int_to_float(raw) * sc; }
     __device__ __forceinline__ float res_val(int64_t) const { return 0.0f; }
     __device__ __forceinline__ float xv(const T* __restrict__ x, int64_t col) const {
         return static_cast<float>(x[col]);
