@@ -390,38 +390,41 @@ float spmv_plans(const std::vector<cove_plan*>& plans, const double* xw, double*
 
 // y_local = A_local x_window on a partition: the block rows that read only
 // own columns are launched first, so the GPU computes them while the host
-// enqueues the halo on the (highest-priority) comm stream; the rest follow
-// once it has landed, then any overflow pass.
+// enqueues the halo on the (highest-priority) comm stream.  The halo block
+// rows follow the exchange on that same stream, beside the interior pass's
+// remaining waves (a short launch of its own would expose one block row's
+// serial load chain); the two passes write disjoint rows.  The compute
+// stream joins before any overflow pass.
 void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s, int route = -1) {
     if (!d->overlap) {
         halo(d, xw, s);
         spmv_plans(d->plans, xw, y, s, route);
         return;
     }
-    CUDA_OK(cudaEventRecord(d->x_ready, s));
-    for (int pass = 0; pass < 2; ++pass) {
-        if (pass == 1) {
-            CUDA_OK(cudaStreamWaitEvent(d->s_comm, d->x_ready, 0));
-            halo(d, xw, d->s_comm);
-            CUDA_OK(cudaEventRecord(d->halo_done, d->s_comm));
-            CUDA_OK(cudaStreamWaitEvent(s, d->halo_done, 0));
-        }
+    auto launch_ranges = [&](bool halo_rows, cudaStream_t st) {
         int64_t off = 0;
         for (size_t i = 0; i < d->plans.size(); ++i) {
             const cove_plan* P = d->plans[i];
             const KernelShape k = P->shape();
             const RouteValues rv = P->route_values(route_of(P, route));
             for (const auto& r : d->ranges[i]) {
-                if (r.halo != (pass == 1)) continue;
+                if (r.halo != halo_rows) continue;
                 KernelShape kr = k;
                 kr.part = 1;
                 kr.br_begin = r.b0;
                 kr.nbr = r.b1;
-                launch_hybrid_spmv(kr, rv, xw, y + off, s);
+                launch_hybrid_spmv(kr, rv, xw, y + off, st);
             }
             off += P->rows;
         }
-    }
+    };
+    CUDA_OK(cudaEventRecord(d->x_ready, s));
+    launch_ranges(false, s);
+    CUDA_OK(cudaStreamWaitEvent(d->s_comm, d->x_ready, 0));
+    halo(d, xw, d->s_comm);
+    launch_ranges(true, d->s_comm);
+    CUDA_OK(cudaEventRecord(d->halo_done, d->s_comm));
+    CUDA_OK(cudaStreamWaitEvent(s, d->halo_done, 0));
     int64_t off = 0;
     for (const cove_plan* P : d->plans) {
         const KernelShape k = P->shape();
