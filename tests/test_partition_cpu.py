@@ -53,6 +53,24 @@ def test_halo_plan_covers_windows():
         cb.halo_plan(0, bad)
 
 
+def test_halo_plan_for_a_window_of_all_columns():
+    """A general matrix partitioned by rows (every rank's window is all of
+    x): each rank receives every other rank's rows where they sit in x and
+    sends its own rows to each peer."""
+    import cove_b200 as cb
+
+    n = 1000
+    cuts = [0, 336, 664, n]
+    blocks = [(cuts[r], cuts[r + 1], 0, n) for r in range(3)]
+    for rank in range(3):
+        got = sorted(cb.halo_plan(rank, blocks))
+        peers = [q for q in range(3) if q != rank]
+        assert [t[0] for t in got] == peers
+        for peer, so, sn, ro, rn in got:
+            assert (so, sn) == (cuts[rank], cuts[rank + 1] - cuts[rank])
+            assert (ro, rn) == (cuts[peer], cuts[peer + 1] - cuts[peer])
+
+
 def _worker(rank, world, port, nx, ny, nz, iters, out_q, mode):
     sys.path.insert(0, os.path.join(ROOT, "cove-spmv_b200"))
     import scipy.sparse as sp
