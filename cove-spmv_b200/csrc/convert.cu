@@ -353,6 +353,43 @@ __device__ __forceinline__ int warp_incl_scan_i32(int v, int lane) {
     return v;
 }
 
+// Block rows with more than kSplitPiece blocks are split as pieces of
+// kSplitPiece blocks, a warp each (an R-MAT hub block row holds ~10^5
+// blocks: one warp would walk them serially); the others keep one warp per
+// block row.  Both walk their blocks with the loops below.
+constexpr int kSplitPiece = 2048;
+
+struct SplitCounts {
+    int kc = 0, kn = 0, rb = 0, sb = 0, sn = 0, fn = 0;
+    int run = 0;  // lane r < 8: residual entries of row r
+};
+
+__device__ __forceinline__ SplitCounts split_count_range(int b0, int b1, int32_t threshold,
+                                                         unsigned long long move_mask,
+                                                         const uint32_t* __restrict__ bitmap, int lane) {
+    SplitCounts c;
+    for (int base = b0; base < b1; base += 32) {
+        const int b = base + lane;
+        const bool valid = b < b1;
+        const uint32_t bm = valid ? bitmap[b] : 0u;
+        const int bn = __popc(bm);
+        const bool small = valid && bn <= threshold;
+        const bool moved = small && ((move_mask >> bn) & 1ULL);
+        const bool kept = valid && !moved;
+        c.kc += __popc(__ballot_sync(0xffffffffu, kept));
+        c.kn += __reduce_add_sync(0xffffffffu, kept ? bn : 0);
+        c.rb += __popc(__ballot_sync(0xffffffffu, moved));
+        c.sb += __popc(__ballot_sync(0xffffffffu, small && !moved));
+        c.sn += __reduce_add_sync(0xffffffffu, (small && !moved) ? bn : 0);
+        c.fn += __reduce_add_sync(0xffffffffu, bn);
+        uint64_t packed = moved ? nibble_counts(bm) : 0ULL;
+        packed = warp_incl_scan_u64(packed, lane);
+        const uint64_t tot = __shfl_sync(0xffffffffu, packed, 31);
+        c.run += static_cast<int>((tot >> (8 * (lane & 7))) & 0xFFu);
+    }
+    return c;
+}
+
 __global__ void split_count_kernel(int32_t rows, int32_t nbr, int32_t threshold,
                                    unsigned long long move_mask,
                                    const int32_t* __restrict__ brp,
@@ -367,69 +404,124 @@ __global__ void split_count_kernel(int32_t rows, int32_t nbr, int32_t threshold,
     const int lane = threadIdx.x & 31;
     if (br >= nbr) return;
     const int b0 = brp[br], b1 = brp[br + 1];
-    int kc = 0, kn = 0, rb = 0, sb = 0, sn = 0;
-    int run = 0;  // lane r < 8: residual entries of row r
-    for (int base = b0; base < b1; base += 32) {
-        const int b = base + lane;
-        const bool valid = b < b1;
-        const uint32_t bm = valid ? bitmap[b] : 0u;
-        const int bn = __popc(bm);
-        const bool small = valid && bn <= threshold;
-        const bool moved = small && ((move_mask >> bn) & 1ULL);
-        const bool kept = valid && !moved;
-        kc += __popc(__ballot_sync(0xffffffffu, kept));
-        kn += __reduce_add_sync(0xffffffffu, kept ? bn : 0);
-        rb += __popc(__ballot_sync(0xffffffffu, moved));
-        sb += __popc(__ballot_sync(0xffffffffu, small && !moved));
-        sn += __reduce_add_sync(0xffffffffu, (small && !moved) ? bn : 0);
-        uint64_t packed = moved ? nibble_counts(bm) : 0ULL;
-        packed = warp_incl_scan_u64(packed, lane);
-        const uint64_t tot = __shfl_sync(0xffffffffu, packed, 31);
-        run += static_cast<int>((tot >> (8 * (lane & 7))) & 0xFFu);
-    }
+    if (b1 - b0 > kSplitPiece) return;  // counted by pieces
+    const SplitCounts c = split_count_range(b0, b1, threshold, move_mask, bitmap, lane);
     if (lane == 0) {
-        kept_count[br] = kc;
-        kept_nnz[br] = kn;
-        res_blocks[br] = rb;
-        skipped_blocks[br] = sb;
-        skipped_nnz[br] = sn;
+        kept_count[br] = c.kc;
+        kept_nnz[br] = c.kn;
+        res_blocks[br] = c.rb;
+        skipped_blocks[br] = c.sb;
+        skipped_nnz[br] = c.sn;
     }
     if (lane < 8) {
         const int64_t row = br * kBlockRows + lane;
-        if (row < rows) res_count[row] = run;
+        if (row < rows) res_count[row] = c.run;
     }
 }
 
-template <typename T>
-__global__ void split_fill_kernel(int32_t rows, int32_t nbr, int32_t threshold,
-                                  unsigned long long move_mask,
-                                  const int32_t* __restrict__ brp,
-                                  const int32_t* __restrict__ brvp,
-                                  const int32_t* __restrict__ full_col,
-                                  const uint32_t* __restrict__ bitmap,
-                                  const T* __restrict__ full_values,
-                                  const int32_t* __restrict__ kept_brp,
-                                  const int32_t* __restrict__ kept_brvp,
-                                  const int32_t* __restrict__ res_rp,
-                                  int32_t* __restrict__ kept_col,
-                                  uint32_t* __restrict__ kept_bitmap,
-                                  T* __restrict__ kept_values,
-                                  int32_t* __restrict__ res_col,
-                                  T* __restrict__ res_values) {
-    __shared__ int s_base[kThreads / 32][8];
-    const int64_t br = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    const int w = threadIdx.x >> 5;
+// Pieces of the heavy block rows: count them, then list (block row, block range).
+__global__ void split_piece_count_kernel(int32_t nbr, const int32_t* __restrict__ brp, int32_t* __restrict__ np) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (br >= nbr) return;
-    if (lane < 8) {
-        const int64_t row = br * kBlockRows + lane;
-        s_base[w][lane] = row < rows ? res_rp[row] : 0;
-    }
-    __syncwarp();
+    const int n = brp[br + 1] - brp[br];
+    np[br] = n > kSplitPiece ? (n + kSplitPiece - 1) / kSplitPiece : 0;
+}
+
+__global__ void split_piece_list_kernel(int32_t nbr, const int32_t* __restrict__ brp,
+                                        const int64_t* __restrict__ first, int32_t* __restrict__ pbr,
+                                        int32_t* __restrict__ pb0, int32_t* __restrict__ pb1) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (br >= nbr) return;
     const int b0 = brp[br], b1 = brp[br + 1];
-    int kb = kept_brp[br];
-    int kv = kept_brvp[br];
-    int fv = brvp[br];
+    int64_t o = first[br];
+    for (int b = b0; o < first[br + 1]; b += kSplitPiece, ++o) {
+        pbr[o] = static_cast<int32_t>(br);
+        pb0[o] = b;
+        pb1[o] = min(b + kSplitPiece, b1);
+    }
+}
+
+// Per piece: kept blocks, kept nnz, full nnz, moved / skipped counts and the
+// eight rows' residual counts (pcnt[p * 14 + ...]).
+constexpr int kPieceFields = 14;
+
+__global__ void split_piece_count_pass(int64_t npieces, int32_t threshold, unsigned long long move_mask,
+                                       const int32_t* __restrict__ pb0, const int32_t* __restrict__ pb1,
+                                       const uint32_t* __restrict__ bitmap, int32_t* __restrict__ pcnt) {
+    const int64_t p = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (p >= npieces) return;
+    const SplitCounts c = split_count_range(pb0[p], pb1[p], threshold, move_mask, bitmap, lane);
+    int32_t* o = pcnt + p * kPieceFields;
+    if (lane == 0) {
+        o[0] = c.kc;
+        o[1] = c.kn;
+        o[2] = c.rb;
+        o[3] = c.sb;
+        o[4] = c.sn;
+        o[5] = c.fn;
+    }
+    if (lane < 8) o[6 + lane] = c.run;
+}
+
+// A heavy block row's totals (into the per-block-row and per-row counts the
+// scans read) and each piece's exclusive prefixes within its block row
+// (pcnt fields 0, 1, 5 and 6..13 are replaced by their prefixes).
+__global__ void split_piece_sum_kernel(int32_t rows, int32_t nbr, const int64_t* __restrict__ first,
+                                       int32_t* __restrict__ pcnt, int32_t* __restrict__ kept_count,
+                                       int32_t* __restrict__ kept_nnz, int32_t* __restrict__ res_count,
+                                       int32_t* __restrict__ res_blocks, int32_t* __restrict__ skipped_blocks,
+                                       int32_t* __restrict__ skipped_nnz) {
+    const int64_t br = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (br >= nbr) return;
+    const int64_t p0 = first[br], p1 = first[br + 1];
+    if (p0 == p1) return;
+    int kc = 0, kn = 0, rb = 0, sb = 0, sn = 0, fn = 0;
+    int run[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t p = p0; p < p1; ++p) {
+        int32_t* o = pcnt + p * kPieceFields;
+        const int c0 = o[0], c1 = o[1], c5 = o[5];
+        o[0] = kc;
+        o[1] = kn;
+        o[5] = fn;
+        kc += c0;
+        kn += c1;
+        fn += c5;
+        rb += o[2];
+        sb += o[3];
+        sn += o[4];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const int t = o[6 + r];
+            o[6 + r] = run[r];
+            run[r] += t;
+        }
+    }
+    kept_count[br] = kc;
+    kept_nnz[br] = kn;
+    res_blocks[br] = rb;
+    skipped_blocks[br] = sb;
+    skipped_nnz[br] = sn;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const int64_t row = br * kBlockRows + r;
+        if (row < rows) res_count[row] = run[r];
+    }
+}
+
+// Blocks [b0, b1) of block row br: kept blocks to kb / kv onward, moved
+// blocks' entries to the rows' residual positions s_base[0..7] onward
+// (shared, one set per warp; advanced here).  fv: the first value of b0.
+template <typename T>
+__device__ __forceinline__ void split_fill_range(int b0, int b1, int kb, int kv, int fv, int* s_base,
+                                                 int32_t threshold, unsigned long long move_mask,
+                                                 const int32_t* __restrict__ full_col,
+                                                 const uint32_t* __restrict__ bitmap,
+                                                 const T* __restrict__ full_values,
+                                                 int32_t* __restrict__ kept_col,
+                                                 uint32_t* __restrict__ kept_bitmap,
+                                                 T* __restrict__ kept_values, int32_t* __restrict__ res_col,
+                                                 T* __restrict__ res_values, int lane) {
     const unsigned lt = (1u << lane) - 1u;
     for (int base = b0; base < b1; base += 32) {
         const int b = base + lane;
@@ -461,7 +553,7 @@ __global__ void split_fill_kernel(int32_t rows, int32_t nbr, int32_t threshold,
                 const int c = bit & 3;
                 const uint32_t nib = (bm >> (4 * r)) & 0xFu;
                 const int within = __popc(nib & ((1u << c) - 1u));
-                const int dst = s_base[w][r] + static_cast<int>((p_excl >> (8 * r)) & 0xFFu) + within;
+                const int dst = s_base[r] + static_cast<int>((p_excl >> (8 * r)) & 0xFFu) + within;
                 res_col[dst] = bc * kBlockCols + c;
                 res_values[dst] = full_values[my_fv + rank];
                 ++rank;
@@ -473,9 +565,72 @@ __global__ void split_fill_kernel(int32_t rows, int32_t nbr, int32_t threshold,
         kv += __shfl_sync(0xffffffffu, kv_incl, 31);
         fv += __shfl_sync(0xffffffffu, fv_incl, 31);
         __syncwarp();
-        if (lane < 8) s_base[w][lane] += static_cast<int>((tot >> (8 * lane)) & 0xFFu);
+        if (lane < 8) s_base[lane] += static_cast<int>((tot >> (8 * lane)) & 0xFFu);
         __syncwarp();
     }
+}
+
+template <typename T>
+__global__ void split_fill_kernel(int32_t rows, int32_t nbr, int32_t threshold,
+                                  unsigned long long move_mask,
+                                  const int32_t* __restrict__ brp,
+                                  const int32_t* __restrict__ brvp,
+                                  const int32_t* __restrict__ full_col,
+                                  const uint32_t* __restrict__ bitmap,
+                                  const T* __restrict__ full_values,
+                                  const int32_t* __restrict__ kept_brp,
+                                  const int32_t* __restrict__ kept_brvp,
+                                  const int32_t* __restrict__ res_rp,
+                                  int32_t* __restrict__ kept_col,
+                                  uint32_t* __restrict__ kept_bitmap,
+                                  T* __restrict__ kept_values,
+                                  int32_t* __restrict__ res_col,
+                                  T* __restrict__ res_values) {
+    __shared__ int s_base[kThreads / 32][8];
+    const int64_t br = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int w = threadIdx.x >> 5;
+    if (br >= nbr) return;
+    const int b0 = brp[br], b1 = brp[br + 1];
+    if (b1 - b0 > kSplitPiece) return;  // filled by pieces
+    if (lane < 8) {
+        const int64_t row = br * kBlockRows + lane;
+        s_base[w][lane] = row < rows ? res_rp[row] : 0;
+    }
+    __syncwarp();
+    split_fill_range<T>(b0, b1, kept_brp[br], kept_brvp[br], brvp[br], s_base[w], threshold, move_mask,
+                        full_col, bitmap, full_values, kept_col, kept_bitmap, kept_values, res_col, res_values,
+                        lane);
+}
+
+template <typename T>
+__global__ void split_piece_fill_kernel(int32_t rows, int64_t npieces, int32_t threshold,
+                                        unsigned long long move_mask, const int32_t* __restrict__ pbr,
+                                        const int32_t* __restrict__ pb0, const int32_t* __restrict__ pb1,
+                                        const int32_t* __restrict__ pcnt, const int32_t* __restrict__ brvp,
+                                        const int32_t* __restrict__ full_col,
+                                        const uint32_t* __restrict__ bitmap,
+                                        const T* __restrict__ full_values,
+                                        const int32_t* __restrict__ kept_brp,
+                                        const int32_t* __restrict__ kept_brvp,
+                                        const int32_t* __restrict__ res_rp, int32_t* __restrict__ kept_col,
+                                        uint32_t* __restrict__ kept_bitmap, T* __restrict__ kept_values,
+                                        int32_t* __restrict__ res_col, T* __restrict__ res_values) {
+    __shared__ int s_base[kThreads / 32][8];
+    const int64_t p = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int w = threadIdx.x >> 5;
+    if (p >= npieces) return;
+    const int32_t* o = pcnt + p * kPieceFields;
+    const int64_t br = pbr[p];
+    if (lane < 8) {
+        const int64_t row = br * kBlockRows + lane;
+        s_base[w][lane] = row < rows ? res_rp[row] + o[6 + lane] : 0;
+    }
+    __syncwarp();
+    split_fill_range<T>(pb0[p], pb1[p], kept_brp[br] + o[0], kept_brvp[br] + o[1], brvp[br] + o[5], s_base[w],
+                        threshold, move_mask, full_col, bitmap, full_values, kept_col, kept_bitmap, kept_values,
+                        res_col, res_values, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -879,6 +1034,36 @@ void build_split(const FullBitBsr& f, const cove_plan_opts& o, SplitParts& out, 
             sb.as<int32_t>(), sn.as<int32_t>());
         CUDA_LAUNCH_OK();
     }
+    // heavy block rows: pieces of kSplitPiece blocks
+    DevBuf pbr, pb0, pb1, pcnt;
+    int64_t npieces = 0;
+    if (nbr > 0) {
+        DevBuf np, first;
+        alloc_n<int32_t>(np, nbr);
+        alloc_n<int64_t>(first, nbr + 1);
+        split_piece_count_kernel<<<grid_for(nbr, kThreads), kThreads, 0, s>>>(
+            nbr, f.block_row_ptr.as<int32_t>(), np.as<int32_t>());
+        CUDA_LAUNCH_OK();
+        npieces = exclusive_scan_total<int32_t, int64_t>(np.as<int32_t>(), first.as<int64_t>(), nbr, s);
+        if (npieces > 0) {
+            alloc_n<int32_t>(pbr, npieces);
+            alloc_n<int32_t>(pb0, npieces);
+            alloc_n<int32_t>(pb1, npieces);
+            alloc_n<int32_t>(pcnt, npieces * kPieceFields);
+            split_piece_list_kernel<<<grid_for(nbr, kThreads), kThreads, 0, s>>>(
+                nbr, f.block_row_ptr.as<int32_t>(), first.as<int64_t>(), pbr.as<int32_t>(), pb0.as<int32_t>(),
+                pb1.as<int32_t>());
+            CUDA_LAUNCH_OK();
+            split_piece_count_pass<<<grid_for(npieces * 32, kThreads), kThreads, 0, s>>>(
+                npieces, thr, mm, pb0.as<int32_t>(), pb1.as<int32_t>(), f.bitmap.as<uint32_t>(),
+                pcnt.as<int32_t>());
+            CUDA_LAUNCH_OK();
+            split_piece_sum_kernel<<<grid_for(nbr, kThreads), kThreads, 0, s>>>(
+                rows, nbr, first.as<int64_t>(), pcnt.as<int32_t>(), kc.as<int32_t>(), kn.as<int32_t>(),
+                rc.as<int32_t>(), rb.as<int32_t>(), sb.as<int32_t>(), sn.as<int32_t>());
+            CUDA_LAUNCH_OK();
+        }
+    }
     alloc_n<int32_t>(out.kept_block_row_ptr, nbr + 1);
     alloc_n<int32_t>(out.kept_block_row_val_ptr, nbr + 1);
     alloc_n<int32_t>(out.res_row_ptr, rows + 1);
@@ -910,6 +1095,16 @@ void build_split(const FullBitBsr& f, const cove_plan_opts& o, SplitParts& out, 
             out.kept_bitmap.as<uint32_t>(), out.kept_values.as<T>(), out.res_col.as<int32_t>(),
             out.res_values.as<T>());
         CUDA_LAUNCH_OK();
+        if (npieces > 0) {
+            split_piece_fill_kernel<T><<<grid_for(npieces * 32, kThreads), kThreads, 0, s>>>(
+                rows, npieces, thr, mm, pbr.as<int32_t>(), pb0.as<int32_t>(), pb1.as<int32_t>(),
+                pcnt.as<int32_t>(), f.block_row_val_ptr.as<int32_t>(), f.block_col_idx.as<int32_t>(),
+                f.bitmap.as<uint32_t>(), f.values.as<T>(), out.kept_block_row_ptr.as<int32_t>(),
+                out.kept_block_row_val_ptr.as<int32_t>(), out.res_row_ptr.as<int32_t>(),
+                out.kept_col.as<int32_t>(), out.kept_bitmap.as<uint32_t>(), out.kept_values.as<T>(),
+                out.res_col.as<int32_t>(), out.res_values.as<T>());
+            CUDA_LAUNCH_OK();
+        }
     }
     // BitBsrMatrix::block_val_ptr of the kept part
     alloc_n<int32_t>(out.kept_block_val_ptr, out.kept_blocks + 1);

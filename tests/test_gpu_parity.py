@@ -407,6 +407,10 @@ def test_heavy_block_rows_convert_in_pieces(zeros):
     assert np.array_equal(p.stream("full_bitmap"), b.bitmap_words)
     assert np.array_equal(p.stream("full_values"), b.values)
     assert np.array_equal(p.stream("full_block_row_val_ptr"), b.block_val_ptr[b.block_row_ptr])
+    # the split of these block rows (more than 2048 blocks: split in pieces)
+    assert_streams_equal_split(p, O.split(rows, cols, rp, ci, v), v.dtype)
+    pt = plan_for(rows, cols, rp, ci, v, split_policy="threshold", residual_threshold=2, value_codec="original")
+    assert_streams_equal_split(pt, O.split(rows, cols, rp, ci, v, threshold=2, use_cost=False), v.dtype)
     brp, brvp, col, bm, vals = _step_api_full(rows, cols, rp, ci, v)
     assert np.array_equal(brp, b.block_row_ptr) and np.array_equal(brvp, b.block_val_ptr[b.block_row_ptr])
     assert np.array_equal(col, b.block_col_idx) and np.array_equal(bm, b.bitmap_words)
@@ -464,6 +468,9 @@ def test_long_rows_and_heavy_block_rows_overflow_path():
     rp = np.array(rp, np.int64)
     ci = np.array(ci, np.int32)
     v = rng.standard_normal(ci.size)
+    # the dense block row (5000 kept blocks) is split in pieces
+    assert_streams_equal_split(plan_for(rows, cols, rp, ci, v, value_codec="original"),
+                               O.split(rows, cols, rp, ci, v), v.dtype)
     for codec in ("original", "bfp8_outlier"):
         p = plan_for(rows, cols, rp, ci, v, value_codec=codec, gate_enable=0)
         assert p.info.kernel_overflow_tasks > 0
