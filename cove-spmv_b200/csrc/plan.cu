@@ -168,18 +168,14 @@ HostPipeline::~HostPipeline() {
 
 namespace {
 
-// Slices for a vector of n elements of esz bytes: about 2^COVE_HOST_SLICE_SHIFT
-// bytes each, at most COVE_HOST_MAX_SLICES; x boundaries on 32-element multiples.
-#ifndef COVE_HOST_SLICE_SHIFT
-#define COVE_HOST_SLICE_SHIFT 20
-#endif
-#ifndef COVE_HOST_MAX_SLICES
-#define COVE_HOST_MAX_SLICES 8
-#endif
+// Slices for a vector of n elements of esz bytes: about 2^kHostSliceShift
+// bytes each, at most kHostMaxSlices; x boundaries on 32-element multiples.
+constexpr int kHostSliceShift = 20;
+constexpr int kHostMaxSlices = 8;
 int slice_count(int64_t n, size_t esz) {
     const int64_t bytes = n * static_cast<int64_t>(esz);
     return static_cast<int>(std::max<int64_t>(
-        1, std::min<int64_t>(COVE_HOST_MAX_SLICES, bytes >> COVE_HOST_SLICE_SHIFT)));
+        1, std::min<int64_t>(kHostMaxSlices, bytes >> kHostSliceShift)));
 }
 
 std::unique_ptr<HostPipeline> build_host_pipeline(const cove_plan* P) {

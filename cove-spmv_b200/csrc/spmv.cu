@@ -78,9 +78,6 @@ __device__ __forceinline__ void load_x4(const T* __restrict__ x, int64_t c4, boo
 // Hint: start pulling [p, p + bytes) into L2 before the dependent loads ask
 // for it.  The range is widened to 16-byte bounds; plan buffers are
 // 256-byte aligned and carry tail slack, so it stays inside the allocation.
-#ifndef L2PF
-#define L2PF 1
-#endif
 __device__ __forceinline__ void prefetch_l2(const void* p, int64_t bytes) {
     if (bytes <= 0) return;
     const uintptr_t a = reinterpret_cast<uintptr_t>(p);
@@ -323,7 +320,7 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
     if (b1 - b0 > k.heavy_limit) b1 = b0 + k.heavy_limit;
     int vb = k.kept_brvp[br];
     const uint64_t* __restrict__ words = k.words;
-    if constexpr (L2PF && Dec::kHasKept) {
+    if constexpr (Dec::kHasKept) {
         if (k.l2_prefetch && gl == 0) {  // the block row's words and values, in bulk
             prefetch_l2(words + b0, static_cast<int64_t>(b1 - b0) * 8);
             dec.prefetch_values(vb, k.kept_brvp[br + 1]);
