@@ -41,3 +41,12 @@ def test_reference_arm_other_ranks_exit_quietly():
                              env={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert rc == 0, err
     assert out.strip() == ""
+
+
+def test_reference_arm_for_the_cg_workload_uses_its_metric():
+    rc, out, err = run_bench("--impl", "reference", "--workload", "lapl3d_cg", "--grid", "32", "--steps", "1",
+                             "--warmup", "3")
+    assert rc == 0, err
+    d = json.loads(out.strip().splitlines()[-1])
+    assert (d["metric"], d["scaling"], d["unit"]) == ("cg_spmv_gflops", "strong", "GFLOP/s")
+    assert d["value"] > 0 and "planes [0, 8)" in d["config"]["workload"]
