@@ -4,8 +4,10 @@
 // 20-700, value_compression.hpp:105-198, selector main_gpu_spmv.cu:127-174).
 // The payloads are the plan fields run_bitbsr_spmv_once decodes; the
 // encodings (cell bit order, tile packing, bf16/fp16 rounding, BFP scales)
-// are the reference's formats, bit for bit.  The k-means codebook builders
-// (k256, global log-k-means) are not provided: their payloads still run.
+// are the reference's formats, bit for bit, and so are the k-means
+// codebooks of k256 and global log-k-means (value_compression.hpp:265-341,
+// 343-422, 452-497; gpu_value_codecs.cuh:693-744), whose steps are kept
+// in the same order so the same libm gives the same doubles.
 #pragma once
 
 #include "structural/bitbsr.hpp"
@@ -422,6 +424,164 @@ Bfp4BlkScaleValueCodec build_bfp4_blkscale_value_codec(const BitBsrMatrix<T>& bi
                        : static_cast<std::uint8_t>((byte & 0xF0) | nib);
     });
     return c;
+}
+
+// ---- k-means codebooks ---------------------------------------------------------
+
+namespace codec_detail {
+
+// Entry of the ascending `centers` nearest to v; at equal distance the lower.
+inline int nearest_center(const std::vector<double>& centers, double v) {
+    const auto it = std::lower_bound(centers.begin(), centers.end(), v);
+    if (it == centers.begin()) return 0;
+    if (it == centers.end()) return static_cast<int>(centers.size()) - 1;
+    const int hi = static_cast<int>(it - centers.begin());
+    return std::abs(v - centers[hi - 1]) <= std::abs(centers[hi] - v) ? hi - 1 : hi;
+}
+
+// One-dimensional k-means on a sample: at most k distinct values are their
+// own centres; otherwise the sorted sample is binned into equal-width bins
+// (bin sums in ascending order), the centres start at evenly spaced order
+// statistics, and each iteration moves every centre to the mean of the bins
+// whose mean lies nearest to it, then re-sorts the centres.
+inline std::vector<double> binned_kmeans_1d(std::vector<double> v, int k_wanted, int bins, int iterations) {
+    if (v.empty() || k_wanted <= 0) return {};
+    std::sort(v.begin(), v.end());
+    std::vector<double> distinct;
+    bool more = false;
+    for (const double a : v) {
+        if (!distinct.empty() && a == distinct.back()) continue;
+        if (static_cast<int>(distinct.size()) == k_wanted) {
+            more = true;
+            break;
+        }
+        distinct.push_back(a);
+    }
+    if (!more) return distinct;
+    const int k = std::min<int>(k_wanted, static_cast<int>(v.size()));
+    if (k <= 1 || v.front() == v.back()) return {v[v.size() / 2]};
+    bins = std::max(k * 16, std::min(bins, static_cast<int>(v.size())));
+    const double lo = v.front();
+    const double per_unit = static_cast<double>(bins - 1) / (v.back() - lo);
+    std::vector<Offset> count(static_cast<size_t>(bins), 0);
+    std::vector<double> total(static_cast<size_t>(bins), 0.0);
+    for (const double a : v) {
+        const int b = std::clamp(static_cast<int>((a - lo) * per_unit), 0, bins - 1);
+        ++count[static_cast<size_t>(b)];
+        total[static_cast<size_t>(b)] += a;
+    }
+    std::vector<double> c(static_cast<size_t>(k));
+    const long long last = static_cast<long long>(v.size() - 1);
+    for (int i = 0; i < k; ++i) c[static_cast<size_t>(i)] = v[static_cast<size_t>((i * last) / std::max(1, k - 1))];
+    std::sort(c.begin(), c.end());
+    std::vector<double> acc(static_cast<size_t>(k));
+    std::vector<Offset> hits(static_cast<size_t>(k));
+    for (int it = 0; it < iterations; ++it) {
+        std::fill(acc.begin(), acc.end(), 0.0);
+        std::fill(hits.begin(), hits.end(), 0);
+        for (int b = 0; b < bins; ++b) {
+            const Offset n = count[static_cast<size_t>(b)];
+            if (n == 0) continue;
+            const int j = nearest_center(c, total[static_cast<size_t>(b)] / static_cast<double>(n));
+            acc[static_cast<size_t>(j)] += total[static_cast<size_t>(b)];
+            hits[static_cast<size_t>(j)] += n;
+        }
+        for (int i = 0; i < k; ++i)
+            if (hits[static_cast<size_t>(i)] != 0)
+                c[static_cast<size_t>(i)] = acc[static_cast<size_t>(i)] / static_cast<double>(hits[static_cast<size_t>(i)]);
+        std::sort(c.begin(), c.end());
+    }
+    return c;
+}
+
+}  // namespace codec_detail
+
+template <typename T>
+struct K256Tile256BuildResult {
+    TileCodeValueCodec<8, T> tile;
+    int used_codebook_size = 0;
+};
+
+template <typename T>
+struct LogKmeansTile256BuildResult {
+    TileCodeValueCodec<8, T> tile;
+    int used_codebook_size = 0;
+};
+
+// 8-bit codes into a 256-slot codebook (unused slots zero): the distinct
+// values themselves when there are at most 256, else 256 k-means centres.
+template <typename T>
+K256Tile256BuildResult<T> build_k256_tile256_build_result(const BitBsrMatrix<T>& bitbsr) {
+    constexpr int kSlots = 256;
+    K256Tile256BuildResult<T> out;
+    const std::vector<T>& vals = bitbsr.values;
+    out.tile.codebook.assign(kSlots, T(0));
+    out.tile.value_ids.assign(vals.size(), 0);
+    out.tile.exact = false;
+    if (!vals.empty()) {
+        std::vector<double> sample;
+        sample.reserve(vals.size());
+        for (const T raw : vals) {
+            if (!std::isfinite(static_cast<double>(raw)))
+                throw std::runtime_error("K256 uint8 value codebook requires finite values");
+            sample.push_back(static_cast<double>(raw));
+        }
+        const auto u = sorted_unique_values(vals, kSlots);
+        if (static_cast<int>(u.size()) <= kSlots) {
+            out.tile.exact = true;
+            out.used_codebook_size = static_cast<int>(u.size());
+            std::copy(u.begin(), u.end(), out.tile.codebook.begin());
+            for (size_t i = 0; i < vals.size(); ++i)
+                out.tile.value_ids[i] =
+                    static_cast<std::uint32_t>(std::lower_bound(u.begin(), u.end(), vals[i]) - u.begin());
+        } else {
+            const auto centers = codec_detail::binned_kmeans_1d(std::move(sample), kSlots, 4096, 16);
+            out.used_codebook_size = static_cast<int>(centers.size());
+            for (size_t i = 0; i < centers.size(); ++i) out.tile.codebook[i] = static_cast<T>(centers[i]);
+            for (size_t i = 0; i < vals.size(); ++i)
+                out.tile.value_ids[i] =
+                    static_cast<std::uint32_t>(codec_detail::nearest_center(centers, static_cast<double>(vals[i])));
+        }
+    }
+    out.tile.tile_code_words = build_tile_code_words_from_value_ids<8>(bitbsr, out.tile.value_ids);
+    return out;
+}
+
+// 8-bit codes over signed magnitudes: k-means of log2|v| (k <= 128 centres),
+// codebook {-2^c, +2^c} per centre, code = 2 * centre + (v >= 0).
+template <typename T>
+LogKmeansTile256BuildResult<T> build_logkmeans_tile256_build_result(const BitBsrMatrix<T>& bitbsr, int requested_k,
+                                                                    int histogram_bins = 4096,
+                                                                    int iterations = 16) {
+    bitbsr.validate();
+    if (requested_k <= 0 || requested_k > 128)
+        throw std::runtime_error("global_logkmeans value codec requires k in [1, 128]");
+    std::vector<double> logs;
+    logs.reserve(bitbsr.values.size());
+    for (const T raw : bitbsr.values) {
+        const double a = static_cast<double>(raw);
+        if (!std::isfinite(a)) throw std::runtime_error("global_logkmeans value codec requires finite values");
+        if (a == 0.0) throw std::runtime_error("global_logkmeans value codec requires nonzero BitBSR values");
+        logs.push_back(std::log2(std::abs(a)));
+    }
+    const auto centers = codec_detail::binned_kmeans_1d(std::move(logs), requested_k, histogram_bins, iterations);
+    if (centers.size() * 2 > 256) throw std::runtime_error("global_logkmeans value codec exceeded the uint8 codebook size");
+    LogKmeansTile256BuildResult<T> out;
+    for (const double c : centers) {
+        const T m = static_cast<T>(std::exp2(c));
+        out.tile.codebook.push_back(-m);
+        out.tile.codebook.push_back(m);
+    }
+    out.used_codebook_size = static_cast<int>(out.tile.codebook.size());
+    out.tile.exact = false;
+    out.tile.value_ids.resize(bitbsr.values.size());
+    for (size_t i = 0; i < bitbsr.values.size(); ++i) {
+        const double a = static_cast<double>(bitbsr.values[i]);
+        const int j = codec_detail::nearest_center(centers, std::log2(std::abs(a)));
+        out.tile.value_ids[i] = static_cast<std::uint32_t>(j * 2 + (a < 0.0 ? 0 : 1));
+    }
+    out.tile.tile_code_words = build_tile_code_words_from_value_ids<8>(bitbsr, out.tile.value_ids);
+    return out;
 }
 
 }  // namespace structural

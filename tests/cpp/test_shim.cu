@@ -416,6 +416,50 @@ void test_family_builders() {
     same(build_round16_nnz_value_codec(b5, hf).values16, g_fp16_nnz, g_fp16_nnz_n, "fp16 nnz");
     same(build_round16_tile512_value_codec(b5, bf).tile_code_words, g_bf16_tile512, g_bf16_tile512_n, "bf16 tile512");
 
+    // k-means codebooks: k256 exact (3 values) and clustered (646 values into
+    // 256), global log-k-means with 16 and 128 centres and with 3 magnitudes
+    const auto k0 = build_k256_tile256_build_result(b0);
+    same_tile(k0.tile, g_k256_exact_codebook, g_k256_exact_codebook_n, g_k256_exact_words, g_k256_exact_words_n,
+              "k256 exact");
+    CHECK(k0.tile.exact && k0.used_codebook_size == g_k256_exact_used[0]);
+    const auto k5 = build_k256_tile256_build_result(b5);
+    same_tile(k5.tile, g_k256_kmeans_codebook, g_k256_kmeans_codebook_n, g_k256_kmeans_words, g_k256_kmeans_words_n,
+              "k256 k-means");
+    CHECK(!k5.tile.exact && k5.used_codebook_size == g_k256_kmeans_used[0]);
+    same_tile(build_logkmeans_tile256_build_result(b5, 16).tile, g_logk16_codebook, g_logk16_codebook_n,
+              g_logk16_words, g_logk16_words_n, "log-k-means 16");
+    same_tile(build_logkmeans_tile256_build_result(b5, 128).tile, g_logk128_codebook, g_logk128_codebook_n,
+              g_logk128_words, g_logk128_words_n, "log-k-means 128");
+    same_tile(build_logkmeans_tile256_build_result(b0, 8).tile, g_logk_exact_codebook, g_logk_exact_codebook_n,
+              g_logk_exact_words, g_logk_exact_words_n, "log-k-means exact");
+    {
+        // the clustered k256 payload runs as K256U8: y = A' x, A' the decoded values
+        DeviceBitBsrMatrix<double> d5;
+        golden_bitbsr(5, &d5);
+        std::vector<double> x(static_cast<size_t>(b5.cols));
+        for (size_t c = 0; c < x.size(); ++c) x[c] = (static_cast<int>(c % 7) - 3) * 0.25;
+        std::vector<double> expected(static_cast<size_t>(b5.rows), 0.0);
+        for (Index br = 0; br < b5.num_block_rows; ++br)
+            for (Offset b = b5.block_row_ptr[br]; b < b5.block_row_ptr[br + 1]; ++b) {
+                Offset k = b5.block_val_ptr[b];
+                for (int bit = 0; bit < 32; ++bit) {
+                    if (!(b5.bitmap_words[b] & (1u << bit))) continue;
+                    const double v = k5.tile.codebook[k5.tile.value_ids[static_cast<size_t>(k++)]];
+                    expected[static_cast<size_t>(br * 8 + bit / 4)] += v * x[static_cast<size_t>(b5.block_col_idx[b] * 4 + bit % 4)];
+                }
+            }
+        BitBsrSpmvPlan8x4<double> plan;
+        make_bitbsr_8x4_col_bitmap_packed(d5, plan.packed_col_bitmap_meta);
+        make_bitbsr_8x4_col_bitmap_flag_load_balance_work_items(d5, plan.load_balance, 32,
+                                                                 plan.packed_col_bitmap_meta);
+        plan.value_codec = BitBsrValueCodecKind8x4::K256U8;
+        plan.tile_code_words = k5.tile.tile_code_words;
+        plan.value_codebook = k5.tile.codebook;
+        thrust::device_vector<double> dx(x.begin(), x.end()), dy;
+        run_bitbsr_spmv_once(d5, plan, dx, dy);
+        close(expected, host(dy), 1e-12);
+    }
+
     // histogram and the auto_lossless choice (main_gpu_spmv.cu:127-174)
     using K = BitBsrValueCodecKind8x4;
     const int kinds[] = {4, 2, 3, 1, 0, 5};
