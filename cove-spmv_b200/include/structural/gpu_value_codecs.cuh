@@ -4,7 +4,8 @@
 // 20-700, value_compression.hpp:105-198, selector main_gpu_spmv.cu:127-174).
 // The payloads are the plan fields run_bitbsr_spmv_once decodes; the
 // encodings (cell bit order, tile packing, bf16/fp16 rounding, BFP scales)
-// are the reference's formats, bit for bit, and so are the k-means
+// are the reference's formats, bit for bit (BFP8 with global outliers
+// included), and so are the k-means
 // codebooks of k256 and global log-k-means (value_compression.hpp:265-341,
 // 343-422, 452-497; gpu_value_codecs.cuh:693-744), whose steps are kept
 // in the same order so the same libm gives the same doubles.
@@ -423,6 +424,85 @@ Bfp4BlkScaleValueCodec build_bfp4_blkscale_value_codec(const BitBsrMatrix<T>& bi
         byte = (k & 1) ? static_cast<std::uint8_t>((byte & 0x0F) | (nib << 4))
                        : static_cast<std::uint8_t>((byte & 0xF0) | nib);
     });
+    return c;
+}
+
+// ---- BFP8 with global outliers (gpu_value_codecs.cuh:319-461) -------------------
+// The largest fraction of |values| (above the (1 - fraction) order statistic)
+// leave the int8 stream (their slot is 0) for an exact side list of
+// (row, col, value) in block-row / block / bit order; block scales cover the
+// remaining values only.
+
+template <typename T>
+struct Bfp8OutlierBlkScaleValueCodec {
+    Offset nnz = 0;
+    Offset num_blocks = 0;
+    Offset num_outliers = 0;
+    std::vector<signed char> int8_values;
+    std::vector<std::uint16_t> block_scale_bf16;
+    std::vector<std::int32_t> outlier_rows;
+    std::vector<std::int32_t> outlier_cols;
+    std::vector<T> outlier_vals;
+    std::size_t payload_bytes() const {
+        return int8_values.size() + block_scale_bf16.size() * 2 +
+               static_cast<std::size_t>(num_outliers) * (8 + sizeof(T));
+    }
+    // positions come from the bitmap: only the exact values are extra
+    std::size_t value_only_payload_bytes() const {
+        return int8_values.size() + block_scale_bf16.size() * 2 + static_cast<std::size_t>(num_outliers) * sizeof(T);
+    }
+};
+
+template <typename T>
+Bfp8OutlierBlkScaleValueCodec<T> build_bfp8_outlier_blkscale_value_codec(const BitBsrMatrix<T>& bitbsr,
+                                                                         double outlier_fraction = 0.005) {
+    bitbsr.validate();
+    Bfp8OutlierBlkScaleValueCodec<T> c;
+    const Offset nnz = bitbsr.nnz();
+    c.nnz = nnz;
+    c.num_blocks = bitbsr.num_blocks();
+    c.int8_values.assign(static_cast<size_t>(nnz), 0);
+    c.block_scale_bf16.assign(static_cast<size_t>(c.num_blocks), 0);
+    std::vector<char> outlier(static_cast<size_t>(nnz), 0);
+    if (outlier_fraction > 0.0 && nnz > 0) {
+        std::vector<double> mag(static_cast<size_t>(nnz));
+        for (Offset k = 0; k < nnz; ++k) mag[static_cast<size_t>(k)] = std::abs(static_cast<double>(bitbsr.values[k]));
+        size_t at = static_cast<size_t>((1.0 - outlier_fraction) * static_cast<double>(nnz));
+        if (at >= mag.size()) at = mag.size() - 1;
+        std::vector<double> order(mag);
+        std::nth_element(order.begin(), order.begin() + static_cast<std::ptrdiff_t>(at), order.end());
+        const double threshold = order[at];
+        for (size_t k = 0; k < mag.size(); ++k) outlier[k] = mag[k] > threshold ? 1 : 0;
+    }
+    for (Offset b = 0; b < c.num_blocks; ++b) {
+        const Offset v0 = bitbsr.block_val_ptr[b], v1 = bitbsr.block_val_ptr[b + 1];
+        double top = 0.0;
+        for (Offset k = v0; k < v1; ++k)
+            if (!outlier[static_cast<size_t>(k)]) top = std::max(top, std::abs(static_cast<double>(bitbsr.values[k])));
+        float scale = static_cast<float>(top / 127.0);
+        if (scale == 0.0f) scale = 1.0f;
+        c.block_scale_bf16[static_cast<size_t>(b)] = float_to_bf16_bits(scale);
+        const double step = static_cast<double>(bf16_bits_to_float(c.block_scale_bf16[static_cast<size_t>(b)]));
+        for (Offset k = v0; k < v1; ++k) {
+            if (outlier[static_cast<size_t>(k)]) continue;  // slot stays 0
+            const long q = std::lround(static_cast<double>(bitbsr.values[k]) / step);
+            c.int8_values[static_cast<size_t>(k)] = static_cast<signed char>(std::max(-127L, std::min(127L, q)));
+        }
+    }
+    for (Index br = 0; br < bitbsr.num_block_rows; ++br)
+        for (Offset b = bitbsr.block_row_ptr[br]; b < bitbsr.block_row_ptr[br + 1]; ++b) {
+            const auto bm = static_cast<std::uint32_t>(bitbsr.bitmap_words[b]);
+            for (int bit = 0; bit < 32; ++bit) {
+                if (!(bm & (1u << bit))) continue;
+                const Offset k = bitbsr.block_val_ptr[b] + popcount_word(bm & ((1u << bit) - 1u));
+                if (!outlier[static_cast<size_t>(k)]) continue;
+                c.outlier_rows.push_back(static_cast<std::int32_t>(br * bitbsr.block_rows + bit / bitbsr.block_cols));
+                c.outlier_cols.push_back(
+                    static_cast<std::int32_t>(bitbsr.block_col_idx[b] * bitbsr.block_cols + bit % bitbsr.block_cols));
+                c.outlier_vals.push_back(bitbsr.values[static_cast<size_t>(k)]);
+            }
+        }
+    c.num_outliers = static_cast<Offset>(c.outlier_vals.size());
     return c;
 }
 

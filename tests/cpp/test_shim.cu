@@ -432,6 +432,21 @@ void test_family_builders() {
               g_logk128_words, g_logk128_words_n, "log-k-means 128");
     same_tile(build_logkmeans_tile256_build_result(b0, 8).tile, g_logk_exact_codebook, g_logk_exact_codebook_n,
               g_logk_exact_words, g_logk_exact_words_n, "log-k-means exact");
+    // BFP8 with global outliers: default fraction (2 outliers) and 5 % (31)
+    {
+        const auto o = build_bfp8_outlier_blkscale_value_codec(b5);
+        same(std::vector<int>(o.int8_values.begin(), o.int8_values.end()), g_bfp8o_q, g_bfp8o_q_n, "bfp8o q");
+        same(o.block_scale_bf16, g_bfp8o_scale, g_bfp8o_scale_n, "bfp8o scale");
+        same(o.outlier_rows, g_bfp8o_rows, g_bfp8o_rows_n, "bfp8o rows");
+        same(o.outlier_cols, g_bfp8o_cols, g_bfp8o_cols_n, "bfp8o cols");
+        same(o.outlier_vals, g_bfp8o_vals, g_bfp8o_vals_n, "bfp8o vals");
+        const auto o5 = build_bfp8_outlier_blkscale_value_codec(b5, 0.05);
+        same(std::vector<int>(o5.int8_values.begin(), o5.int8_values.end()), g_bfp8o5_q, g_bfp8o5_q_n, "bfp8o5 q");
+        same(o5.block_scale_bf16, g_bfp8o5_scale, g_bfp8o5_scale_n, "bfp8o5 scale");
+        same(o5.outlier_rows, g_bfp8o5_rows, g_bfp8o5_rows_n, "bfp8o5 rows");
+        same(o5.outlier_cols, g_bfp8o5_cols, g_bfp8o5_cols_n, "bfp8o5 cols");
+        same(o5.outlier_vals, g_bfp8o5_vals, g_bfp8o5_vals_n, "bfp8o5 vals");
+    }
     {
         // the clustered k256 payload runs as K256U8: y = A' x, A' the decoded values
         DeviceBitBsrMatrix<double> d5;
