@@ -1,0 +1,775 @@
+// struct_gpu_spmv -- command-line driver of the BitBSR-only family runner
+// (run_bitbsr_spmv_once over every value codec) and of the cuSPARSE CSR
+// baseline, with the reference CLI's options, operator contract and
+// key: value report (structural/src/main_gpu_spmv.cu, options
+// structural/include/structural/spmv_cli_options.hpp, operator naming
+// spmv_operator_plan.hpp), so run_gpu_spmv_family_sweep.py can drive this
+// build unchanged.  The BitBSR layouts run through the C++ shim
+// (include/structural/*) over the library's C ABI; x is the reference's
+// canonical input vector; every timed SpMV is a CUDA-event pair.
+#include "structural/gpu_convert.cuh"
+#include "structural/gpu_value_codecs.cuh"
+#include "structural/matrix_market.hpp"
+#include "structural/operators/bitbsr_spmv_8x4_dispatch.cuh"
+
+#include <cuda_runtime.h>
+#include <cusparse.h>
+#include <thrust/device_vector.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdlib>
+#include <iomanip>
+#include <iostream>
+#include <limits>
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <vector>
+
+namespace {
+
+using structural::Index;
+using structural::Offset;
+using Layout = structural::BitBsrSpmvLayoutKind8x4;
+using Codec = structural::BitBsrValueCodecKind8x4;
+
+// ---- options (spmv_cli_options.hpp) -----------------------------------------------
+
+struct Options {
+    std::string matrix_path;
+    std::string precision = "double";
+    std::string layout = "col_bitmap64_flag_lb";
+    std::string value_codec = "original";
+    int lb_chunk_blocks = 32;
+    int lb_split_threshold_blocks = -1;
+    std::string lb_policy = "manual";
+    bool lb_override = false;  // --lb-chunk-blocks or --lb-split-threshold-blocks given
+    std::string cusparse_alg = "default";
+    int warmup = 5;
+    int iterations = 20;
+    bool verify_cpu = false;
+};
+
+void usage(const char* argv0, std::ostream& os) {
+    os << "usage: " << argv0 << " MATRIX.mtx [--precision float|double]"
+       << " [--layout col_bitmap64|col_bitmap64_flag_lb|cusparse_csr]"
+       << " [--value-codec original|all_one|const_c|sign2|sign2_scale|dict2|dict4|dict16|"
+          "dict256_u8|dict65536_u16|auto_lossless|fp16|bf16|bfp8|bfp8_outlier|bfp4|codebook256_u8|"
+          "global_logkmeans16|global_logkmeans32|global_logkmeans64|global_logkmeans128]"
+       << " [--lb-policy manual|binary_implicit_one] [--lb-chunk-blocks N]"
+       << " [--lb-split-threshold-blocks N] [--cusparse-alg default|csr_alg1|csr_alg2]"
+       << " [--warmup N] [--iters N] [--verify-cpu]\n";
+}
+
+// Accepted spellings -> canonical names (the reference's alias tables).
+std::string canonical_layout(const std::string& s, std::string& alg) {
+    static const std::map<std::string, std::string> names = {
+        {"col_bitmap", "col_bitmap64"}, {"packed_abs", "col_bitmap64"}, {"abs_packed", "col_bitmap64"},
+        {"col_bitmap64", "col_bitmap64"}, {"col_bitmap64_packed", "col_bitmap64"},
+        {"col_bitmap_flag_lb", "col_bitmap64_flag_lb"}, {"packed_abs_flag_lb", "col_bitmap64_flag_lb"},
+        {"abs_packed_flag_lb", "col_bitmap64_flag_lb"}, {"col_bitmap64_flag_lb", "col_bitmap64_flag_lb"},
+        {"col_bitmap64_packed_flag_lb", "col_bitmap64_flag_lb"}, {"cusparse", "cusparse_csr"},
+        {"cusparse_spmv", "cusparse_csr"}, {"cusparse_csr", "cusparse_csr"}};
+    const auto it = names.find(s);
+    if (it != names.end()) return it->second;
+    if (s == "cusparse_csr_alg1" || s == "cusparse_alg1") {
+        alg = "csr_alg1";
+        return "cusparse_csr";
+    }
+    if (s == "cusparse_csr_alg2" || s == "cusparse_alg2") {
+        alg = "csr_alg2";
+        return "cusparse_csr";
+    }
+    throw std::runtime_error("layout must be col_bitmap64, col_bitmap64_flag_lb, or cusparse_csr");
+}
+
+std::string canonical_codec(const std::string& s) {
+    static const char* const kCanonical[] = {
+        "original", "all_one", "const_c", "sign2", "sign2_scale", "dict4", "dict2", "dict16", "dict256_u8",
+        "dict65536_u16", "auto_lossless", "fp16", "bf16", "bfp8", "bfp8_outlier", "bfp4", "codebook256_u8",
+        "global_logkmeans16", "global_logkmeans32", "global_logkmeans64", "global_logkmeans128"};
+    for (const char* c : kCanonical)
+        if (s == c) return s;
+    static const std::map<std::string, std::vector<std::string>> aliases = {
+        {"original", {"raw", "orig", "origin"}},
+        {"all_one", {"one", "pattern", "implicit1", "implicit_one"}},
+        {"const_c", {"dict1", "const", "constant", "constant_c"}},
+        {"sign2", {"sign", "sign_i8", "sign_tile32", "tile_sign"}},
+        {"sign2_scale", {"scaled_sign", "scaled_sign2", "sign_scale", "sign2_c"}},
+        {"dict2", {"code1", "u1", "unique2_tile32", "tile1", "unique2"}},
+        {"dict4", {"code2", "u2", "unique4_tile64", "ternary", "ternary3", "tile2", "unique4"}},
+        {"dict16", {"u4", "unique_u8", "unique16_tile128", "tile4", "unique16"}},
+        {"dict256_u8", {"dict256", "unique256", "unique256_tile256", "dict256_tile256", "exact_u8"}},
+        {"dict65536_u16",
+         {"dict65536", "dict_u16", "unique65536", "unique65536_tile512", "dict65536_tile512", "tile16", "exact_u16"}},
+        {"codebook256_u8", {"k256", "k256_uint8", "uint8", "u8", "k256_tile256", "tile8", "k256_u8"}},
+        {"fp16", {"half", "fp16_tile512"}},
+        {"bf16", {"bfloat16", "bf16_tile512"}},
+        {"bfp8", {"bfp8_blkscale", "int8_blkscale", "int8_8x4"}},
+        {"bfp8_outlier", {"bfp8_outlier_blkscale", "bfp8_outlier_lb", "int8_outlier", "bfp8_2pass"}},
+        {"bfp4", {"bfp4_blkscale", "int4_blkscale", "int4_8x4"}},
+        {"global_logkmeans16", {"logkmeans16", "log_kmeans16"}},
+        {"global_logkmeans32", {"logkmeans32", "log_kmeans32"}},
+        {"global_logkmeans64", {"logkmeans64", "log_kmeans64"}},
+        {"global_logkmeans128", {"logkmeans128", "log_kmeans128"}}};
+    for (const auto& [name, list] : aliases)
+        if (std::find(list.begin(), list.end(), s) != list.end()) return name;
+    throw std::runtime_error(
+        "value-codec must be original, all_one, const_c, sign2, sign2_scale, dict2, dict4, dict16, dict256_u8, "
+        "dict65536_u16, auto_lossless, fp16, bf16, codebook256_u8, or global_logkmeans{16,32,64,128}");
+}
+
+Options parse(int argc, char** argv) {
+    Options o;
+    if (argc < 2) {
+        usage(argv[0], std::cerr);
+        std::exit(2);
+    }
+    o.matrix_path = argv[1];
+    for (int i = 2; i < argc; ++i) {
+        const std::string a = argv[i];
+        const bool more = i + 1 < argc;
+        if (a == "--precision" && more) {
+            o.precision = argv[++i];
+            if (o.precision != "float" && o.precision != "double")
+                throw std::runtime_error("precision must be float or double");
+        } else if (a == "--layout" && more) {
+            o.layout = canonical_layout(argv[++i], o.cusparse_alg);
+        } else if (a == "--value-codec" && more) {
+            o.value_codec = canonical_codec(argv[++i]);
+        } else if ((a == "--lb-chunk-blocks" || a == "--chunk-blocks") && more) {
+            o.lb_chunk_blocks = std::stoi(argv[++i]);
+            o.lb_override = true;
+        } else if ((a == "--lb-split-threshold-blocks" || a == "--split-threshold-blocks" ||
+                    a == "--lb-split-threshold") && more) {
+            o.lb_split_threshold_blocks = std::stoi(argv[++i]);
+            o.lb_override = true;
+        } else if (a == "--lb-policy" && more) {
+            const std::string p = argv[++i];
+            if (p == "manual" || p == "binary_implicit_one") o.lb_policy = p;
+            else if (p == "binary" || p == "implicit_one" || p == "all_one" || p == "binary_one")
+                o.lb_policy = "binary_implicit_one";
+            else throw std::runtime_error("lb-policy must be manual or binary_implicit_one");
+        } else if (a == "--cusparse-alg" && more) {
+            const std::string g = argv[++i];
+            if (g == "default" || g == "csr_alg1" || g == "csr_alg2") o.cusparse_alg = g;
+            else if (g == "alg1") o.cusparse_alg = "csr_alg1";
+            else if (g == "alg2") o.cusparse_alg = "csr_alg2";
+            else throw std::runtime_error("cusparse-alg must be default, csr_alg1, or csr_alg2");
+        } else if (a == "--warmup" && more) {
+            o.warmup = std::stoi(argv[++i]);
+        } else if ((a == "--iters" || a == "--iterations") && more) {
+            o.iterations = std::stoi(argv[++i]);
+        } else if (a == "--verify-cpu") {
+            o.verify_cpu = true;
+        } else if (a == "--help" || a == "-h") {
+            usage(argv[0], std::cerr);
+            std::exit(0);
+        } else {
+            throw std::runtime_error("unknown or incomplete argument: " + a);
+        }
+    }
+    if (o.warmup < 0 || o.iterations <= 0)
+        throw std::runtime_error("warmup must be non-negative and iterations must be positive");
+    if (o.lb_chunk_blocks <= 0) throw std::runtime_error("lb-chunk-blocks must be positive");
+    if (o.lb_split_threshold_blocks < 0) o.lb_split_threshold_blocks = o.lb_chunk_blocks;
+    if (o.lb_split_threshold_blocks <= 0) throw std::runtime_error("lb-split-threshold-blocks must be positive");
+    return o;
+}
+
+Layout layout_kind(const std::string& s) {
+    if (s == "col_bitmap64") return Layout::ColBitmap64;
+    if (s == "col_bitmap64_flag_lb") return Layout::ColBitmap64FlagLb;
+    return Layout::CusparseCsr;
+}
+
+// canonical codec name <-> enum, in the enum's order
+const std::vector<std::pair<Codec, const char*>>& codec_names() {
+    static const std::vector<std::pair<Codec, const char*>> t = {
+        {Codec::Raw, "original"},          {Codec::ImplicitOne, "all_one"},
+        {Codec::ConstC, "const_c"},        {Codec::Sign2, "sign2"},
+        {Codec::Sign2Scale, "sign2_scale"}, {Codec::Dict2, "dict2"},
+        {Codec::Unique4, "dict4"},         {Codec::Unique16, "dict16"},
+        {Codec::Dict256U8, "dict256_u8"},  {Codec::Dict65536U16, "dict65536_u16"},
+        {Codec::Fp16, "fp16"},             {Codec::Bf16, "bf16"},
+        {Codec::Bfp8, "bfp8"},             {Codec::Bfp8Outlier, "bfp8_outlier"},
+        {Codec::Bfp4, "bfp4"},             {Codec::K256U8, "codebook256_u8"},
+        {Codec::GlobalLogKmeans16, "global_logkmeans16"}, {Codec::GlobalLogKmeans32, "global_logkmeans32"},
+        {Codec::GlobalLogKmeans64, "global_logkmeans64"}, {Codec::GlobalLogKmeans128, "global_logkmeans128"}};
+    return t;
+}
+Codec codec_kind(const std::string& s) {
+    for (const auto& [k, n] : codec_names())
+        if (s == n) return k;
+    throw std::runtime_error("internal error: unknown normalized value codec");
+}
+const char* codec_name(Codec c) {
+    for (const auto& [k, n] : codec_names())
+        if (k == c) return n;
+    return "unknown";
+}
+
+// ---- operator contract (spmv_operator_plan.hpp) -----------------------------------
+
+struct OperatorSpec {
+    std::string name;
+    const char* family = "load_balanced_traversal";
+    const char* promotion = "promoted";
+    const char* runner = "bitbsr_original_traversal";
+    bool lossy_gate = false;  // spmv_max_rel, else exact_abs_or_rel
+};
+
+OperatorSpec operator_spec(Layout layout, Codec codec, bool binary_policy) {
+    if (binary_policy && (layout != Layout::ColBitmap64FlagLb || codec != Codec::ImplicitOne))
+        throw std::runtime_error(
+            "lb-policy binary_implicit_one requires col_bitmap64_flag_lb layout and all_one value codec");
+    const bool non_raw = codec != Codec::Raw;
+    if (layout == Layout::CusparseCsr && non_raw)
+        throw std::runtime_error("compressed value codecs are only supported for BitBSR layouts");
+    OperatorSpec s;
+    s.lossy_gate = structural::bitbsr_spmv_8x4_is_controlled_lossy_value_codec(codec);
+    if (layout == Layout::CusparseCsr) {
+        s.name = "cusparse_csr";
+        s.family = "external_baseline";
+        s.promotion = "external_baseline";
+        s.runner = "cusparse_csr";
+        return s;
+    }
+    const bool lb = layout == Layout::ColBitmap64FlagLb;
+    s.name = std::string(codec_name(codec)) + (lb ? "_lb" : "_nolb");
+    if (s.lossy_gate) {
+        s.family = "controlled_lossy_value_specialized";
+        s.promotion = "buildable_needs_report";
+        s.runner = "bitbsr_value_specialized";
+    } else if (non_raw) {
+        s.family = "lossless_value_specialized";
+        s.promotion = binary_policy ? "promoted" : "buildable_needs_report";
+        s.runner = "bitbsr_value_specialized";
+    } else if (!lb) {
+        s.family = "non_load_balanced_traversal";
+        s.promotion = "buildable_needs_report";
+    }
+    return s;
+}
+
+// Load-balance chunking for binary all-one matrices (load_balance_policy.hpp:
+// the reference's calibrated table of chunk sizes by block count and blocks
+// per block row); 32 / 32 where no rule applies.
+std::pair<int, int> binary_implicit_one_chunks(Offset num_blocks, Index rows) {
+    if (num_blocks <= 0 || rows <= 0) return {32, 32};
+    const double per_row = static_cast<double>(num_blocks) / std::max<Index>((rows + 7) / 8, 1);
+    auto c = [](int n) { return std::make_pair(n, n); };
+    if (num_blocks < 30000) return c(8);
+    if (per_row >= 20000.0 && num_blocks >= 700000) return c(128);
+    if (per_row >= 6000.0) {
+        if (num_blocks >= 400000) return c(128);
+        if (num_blocks >= 250000) return c(64);
+    }
+    if (per_row >= 500.0) {
+        if (num_blocks < 120000) return c(16);
+        if (num_blocks >= 3000000) return c(64);
+        return {32, 32};
+    }
+    if (num_blocks >= 8000000 && per_row >= 128.0) return c(128);
+    if (num_blocks >= 3000000) return c(64);
+    return {32, 32};
+}
+
+// ---- shared pieces ------------------------------------------------------------------
+
+void cuda_ok(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+void cusparse_ok(cusparseStatus_t s, const char* what) {
+    if (s != CUSPARSE_STATUS_SUCCESS) throw std::runtime_error(std::string("cuSPARSE ") + what + " failed");
+}
+
+template <typename F>
+auto timed_host(F&& f, double& ms) {
+    const auto t0 = std::chrono::steady_clock::now();
+    auto r = f();
+    ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return r;
+}
+
+template <typename T>
+std::vector<T> canonical_x(Index n) {  // spmv_harness.hpp:32-39
+    std::vector<T> x(static_cast<size_t>(n));
+    for (Index i = 0; i < n; ++i) x[static_cast<size_t>(i)] = static_cast<T>(static_cast<int>(i % 17) - 8) * static_cast<T>(0.125);
+    return x;
+}
+
+struct Verify {
+    bool run = false, pass = true;
+    double max_abs = 0, max_rel = 0, global_rel = 0, cpu_ms = 0;
+};
+
+// y0 = A x in T on the host (spmv_csr), compared with the device y by the
+// library's compare (max_abs, max_rel, global_rel of spmv.hpp:73-89).
+template <typename T>
+Verify verify(const structural::CsrMatrix<T>& a, const std::vector<T>& x, const thrust::device_vector<T>& d_y,
+              bool lossy_gate) {
+    Verify v;
+    v.run = true;
+    std::vector<T> y0(static_cast<size_t>(a.rows));
+    timed_host([&] {
+#pragma omp parallel for schedule(static)
+        for (Index r = 0; r < a.rows; ++r) {
+            T s = T(0);
+            for (Offset p = a.row_ptr[r]; p < a.row_ptr[r + 1]; ++p) s += a.values[p] * x[a.col_idx[p]];
+            y0[static_cast<size_t>(r)] = s;
+        }
+        return 0;
+    }, v.cpu_ms);
+    thrust::device_vector<T> d_y0(y0.begin(), y0.end());
+    double e[3] = {0, 0, 0};
+    const cove_status st = cove_compare_vectors(thrust::raw_pointer_cast(d_y0.data()),
+                                                thrust::raw_pointer_cast(d_y.data()), a.rows,
+                                                sizeof(T) == 8 ? COVE_F64 : COVE_F32, e, nullptr);
+    if (st != COVE_OK) throw std::runtime_error(cove_last_error());
+    v.max_abs = e[0];
+    v.max_rel = e[1];
+    v.global_rel = e[2];
+    if (lossy_gate) {
+        v.pass = v.global_rel <= 1e-2;
+    } else {
+        const double abs_tol = sizeof(T) == 4 ? 1e-2 : 1e-9, rel_tol = sizeof(T) == 4 ? 1e-4 : 1e-10;
+        v.pass = v.max_abs <= abs_tol || v.max_rel <= rel_tol;
+    }
+    return v;
+}
+
+template <typename T>
+void print_matrix_header(const Options& o, const structural::MatrixMarketLoadResult<T>& m, const char* block) {
+    std::cout << "report_schema: structural_spmv_cli_v3\n";
+    std::cout << "matrix: " << o.matrix_path << "\n";
+    std::cout << "matrix_market_field: " << structural::to_string(m.info.field) << "\n";
+    std::cout << "matrix_market_symmetry: " << structural::to_string(m.info.symmetry) << "\n";
+    std::cout << "precision: " << o.precision << "\n";
+    std::cout << "shape: " << m.matrix.rows << " x " << m.matrix.cols << "\n";
+    std::cout << "nnz: " << m.matrix.nnz() << "\n";
+    std::cout << "block: " << block << "\n";
+}
+
+void print_contract(const OperatorSpec& s) {
+    std::cout << "operator_name: " << s.name << "\n";
+    std::cout << "operator_family: " << s.family << "\n";
+    std::cout << "operator_promotion_status: " << s.promotion << "\n";
+    std::cout << "operator_runner: " << s.runner << "\n";
+}
+
+void print_verify(const Verify& v) {
+    if (!v.run) {
+        std::cout << "verify_cpu: SKIP\n";
+        return;
+    }
+    std::cout << std::defaultfloat;
+    std::cout << "verify_cpu: " << (v.pass ? "PASS" : "FAIL") << ", max_abs=" << v.max_abs
+              << ", max_rel=" << v.max_rel << "\n";
+    std::cout << "spmv_output_rel_err: " << v.global_rel << "\n";
+}
+
+// Warm-up and timed launches of `once(iter_ms)`; returns {sum, min}.
+template <typename F>
+std::pair<double, float> time_loop(const Options& o, F&& once) {
+    for (int i = 0; i < o.warmup; ++i) once(nullptr);
+    double sum = 0.0;
+    float mn = std::numeric_limits<float>::max();
+    for (int i = 0; i < o.iterations; ++i) {
+        float ms = 0.0f;
+        once(&ms);
+        sum += ms;
+        mn = std::min(mn, ms);
+    }
+    return {sum, mn};
+}
+
+// ---- cuSPARSE CSR baseline ---------------------------------------------------------
+
+template <typename T>
+int run_cusparse(const Options& o, const OperatorSpec& spec) {
+    if (o.value_codec != "original")
+        throw std::runtime_error("compressed value codecs are only supported for BitBSR layouts");
+    double load_ms = 0, ctx_ms = 0, upload_ms = 0, setup_ms = 0, pre_ms = 0;
+    float pre_event_ms = 0.0f;
+    const auto m = timed_host([&] { return structural::read_matrix_market_with_info<T>(o.matrix_path); }, load_ms);
+    const auto& a = m.matrix;
+    timed_host([&] { cuda_ok(cudaFree(nullptr), "CUDA context"); return 0; }, ctx_ms);
+    const auto x = canonical_x<T>(a.cols);
+    thrust::device_vector<Offset> d_rp;
+    thrust::device_vector<Index> d_ci;
+    thrust::device_vector<T> d_v, d_x, d_y;
+    timed_host([&] {
+        d_rp = a.row_ptr;
+        d_ci = a.col_idx;
+        d_v = a.values;
+        d_x = x;
+        d_y.assign(static_cast<size_t>(a.rows), T(0));
+        return 0;
+    }, upload_ms);
+    const cudaDataType vt = sizeof(T) == 8 ? CUDA_R_64F : CUDA_R_32F;
+    const cusparseSpMVAlg_t alg = o.cusparse_alg == "csr_alg1"   ? CUSPARSE_SPMV_CSR_ALG1
+                                  : o.cusparse_alg == "csr_alg2" ? CUSPARSE_SPMV_CSR_ALG2
+                                                                 : CUSPARSE_SPMV_ALG_DEFAULT;
+    cusparseHandle_t h = nullptr;
+    cusparseSpMatDescr_t ma = nullptr;
+    cusparseDnVecDescr_t vx = nullptr, vy = nullptr;
+    size_t buf_bytes = 0;
+    const T alpha = T(1), beta = T(0);
+    timed_host([&] {
+        cusparse_ok(cusparseCreate(&h), "create");
+        cusparse_ok(cusparseCreateCsr(&ma, a.rows, a.cols, a.nnz(), thrust::raw_pointer_cast(d_rp.data()),
+                                      thrust::raw_pointer_cast(d_ci.data()), thrust::raw_pointer_cast(d_v.data()),
+                                      CUSPARSE_INDEX_32I, CUSPARSE_INDEX_32I, CUSPARSE_INDEX_BASE_ZERO, vt),
+                    "create CSR");
+        cusparse_ok(cusparseCreateDnVec(&vx, a.cols, thrust::raw_pointer_cast(d_x.data()), vt), "create x");
+        cusparse_ok(cusparseCreateDnVec(&vy, a.rows, thrust::raw_pointer_cast(d_y.data()), vt), "create y");
+        cusparse_ok(cusparseSpMV_bufferSize(h, CUSPARSE_OPERATION_NON_TRANSPOSE, &alpha, ma, vx, &beta, vy, vt, alg,
+                                            &buf_bytes),
+                    "buffer size");
+        return 0;
+    }, setup_ms);
+    thrust::device_vector<std::uint8_t> buf(buf_bytes);
+    void* bp = buf_bytes ? thrust::raw_pointer_cast(buf.data()) : nullptr;
+    cudaEvent_t e0, e1;
+    cuda_ok(cudaEventCreate(&e0), "event");
+    cuda_ok(cudaEventCreate(&e1), "event");
+    timed_host([&] {
+#if defined(CUSPARSE_VERSION) && CUSPARSE_VERSION >= 12700
+        cuda_ok(cudaEventRecord(e0), "event");
+        cusparse_ok(cusparseSpMV_preprocess(h, CUSPARSE_OPERATION_NON_TRANSPOSE, &alpha, ma, vx, &beta, vy, vt, alg, bp),
+                    "preprocess");
+        cuda_ok(cudaEventRecord(e1), "event");
+        cuda_ok(cudaEventSynchronize(e1), "event");
+        cuda_ok(cudaEventElapsedTime(&pre_event_ms, e0, e1), "event");
+#endif
+        return 0;
+    }, pre_ms);
+    const auto [sum_ms, min_ms] = time_loop(o, [&](float* ms) {
+        if (ms) cuda_ok(cudaEventRecord(e0), "event");
+        cusparse_ok(cusparseSpMV(h, CUSPARSE_OPERATION_NON_TRANSPOSE, &alpha, ma, vx, &beta, vy, vt, alg, bp), "SpMV");
+        if (ms) {
+            cuda_ok(cudaEventRecord(e1), "event");
+            cuda_ok(cudaEventSynchronize(e1), "event");
+            cuda_ok(cudaEventElapsedTime(ms, e0, e1), "event");
+        }
+    });
+    cuda_ok(cudaDeviceSynchronize(), "SpMV");
+    Verify v;
+    if (o.verify_cpu) v = verify(a, x, d_y, spec.lossy_gate);
+
+    print_matrix_header(o, m, "csr");
+    print_contract(spec);
+    std::cout << "spmv_layout: " << o.layout << "\n";
+    std::cout << "spmv_effective_layout: cusparse_csr\n";
+    std::cout << "position_codec: csr\n";
+    std::cout << "position_codec_exact: true\n";
+    std::cout << "position_codec_payload_bytes: "
+              << static_cast<size_t>(a.rows + 1) * sizeof(Offset) + static_cast<size_t>(a.nnz()) * sizeof(Index) << "\n";
+    std::cout << "value_codec: original\n";
+    std::cout << "value_codec_exact: true\n";
+    std::cout << "value_codec_codebook_size: 0\n";
+    std::cout << "value_codec_payload_bytes: " << static_cast<size_t>(a.nnz()) * sizeof(T) << "\n";
+    std::cout << "value_codec_bytes_per_nnz: " << sizeof(T) << "\n";
+    std::cout << "cusparse_alg: " << o.cusparse_alg << "\n";
+    std::cout << "cusparse_buffer_bytes: " << buf_bytes << "\n";
+    std::cout << "load_balance_policy: manual\n";
+    std::cout << "load_balance_chunk_blocks: 0\n";
+    std::cout << "load_balance_split_threshold_blocks: 0\n";
+    std::cout << "gpu_work_items: 0\n";
+    std::cout << "gpu_output_residency: device\n";
+    std::cout << "gpu_num_blocks: 0\n";
+    std::cout << "verify_gate: " << (spec.lossy_gate ? "spmv_max_rel" : "exact_abs_or_rel") << "\n";
+    std::cout << "timing_scope: cusparse_event_includes_beta_zero\n";
+    std::cout << std::fixed << std::setprecision(4);
+    std::cout << "timing_ms: load=" << load_ms << ", cuda_context=" << ctx_ms
+              << ", gpu_convert_host=0.0000, gpu_convert_event=0.0000, csr_upload_host=" << upload_ms
+              << ", cusparse_setup_host=" << setup_ms << ", cusparse_preprocess_host=" << pre_ms
+              << ", cusparse_preprocess_event=" << pre_event_ms
+              << ", col_bitmap_pack_host=0.0000, col_bitmap_pack_event=0.0000, load_balance_pack_host=0.0000"
+              << ", load_balance_pack_event=0.0000, value_codec_pack_host=0.0000"
+              << ", gpu_spmv_avg_event=" << (sum_ms / o.iterations) << ", gpu_spmv_min_event=" << min_ms
+              << ", cpu_spmv=" << (o.verify_cpu ? v.cpu_ms : 0.0) << "\n";
+    print_verify(v);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cusparseDestroyDnVec(vy);
+    cusparseDestroyDnVec(vx);
+    cusparseDestroySpMat(ma);
+    cusparseDestroy(h);
+    return v.pass ? 0 : 1;
+}
+
+// ---- BitBSR family runner ----------------------------------------------------------
+
+struct Report {
+    bool auto_selected = false;
+    int auto_unique_count = 0;
+    bool auto_unique_overflow = false;
+    size_t auto_raw_bytes = 0, auto_candidate_bytes = 0;
+    size_t position_bytes = 0;
+    bool exact = false;
+    int codebook_size = 0;
+    size_t payload_bytes = 0;
+    bool value_only_valid = false;
+    size_t value_only_bytes = 0;
+    long long num_outliers = 0;
+};
+
+struct Timing {
+    double load = 0, ctx = 0, convert_host = 0, auto_host = 0, pack_host = 0, lb_host = 0, codec_host = 0;
+    float convert_event = 0, auto_event = 0, pack_event = 0, lb_event = 0;
+};
+
+size_t candidate_bytes(const structural::DeviceExactValueHistogram& h, Codec c) {
+    switch (c) {
+        case Codec::ImplicitOne: return 0;
+        case Codec::ConstC: return h.const_c_payload_bytes;
+        case Codec::Sign2: return h.sign2_payload_bytes;
+        case Codec::Sign2Scale: return h.sign2_scale_payload_bytes;
+        case Codec::Dict2: return h.dict2_payload_bytes;
+        case Codec::Unique4: return h.dict4_payload_bytes;
+        case Codec::Unique16: return h.dict16_payload_bytes;
+        case Codec::Dict256U8: return h.dict256_u8_payload_bytes;
+        case Codec::Dict65536U16: return h.dict65536_u16_payload_bytes;
+        default: return h.raw_payload_bytes;
+    }
+}
+
+// The value payload of `codec` built on the host from the BitBSR values and
+// loaded into the plan (main_gpu_spmv.cu:631-848 lists the same fields).
+template <typename T>
+void build_values(const structural::BitBsrMatrix<T>& b, Codec codec, structural::BitBsrSpmvPlan8x4<T>& plan,
+                  Report& r) {
+    using namespace structural;
+    auto load_tile = [&](const auto& t) {
+        plan.tile_code_words.assign(t.tile_code_words.begin(), t.tile_code_words.end());
+        plan.value_codebook.assign(t.codebook.begin(), t.codebook.end());
+    };
+    r.exact = !bitbsr_spmv_8x4_is_controlled_lossy_value_codec(codec);
+    switch (codec) {
+        case Codec::ImplicitOne:
+            for (const T v : b.values)
+                if (v != T(1)) throw std::runtime_error("all_one value codec requires every stored value to be 1");
+            r.codebook_size = 0;
+            r.payload_bytes = 0;
+            break;
+        case Codec::ConstC:
+            plan.value_scale = build_const_c_value(b);
+            r.codebook_size = 1;
+            r.payload_bytes = sizeof(T);
+            break;
+        case Codec::Sign2: {
+            const auto m = build_sign2_tile32_masks(b);
+            plan.sign_masks.assign(m.begin(), m.end());
+            r.payload_bytes = m.size() * 4;
+            break;
+        }
+        case Codec::Sign2Scale: {
+            const auto c = build_sign2_scale_tile32_value_codec(b);
+            plan.value_scale = c.scale;
+            plan.sign_masks.assign(c.sign_masks.begin(), c.sign_masks.end());
+            r.codebook_size = 1;
+            r.payload_bytes = c.sign_masks.size() * 4 + sizeof(T);
+            break;
+        }
+        case Codec::Dict2: { const auto c = build_dict2_tile32_value_codec(b); load_tile(c); r.codebook_size = static_cast<int>(c.codebook.size()); r.payload_bytes = c.payload_bytes(); break; }
+        case Codec::Unique4: { const auto c = build_unique4_tile64_value_codec(b); load_tile(c); r.codebook_size = static_cast<int>(c.codebook.size()); r.payload_bytes = c.payload_bytes(); break; }
+        case Codec::Unique16: { const auto c = build_unique16_tile128_value_codec(b); load_tile(c); r.codebook_size = static_cast<int>(c.codebook.size()); r.payload_bytes = c.payload_bytes(); break; }
+        case Codec::Dict256U8: { const auto c = build_dict256_tile256_value_codec(b); load_tile(c); r.codebook_size = static_cast<int>(c.codebook.size()); r.payload_bytes = c.payload_bytes(); break; }
+        case Codec::Dict65536U16: { const auto c = build_dict65536_tile512_value_codec(b); load_tile(c); r.codebook_size = static_cast<int>(c.codebook.size()); r.payload_bytes = c.payload_bytes(); break; }
+        case Codec::Fp16:
+        case Codec::Bf16: {
+            const auto c = codec == Codec::Fp16
+                               ? build_round16_nnz_value_codec(b, [](T v) { return float_to_fp16_bits(static_cast<float>(v)); })
+                               : build_round16_nnz_value_codec(b, [](T v) { return float_to_bf16_bits(static_cast<float>(v)); });
+            plan.values16.assign(c.values16.begin(), c.values16.end());
+            r.payload_bytes = c.values16.size() * 2;
+            break;
+        }
+        case Codec::Bfp8: {
+            const auto c = build_bfp8_blkscale_value_codec(b);
+            plan.int8_values.assign(c.int8_values.begin(), c.int8_values.end());
+            plan.block_scale_bf16.assign(c.block_scale_bf16.begin(), c.block_scale_bf16.end());
+            r.payload_bytes = c.int8_values.size() + c.block_scale_bf16.size() * 2;
+            break;
+        }
+        case Codec::Bfp8Outlier: {
+            const auto c = build_bfp8_outlier_blkscale_value_codec(b);
+            plan.int8_values.assign(c.int8_values.begin(), c.int8_values.end());
+            plan.block_scale_bf16.assign(c.block_scale_bf16.begin(), c.block_scale_bf16.end());
+            plan.outlier_rows.assign(c.outlier_rows.begin(), c.outlier_rows.end());
+            plan.outlier_cols.assign(c.outlier_cols.begin(), c.outlier_cols.end());
+            plan.outlier_vals.assign(c.outlier_vals.begin(), c.outlier_vals.end());
+            r.payload_bytes = c.payload_bytes();
+            r.value_only_valid = true;
+            r.value_only_bytes = c.value_only_payload_bytes();
+            r.num_outliers = c.num_outliers;
+            break;
+        }
+        case Codec::Bfp4: {
+            const auto c = build_bfp4_blkscale_value_codec(b);
+            plan.packed_int4.assign(c.packed_int4.begin(), c.packed_int4.end());
+            plan.block_scale_bf16.assign(c.block_scale_bf16.begin(), c.block_scale_bf16.end());
+            r.payload_bytes = c.packed_int4.size() + c.block_scale_bf16.size() * 2;
+            break;
+        }
+        case Codec::K256U8: {
+            const auto c = build_k256_tile256_build_result(b);
+            load_tile(c.tile);
+            r.exact = c.tile.exact;
+            r.codebook_size = c.used_codebook_size;
+            r.payload_bytes = c.tile.payload_bytes();
+            break;
+        }
+        case Codec::GlobalLogKmeans16:
+        case Codec::GlobalLogKmeans32:
+        case Codec::GlobalLogKmeans64:
+        case Codec::GlobalLogKmeans128: {
+            const int k = codec == Codec::GlobalLogKmeans16   ? 16
+                          : codec == Codec::GlobalLogKmeans32 ? 32
+                          : codec == Codec::GlobalLogKmeans64 ? 64
+                                                              : 128;
+            const auto c = build_logkmeans_tile256_build_result(b, k);
+            load_tile(c.tile);
+            r.exact = false;
+            r.codebook_size = c.used_codebook_size;
+            r.payload_bytes = c.tile.payload_bytes();
+            break;
+        }
+        case Codec::Raw:
+            throw std::runtime_error("original value codec must use the original traversal runner");
+    }
+}
+
+template <typename T>
+int run(const Options& o) {
+    const Layout layout = layout_kind(o.layout);
+    const bool auto_lossless = o.value_codec == "auto_lossless";
+    if (auto_lossless && layout == Layout::CusparseCsr)
+        throw std::runtime_error("auto_lossless value codec is only supported for BitBSR layouts");
+    Codec codec = auto_lossless ? Codec::Raw : codec_kind(o.value_codec);
+    const bool binary = o.lb_policy == "binary_implicit_one" && !o.lb_override;
+    OperatorSpec spec = operator_spec(layout, codec, binary && !auto_lossless);
+    if (layout == Layout::CusparseCsr) return run_cusparse<T>(o, spec);
+
+    Timing tm;
+    Report r;
+    r.auto_selected = auto_lossless;
+    const auto m = timed_host([&] { return structural::read_matrix_market_with_info<T>(o.matrix_path); }, tm.load);
+    const auto& a = m.matrix;
+    timed_host([&] { cuda_ok(cudaFree(nullptr), "CUDA context"); return 0; }, tm.ctx);
+    structural::GpuBitBsrWorkspace<T> ws;
+    structural::DeviceBitBsrMatrix<T> dev;
+    timed_host([&] {
+        structural::convert_to_bitbsr_gpu_warp_direct_8x4_device(a, ws, dev, &tm.convert_event);
+        return 0;
+    }, tm.convert_host);
+    if (auto_lossless) {
+        const auto h = timed_host([&] { return structural::build_device_exact_value_histogram(dev, &tm.auto_event); },
+                                  tm.auto_host);
+        codec = structural::select_auto_lossless_value_codec(h);
+        spec = operator_spec(layout, codec, binary);
+        r.auto_unique_count = h.unique_count;
+        r.auto_unique_overflow = h.unique_overflow;
+        r.auto_raw_bytes = h.raw_payload_bytes;
+        r.auto_candidate_bytes = candidate_bytes(h, codec);
+    }
+    const auto x = canonical_x<T>(a.cols);
+    thrust::device_vector<T> d_x(x.begin(), x.end()), d_y;
+    // load-balance chunking: the requested policy unless chunk sizes were given
+    int chunk = o.lb_chunk_blocks, split = o.lb_split_threshold_blocks;
+    const bool binary_lb = o.lb_policy == "binary_implicit_one" && !o.lb_override;
+    if (binary_lb) {
+        if (layout != Layout::ColBitmap64FlagLb || codec != Codec::ImplicitOne)
+            throw std::runtime_error(
+                "lb-policy binary_implicit_one requires col_bitmap64_flag_lb layout and all_one value codec");
+        std::tie(chunk, split) = binary_implicit_one_chunks(dev.num_blocks, dev.rows);
+    }
+
+    structural::BitBsrSpmvPlan8x4<T> plan;
+    plan.layout = layout;
+    plan.value_codec = codec;
+    if (codec == Codec::Raw) {
+        r.exact = true;
+        r.payload_bytes = static_cast<size_t>(dev.nnz) * sizeof(T);
+    } else {
+        timed_host([&] {
+            build_values(dev.to_host(), codec, plan, r);
+            return 0;
+        }, tm.codec_host);
+    }
+    timed_host([&] {
+        structural::make_bitbsr_8x4_col_bitmap_packed(dev, plan.packed_col_bitmap_meta, &tm.pack_event);
+        return 0;
+    }, tm.pack_host);
+    r.position_bytes = plan.packed_col_bitmap_meta.size() * sizeof(std::uint64_t);
+    if (layout == Layout::ColBitmap64FlagLb) {
+        timed_host([&] {
+            structural::make_bitbsr_8x4_col_bitmap_flag_load_balance_work_items(
+                dev, plan.load_balance, chunk, split, plan.packed_col_bitmap_meta, &tm.lb_event);
+            return 0;
+        }, tm.lb_host);
+    }
+    const auto [sum_ms, min_ms] =
+        time_loop(o, [&](float* ms) { structural::run_bitbsr_spmv_once(dev, plan, d_x, d_y, ms); });
+    cuda_ok(cudaDeviceSynchronize(), "SpMV");
+    Verify v;
+    if (o.verify_cpu) v = verify(a, x, d_y, spec.lossy_gate);
+
+    print_matrix_header(o, m, "8 x 4");
+    print_contract(spec);
+    const double nnz = static_cast<double>(dev.nnz);
+    std::cout << "spmv_layout: " << o.layout << "\n";
+    std::cout << "spmv_effective_layout: " << o.layout << "\n";
+    std::cout << "position_codec: col_bitmap64\n";
+    std::cout << "position_codec_exact: true\n";
+    std::cout << "position_codec_payload_bytes: " << r.position_bytes << "\n";
+    std::cout << "value_codec: " << o.value_codec << "\n";
+    std::cout << "value_codec_effective: " << codec_name(codec) << "\n";
+    std::cout << "value_codec_auto_selected: " << (r.auto_selected ? "true" : "false") << "\n";
+    std::cout << "value_codec_auto_unique_count: " << r.auto_unique_count << "\n";
+    std::cout << "value_codec_auto_unique_overflow: " << (r.auto_unique_overflow ? "true" : "false") << "\n";
+    std::cout << "value_codec_auto_raw_payload_bytes: " << r.auto_raw_bytes << "\n";
+    std::cout << "value_codec_auto_candidate_payload_bytes: " << r.auto_candidate_bytes << "\n";
+    std::cout << "value_codec_exact: " << (r.exact ? "true" : "false") << "\n";
+    std::cout << "value_codec_codebook_size: " << r.codebook_size << "\n";
+    std::cout << "value_codec_payload_bytes: " << r.payload_bytes << "\n";
+    std::cout << "value_codec_bytes_per_nnz: " << (nnz == 0 ? 0.0 : static_cast<double>(r.payload_bytes) / nnz) << "\n";
+    const size_t vo = r.value_only_valid ? r.value_only_bytes : r.payload_bytes;
+    std::cout << "value_codec_value_only_payload_bytes: " << vo << "\n";
+    std::cout << "value_codec_value_only_bytes_per_nnz: " << (nnz == 0 ? 0.0 : static_cast<double>(vo) / nnz) << "\n";
+    std::cout << "value_codec_num_outliers: " << r.num_outliers << "\n";
+    std::cout << "load_balance_policy: " << (binary_lb ? "binary_implicit_one" : "manual") << "\n";
+    std::cout << "load_balance_chunk_blocks: " << plan.load_balance.chunk_blocks << "\n";
+    std::cout << "load_balance_split_threshold_blocks: " << plan.load_balance.split_threshold_blocks << "\n";
+    std::cout << "gpu_work_items: " << plan.load_balance.work_items.size() << "\n";
+    std::cout << "gpu_output_residency: device\n";
+    std::cout << "gpu_num_blocks: " << dev.num_blocks << "\n";
+    std::cout << "verify_gate: " << (spec.lossy_gate ? "spmv_max_rel" : "exact_abs_or_rel") << "\n";
+    std::cout << "timing_scope: event_excludes_output_init\n";
+    std::cout << std::fixed << std::setprecision(4);
+    std::cout << "timing_ms: load=" << tm.load << ", cuda_context=" << tm.ctx << ", gpu_convert_host=" << tm.convert_host
+              << ", gpu_convert_event=" << tm.convert_event << ", value_codec_auto_select_host=" << tm.auto_host
+              << ", value_codec_auto_select_event=" << tm.auto_event << ", col_bitmap_pack_host=" << tm.pack_host
+              << ", col_bitmap_pack_event=" << tm.pack_event << ", load_balance_pack_host=" << tm.lb_host
+              << ", load_balance_pack_event=" << tm.lb_event << ", value_codec_pack_host=" << tm.codec_host
+              << ", gpu_spmv_avg_event=" << (sum_ms / o.iterations) << ", gpu_spmv_min_event=" << min_ms
+              << ", cpu_spmv=" << (o.verify_cpu ? v.cpu_ms : 0.0) << "\n";
+    print_verify(v);
+    return v.pass ? 0 : 1;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    try {
+        const Options o = parse(argc, argv);
+        return o.precision == "float" ? run<float>(o) : run<double>(o);
+    } catch (const std::exception& e) {
+        std::cerr << "error: " << e.what() << "\n";
+        return 1;
+    }
+}
