@@ -5,9 +5,10 @@
 // sweep's parse_key_values) can drive this build unchanged.
 //
 // Built: --mode fused_lb with the CSR residual (the hot path).  The
-// reference's other layouts (--mode two_pass, --residual-format brcoo|sell)
-// and its cuSPARSE baselines are not part of this library and are rejected
-// with an error.  Everything runs through the C ABI (cove_b200.h): the plan
+// reference's other layouts of this CLI (--mode two_pass, --residual-format
+// brcoo|sell) are not part of this library and are rejected with an error;
+// the cuSPARSE CSR baseline is the cusparse_csr layout of struct_gpu_spmv.
+// Everything runs through the C ABI (cove_b200.h): the plan
 // is built on the GPU, x is the reference's canonical input vector, y is
 // timed with CUDA events, and --verify-cpu compares against a CPU CSR SpMV.
 #include "cove_b200.h"
