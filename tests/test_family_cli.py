@@ -292,3 +292,26 @@ def test_family_cli_rejects_before_loading(tmp_path):
         rc, _, err = run(missing, "--layout", layout, "--value-codec", "original", "--lb-policy",
                          "binary_implicit_one", "--warmup", "0", "--iters", "1")
         assert rc != 0 and "binary_implicit_one requires col_bitmap64_flag_lb layout and all_one" in err
+
+
+FLOAT_CASES = [
+    ("original", "plain", ["--value-codec", "original"], {"operator_name": "original_lb",
+                                                          **_payload("true", 0, 20, "4")}),
+    ("dict2", "sign", ["--value-codec", "dict2"], {"operator_name": "dict2_lb", **_payload("true", 2, 12, "0.375")}),
+    ("auto_unique", "unique", ["--value-codec", "auto_lossless"], {"value_codec_effective": "dict4"}),
+    ("bf16", "sign", ["--value-codec", "bf16"], {"operator_name": "bf16_lb", "verify_gate": "spmv_max_rel"}),
+    ("cusparse", "plain", ["--layout", "cusparse_csr"], {"operator_name": "cusparse_csr",
+                                                         **_payload("true", 0, 20, "4")}),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", FLOAT_CASES, ids=[c[0] for c in FLOAT_CASES])
+def test_family_cli_float_precision(ref_mats, case):
+    """--precision float: 4-byte values and codebooks, the fp32 gates."""
+    _, mat, args, expected = case
+    rc, out, err = run(ref_mats[mat], "--precision", "float", *args, "--warmup", "0", "--iters", "1", "--verify-cpu")
+    assert rc == 0, err
+    d = parse(out)
+    assert d["precision"] == "float" and d["verify_cpu"].startswith("PASS,")
+    assert {k: d.get(k) for k in expected} == expected
