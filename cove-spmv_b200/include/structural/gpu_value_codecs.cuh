@@ -664,4 +664,49 @@ LogKmeansTile256BuildResult<T> build_logkmeans_tile256_build_result(const BitBsr
     return out;
 }
 
+// ---- checked builders (gpu_value_codecs.cuh:760-875): the 8x4 tile shape first --
+
+template <typename T>
+void validate_tile_shape_8x4(const BitBsrMatrix<T>& bitbsr) {
+    if (bitbsr.block_rows != 8 || bitbsr.block_cols != 4 || bitbsr.words_per_block != 1)
+        throw std::runtime_error("tile value codecs require 8x4 BitBSR blocks");
+}
+
+template <typename T>
+std::vector<std::uint32_t> build_checked_sign2_tile32_masks(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_sign2_tile32_masks(bitbsr);
+}
+
+template <typename T>
+Round16NnzValueCodec build_checked_fp16_nnz_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_round16_nnz_value_codec(bitbsr, [](T v) { return float_to_fp16_bits(static_cast<float>(v)); });
+}
+
+template <typename T>
+Round16NnzValueCodec build_checked_bf16_nnz_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_round16_nnz_value_codec(bitbsr, [](T v) { return float_to_bf16_bits(static_cast<float>(v)); });
+}
+
+template <typename T>
+Bfp8BlkScaleValueCodec build_checked_bfp8_blkscale_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_bfp8_blkscale_value_codec(bitbsr);
+}
+
+template <typename T>
+Bfp8OutlierBlkScaleValueCodec<T> build_checked_bfp8_outlier_blkscale_value_codec(const BitBsrMatrix<T>& bitbsr,
+                                                                                 double outlier_fraction = 0.005) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_bfp8_outlier_blkscale_value_codec(bitbsr, outlier_fraction);
+}
+
+template <typename T>
+Bfp4BlkScaleValueCodec build_checked_bfp4_blkscale_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_bfp4_blkscale_value_codec(bitbsr);
+}
+
 }  // namespace structural

@@ -1,0 +1,139 @@
+// structural/operators/bitbsr_spmv_8x4.cuh -- the operator umbrella header
+// (structural/include/structural/operators/bitbsr_spmv_8x4.cuh) with the
+// per-codec load-balanced device wrappers that callers such as the CG bench
+// (bench_cg_solve.cu:567-582) use directly:
+//   spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_device
+//       (bitbsr_spmv_8x4_raw.cuh:227-270)
+//   spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_round16_nnz_device
+//       (bitbsr_spmv_8x4_common.cuh:1418-1460)
+//   spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_bfp8_blkscale_device
+//       (:1512-1560)
+//   spmv_bitbsr_gpu_8x4_bfp8_outlier_flag_load_balance_device (:1566-1620)
+// Same parameters, size checks and messages; y is resized to rows and every
+// row written (no zero-fill needed); synchronous unless device_ms is given,
+// then timed with a CUDA event pair.  Each is one cove_hybrid_spmv call on
+// the BitBSR-only route of its codec; the library sizes its own work split,
+// so the load-balance layout is only checked, as the reference checks it.
+#pragma once
+
+#include "structural/operators/bitbsr_spmv_8x4_common.cuh"
+#include "structural/operators/bitbsr_spmv_8x4_dispatch.cuh"
+
+#include <string>
+
+namespace structural {
+
+namespace gpu_detail {
+
+template <typename T>
+void check_flag_lb_inputs(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<std::uint64_t>& packed_meta,
+                          const BitBsrLoadBalanceLayout8x4& layout, const thrust::device_vector<T>& x) {
+    validate_bitbsr_8x4_shape(m);
+    if (static_cast<Index>(x.size()) != m.cols) throw std::runtime_error("GPU BitBSR SpMV input vector size mismatch");
+    if (static_cast<Offset>(packed_meta.size()) != m.num_blocks)
+        throw std::runtime_error("GPU BitBSR col_bitmap_packed layout size mismatch");
+    if (static_cast<Index>(layout.work_item_row_ptr.size()) != m.num_block_rows + 1)
+        throw std::runtime_error("GPU BitBSR load-balance work_item_row_ptr size mismatch");
+}
+
+template <typename T>
+void check_bfp8_payload(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<signed char>& int8_values,
+                        const thrust::device_vector<std::uint16_t>& block_scale_bf16, const char* name) {
+    if (static_cast<Offset>(int8_values.size()) != m.nnz)
+        throw std::runtime_error(std::string("GPU BitBSR ") + name + " int8 value size mismatch");
+    if (static_cast<Offset>(block_scale_bf16.size()) != m.num_blocks)
+        throw std::runtime_error(std::string("GPU BitBSR ") + name + " per-block scale size mismatch");
+}
+
+template <typename T>
+void run_bitbsr_route(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<std::uint64_t>& packed_meta,
+                      const cove_values_desc& v, const thrust::device_vector<T>& x, thrust::device_vector<T>& y,
+                      float* device_ms) {
+    y.resize(static_cast<size_t>(m.rows));
+    const cove_hybrid_desc a = bitbsr_only_desc(m, packed_meta);
+    CudaEventTimer timer(device_ms);
+    cove_check(cove_hybrid_spmv(&a, &v, raw(x), raw(y), nullptr));
+    finish(timer, device_ms);
+}
+
+}  // namespace gpu_detail
+
+// y = A x with the raw T values (the lossless route).
+template <typename T>
+void spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const BitBsrLoadBalanceLayout8x4& layout, const thrust::device_vector<T>& x, thrust::device_vector<T>& y,
+    float* device_ms = nullptr) {
+    gpu_detail::check_flag_lb_inputs(bitbsr, packed_meta, layout, x);
+    cove_values_desc v{};
+    v.route = COVE_ROUTE_HYBRID;
+    v.kept = gpu_detail::raw(bitbsr.values);
+    gpu_detail::run_bitbsr_route(bitbsr, packed_meta, v, x, y, device_ms);
+}
+
+template <typename T>
+thrust::device_vector<T> spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const BitBsrLoadBalanceLayout8x4& layout, const thrust::device_vector<T>& x, float* device_ms = nullptr) {
+    thrust::device_vector<T> y;
+    spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_device(bitbsr, packed_meta, layout, x, y, device_ms);
+    return y;
+}
+
+// y = A x with one 16-bit value per nonzero: bf16 if Bf16, else fp16.
+template <bool Bf16, typename T>
+void spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_round16_nnz_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const BitBsrLoadBalanceLayout8x4& layout, const thrust::device_vector<std::uint16_t>& values16,
+    const char* codec_name, const thrust::device_vector<T>& x, thrust::device_vector<T>& y,
+    float* device_ms = nullptr) {
+    gpu_detail::check_flag_lb_inputs(bitbsr, packed_meta, layout, x);
+    if (static_cast<Offset>(values16.size()) != bitbsr.nnz)
+        throw std::runtime_error(std::string("GPU BitBSR ") + codec_name + " per-nnz value size mismatch");
+    cove_values_desc v{};
+    v.route = Bf16 ? COVE_ROUTE_BF16_NNZ : COVE_ROUTE_FP16_NNZ;
+    v.kept = gpu_detail::raw(values16);
+    gpu_detail::run_bitbsr_route(bitbsr, packed_meta, v, x, y, device_ms);
+}
+
+// y = A x with int8 mantissas times a bf16 scale per block.
+template <typename T>
+void spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_bfp8_blkscale_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const BitBsrLoadBalanceLayout8x4& layout, const thrust::device_vector<signed char>& int8_values,
+    const thrust::device_vector<std::uint16_t>& block_scale_bf16, const thrust::device_vector<T>& x,
+    thrust::device_vector<T>& y, float* device_ms = nullptr) {
+    gpu_detail::check_flag_lb_inputs(bitbsr, packed_meta, layout, x);
+    gpu_detail::check_bfp8_payload(bitbsr, int8_values, block_scale_bf16, "bfp8_blkscale");
+    cove_values_desc v{};
+    v.route = COVE_ROUTE_BFP8;
+    v.kept = gpu_detail::raw(int8_values);
+    v.block_scale = gpu_detail::raw(block_scale_bf16);
+    gpu_detail::run_bitbsr_route(bitbsr, packed_meta, v, x, y, device_ms);
+}
+
+// BFP8 bulk plus the exact side list of outliers (row, col, value), one
+// event interval around both when timed.
+template <typename T>
+void spmv_bitbsr_gpu_8x4_bfp8_outlier_flag_load_balance_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const BitBsrLoadBalanceLayout8x4& layout, const thrust::device_vector<signed char>& int8_values,
+    const thrust::device_vector<std::uint16_t>& block_scale_bf16, const thrust::device_vector<std::int32_t>& outlier_rows,
+    const thrust::device_vector<std::int32_t>& outlier_cols, const thrust::device_vector<T>& outlier_vals,
+    const thrust::device_vector<T>& x, thrust::device_vector<T>& y, float* device_ms = nullptr) {
+    gpu_detail::check_flag_lb_inputs(bitbsr, packed_meta, layout, x);
+    gpu_detail::check_bfp8_payload(bitbsr, int8_values, block_scale_bf16, "bfp8_outlier_blkscale");
+    if (outlier_rows.size() != outlier_cols.size() || outlier_rows.size() != outlier_vals.size())
+        throw std::runtime_error("GPU BitBSR bfp8_outlier side-list size mismatch");
+    cove_values_desc v{};
+    v.route = COVE_ROUTE_BFP8_OUTLIER;
+    v.kept = gpu_detail::raw(int8_values);
+    v.block_scale = gpu_detail::raw(block_scale_bf16);
+    v.num_outliers = static_cast<int64_t>(outlier_vals.size());
+    v.outlier_rows = gpu_detail::raw(outlier_rows);
+    v.outlier_cols = gpu_detail::raw(outlier_cols);
+    v.outlier_vals = gpu_detail::raw(outlier_vals);
+    gpu_detail::run_bitbsr_route(bitbsr, packed_meta, v, x, y, device_ms);
+}
+
+}  // namespace structural
