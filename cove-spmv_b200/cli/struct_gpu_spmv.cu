@@ -11,6 +11,7 @@
 #include "structural/gpu_value_codecs.cuh"
 #include "structural/matrix_market.hpp"
 #include "structural/operators/bitbsr_spmv_8x4_dispatch.cuh"
+#include "structural/spmv_operator_plan.hpp"
 
 #include <cuda_runtime.h>
 #include <cusparse.h>
@@ -211,71 +212,16 @@ const char* codec_name(Codec c) {
     return "unknown";
 }
 
-// ---- operator contract (spmv_operator_plan.hpp) -----------------------------------
+// ---- operator contract: structural/spmv_operator_plan.hpp --------------------------
 
-struct OperatorSpec {
-    std::string name;
-    const char* family = "load_balanced_traversal";
-    const char* promotion = "promoted";
-    const char* runner = "bitbsr_original_traversal";
-    bool lossy_gate = false;  // spmv_max_rel, else exact_abs_or_rel
-};
+using structural::SpmvOperatorSpec;
 
-OperatorSpec operator_spec(Layout layout, Codec codec, bool binary_policy) {
-    if (binary_policy && (layout != Layout::ColBitmap64FlagLb || codec != Codec::ImplicitOne))
-        throw std::runtime_error(
-            "lb-policy binary_implicit_one requires col_bitmap64_flag_lb layout and all_one value codec");
-    const bool non_raw = codec != Codec::Raw;
-    if (layout == Layout::CusparseCsr && non_raw)
-        throw std::runtime_error("compressed value codecs are only supported for BitBSR layouts");
-    OperatorSpec s;
-    s.lossy_gate = structural::bitbsr_spmv_8x4_is_controlled_lossy_value_codec(codec);
-    if (layout == Layout::CusparseCsr) {
-        s.name = "cusparse_csr";
-        s.family = "external_baseline";
-        s.promotion = "external_baseline";
-        s.runner = "cusparse_csr";
-        return s;
-    }
-    const bool lb = layout == Layout::ColBitmap64FlagLb;
-    s.name = std::string(codec_name(codec)) + (lb ? "_lb" : "_nolb");
-    if (s.lossy_gate) {
-        s.family = "controlled_lossy_value_specialized";
-        s.promotion = "buildable_needs_report";
-        s.runner = "bitbsr_value_specialized";
-    } else if (non_raw) {
-        s.family = "lossless_value_specialized";
-        s.promotion = binary_policy ? "promoted" : "buildable_needs_report";
-        s.runner = "bitbsr_value_specialized";
-    } else if (!lb) {
-        s.family = "non_load_balanced_traversal";
-        s.promotion = "buildable_needs_report";
-    }
-    return s;
+structural::LoadBalancePolicy requested_policy(const Options& o) {
+    return o.lb_policy == "binary_implicit_one" ? structural::LoadBalancePolicy::BinaryImplicitOne
+                                                : structural::LoadBalancePolicy::Manual;
 }
 
-// Load-balance chunking for binary all-one matrices (load_balance_policy.hpp:
-// the reference's calibrated table of chunk sizes by block count and blocks
-// per block row); 32 / 32 where no rule applies.
-std::pair<int, int> binary_implicit_one_chunks(Offset num_blocks, Index rows) {
-    if (num_blocks <= 0 || rows <= 0) return {32, 32};
-    const double per_row = static_cast<double>(num_blocks) / std::max<Index>((rows + 7) / 8, 1);
-    auto c = [](int n) { return std::make_pair(n, n); };
-    if (num_blocks < 30000) return c(8);
-    if (per_row >= 20000.0 && num_blocks >= 700000) return c(128);
-    if (per_row >= 6000.0) {
-        if (num_blocks >= 400000) return c(128);
-        if (num_blocks >= 250000) return c(64);
-    }
-    if (per_row >= 500.0) {
-        if (num_blocks < 120000) return c(16);
-        if (num_blocks >= 3000000) return c(64);
-        return {32, 32};
-    }
-    if (num_blocks >= 8000000 && per_row >= 128.0) return c(128);
-    if (num_blocks >= 3000000) return c(64);
-    return {32, 32};
-}
+bool lossy_gate(const SpmvOperatorSpec& s) { return s.verify_gate == structural::SpmvVerifyGate::SpmvMaxRel; }
 
 // ---- shared pieces ------------------------------------------------------------------
 
@@ -353,11 +299,11 @@ void print_matrix_header(const Options& o, const structural::MatrixMarketLoadRes
     std::cout << "block: " << block << "\n";
 }
 
-void print_contract(const OperatorSpec& s) {
-    std::cout << "operator_name: " << s.name << "\n";
-    std::cout << "operator_family: " << s.family << "\n";
-    std::cout << "operator_promotion_status: " << s.promotion << "\n";
-    std::cout << "operator_runner: " << s.runner << "\n";
+void print_contract(const SpmvOperatorSpec& s) {
+    std::cout << "operator_name: " << s.operator_name << "\n";
+    std::cout << "operator_family: " << structural::spmv_operator_family_name(s.family) << "\n";
+    std::cout << "operator_promotion_status: " << structural::spmv_promotion_status_name(s.promotion_status) << "\n";
+    std::cout << "operator_runner: " << structural::spmv_operator_runner_name(s.runner) << "\n";
 }
 
 void print_verify(const Verify& v) {
@@ -389,7 +335,7 @@ std::pair<double, float> time_loop(const Options& o, F&& once) {
 // ---- cuSPARSE CSR baseline ---------------------------------------------------------
 
 template <typename T>
-int run_cusparse(const Options& o, const OperatorSpec& spec) {
+int run_cusparse(const Options& o, const SpmvOperatorSpec& spec) {
     if (o.value_codec != "original")
         throw std::runtime_error("compressed value codecs are only supported for BitBSR layouts");
     double load_ms = 0, ctx_ms = 0, upload_ms = 0, setup_ms = 0, pre_ms = 0;
@@ -458,7 +404,7 @@ int run_cusparse(const Options& o, const OperatorSpec& spec) {
     });
     cuda_ok(cudaDeviceSynchronize(), "SpMV");
     Verify v;
-    if (o.verify_cpu) v = verify(a, x, d_y, spec.lossy_gate);
+    if (o.verify_cpu) v = verify(a, x, d_y, lossy_gate(spec));
 
     print_matrix_header(o, m, "csr");
     print_contract(spec);
@@ -481,7 +427,7 @@ int run_cusparse(const Options& o, const OperatorSpec& spec) {
     std::cout << "gpu_work_items: 0\n";
     std::cout << "gpu_output_residency: device\n";
     std::cout << "gpu_num_blocks: 0\n";
-    std::cout << "verify_gate: " << (spec.lossy_gate ? "spmv_max_rel" : "exact_abs_or_rel") << "\n";
+    std::cout << "verify_gate: " << structural::spmv_verify_gate_name(spec.verify_gate) << "\n";
     std::cout << "timing_scope: cusparse_event_includes_beta_zero\n";
     std::cout << std::fixed << std::setprecision(4);
     std::cout << "timing_ms: load=" << load_ms << ", cuda_context=" << ctx_ms
@@ -651,8 +597,9 @@ int run(const Options& o) {
     if (auto_lossless && layout == Layout::CusparseCsr)
         throw std::runtime_error("auto_lossless value codec is only supported for BitBSR layouts");
     Codec codec = auto_lossless ? Codec::Raw : codec_kind(o.value_codec);
-    const bool binary = o.lb_policy == "binary_implicit_one" && !o.lb_override;
-    OperatorSpec spec = operator_spec(layout, codec, binary && !auto_lossless);
+    // before loading the matrix; auto_lossless re-derives it for the chosen codec
+    SpmvOperatorSpec spec = structural::make_spmv_operator_spec(
+        layout, codec, auto_lossless ? structural::LoadBalancePolicy::Manual : requested_policy(o), o.lb_override);
     if (layout == Layout::CusparseCsr) return run_cusparse<T>(o, spec);
 
     Timing tm;
@@ -671,7 +618,7 @@ int run(const Options& o) {
         const auto h = timed_host([&] { return structural::build_device_exact_value_histogram(dev, &tm.auto_event); },
                                   tm.auto_host);
         codec = structural::select_auto_lossless_value_codec(h);
-        spec = operator_spec(layout, codec, binary);
+        spec = structural::make_spmv_operator_spec(layout, codec, requested_policy(o), o.lb_override);
         r.auto_unique_count = h.unique_count;
         r.auto_unique_overflow = h.unique_overflow;
         r.auto_raw_bytes = h.raw_payload_bytes;
@@ -681,12 +628,12 @@ int run(const Options& o) {
     thrust::device_vector<T> d_x(x.begin(), x.end()), d_y;
     // load-balance chunking: the requested policy unless chunk sizes were given
     int chunk = o.lb_chunk_blocks, split = o.lb_split_threshold_blocks;
-    const bool binary_lb = o.lb_policy == "binary_implicit_one" && !o.lb_override;
-    if (binary_lb) {
-        if (layout != Layout::ColBitmap64FlagLb || codec != Codec::ImplicitOne)
-            throw std::runtime_error(
-                "lb-policy binary_implicit_one requires col_bitmap64_flag_lb layout and all_one value codec");
-        std::tie(chunk, split) = binary_implicit_one_chunks(dev.num_blocks, dev.rows);
+    const bool binary_lb = structural::effective_requested_load_balance_policy(requested_policy(o), o.lb_override) ==
+                           structural::LoadBalancePolicy::BinaryImplicitOne;
+    if (binary_lb) {  // the spec above already required flag_lb + all_one
+        const auto p = structural::select_binary_implicit_one_load_balance_policy(dev.num_blocks, dev.rows);
+        chunk = p.chunk_blocks;
+        split = p.split_threshold_blocks;
     }
 
     structural::BitBsrSpmvPlan8x4<T> plan;
@@ -717,7 +664,7 @@ int run(const Options& o) {
         time_loop(o, [&](float* ms) { structural::run_bitbsr_spmv_once(dev, plan, d_x, d_y, ms); });
     cuda_ok(cudaDeviceSynchronize(), "SpMV");
     Verify v;
-    if (o.verify_cpu) v = verify(a, x, d_y, spec.lossy_gate);
+    if (o.verify_cpu) v = verify(a, x, d_y, lossy_gate(spec));
 
     print_matrix_header(o, m, "8 x 4");
     print_contract(spec);
@@ -748,7 +695,7 @@ int run(const Options& o) {
     std::cout << "gpu_work_items: " << plan.load_balance.work_items.size() << "\n";
     std::cout << "gpu_output_residency: device\n";
     std::cout << "gpu_num_blocks: " << dev.num_blocks << "\n";
-    std::cout << "verify_gate: " << (spec.lossy_gate ? "spmv_max_rel" : "exact_abs_or_rel") << "\n";
+    std::cout << "verify_gate: " << structural::spmv_verify_gate_name(spec.verify_gate) << "\n";
     std::cout << "timing_scope: event_excludes_output_init\n";
     std::cout << std::fixed << std::setprecision(4);
     std::cout << "timing_ms: load=" << tm.load << ", cuda_context=" << tm.ctx << ", gpu_convert_host=" << tm.convert_host

@@ -44,6 +44,10 @@ inline bool bitbsr_spmv_8x4_uses_load_balance(BitBsrSpmvLayoutKind8x4 layout) {
     return layout == BitBsrSpmvLayoutKind8x4::ColBitmap64FlagLb;
 }
 
+inline bool bitbsr_spmv_8x4_is_non_raw_value_codec(BitBsrValueCodecKind8x4 c) {
+    return c != BitBsrValueCodecKind8x4::Raw;
+}
+
 inline bool bitbsr_spmv_8x4_is_controlled_lossy_value_codec(BitBsrValueCodecKind8x4 c) {
     switch (c) {
         case BitBsrValueCodecKind8x4::Fp16:
