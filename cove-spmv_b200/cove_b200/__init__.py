@@ -27,7 +27,7 @@ ROUTE_NAMES = {0: "original", 1: "dict_u8_lossless", 2: "dict_u16_lossless",
                3: "bfp8_blocks+bf16_residual", 4: "bfp8_outlier_blocks+bf16_residual"}
 ROUTE_NAMES_INV = {v: k for k, v in ROUTE_NAMES.items()}
 ROUTE_NAMES_INV.update({"hybrid": 0, "dict_u8": 1, "dict_u16": 2, "bfp8": 3, "bfp8_outlier": 4})
-SPLIT = {"cost_gated": 0, "threshold": 1, "none": 2}
+SPLIT = {"cost_gated": 0, "threshold": 1, "none": 2, "mask": 3}
 LB_STYLE = {"hybrid": 0, "device": 1}
 
 STREAM = {
@@ -66,7 +66,8 @@ class PlanOpts(C.Structure):
                 ("lb_style", C.c_int32), ("long_row_split", C.c_int32),
                 ("value_codec", C.c_int32), ("outlier_fraction", C.c_double),
                 ("gate_tolerance", C.c_double), ("gate_enable", C.c_int32),
-                ("keep_full_bitbsr", C.c_int32), ("keep_lossless", C.c_int32)]
+                ("keep_full_bitbsr", C.c_int32), ("keep_lossless", C.c_int32),
+                ("move_mask", C.c_uint64)]
 
 
 class PlanInfo(C.Structure):

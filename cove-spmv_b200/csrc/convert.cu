@@ -994,8 +994,10 @@ void lb_fill(int32_t nbr, const int32_t* brp, const int32_t* brvp, const uint32_
 
 // CsrBitBsrSplitCostModel::should_move_to_residual (csr_bitbsr_split.hpp:66-73)
 // tabulated for every block population 0..32 on the host, with plain double
-// arithmetic, so the device applies exactly the reference's decisions.
+// arithmetic, so the device applies exactly the reference's decisions; the
+// mask policy hands over a caller's own table.
 unsigned long long move_mask_for(const cove_plan_opts& o) {
+    if (o.split_policy == COVE_SPLIT_MASK) return o.move_mask & ((1ULL << 33) - 1);
     unsigned long long m = 0;
     for (int bn = 0; bn <= 32; ++bn) {
         bool move = true;

@@ -580,7 +580,7 @@ cove_status cove_plan_build(const cove_csr_desc* csr, const cove_plan_opts* opts
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "lb-split-threshold-blocks must be positive");
         }
         if (o.long_row_split < 0) COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "long-row-split must be non-negative");
-        if (o.split_policy < 0 || o.split_policy > 2 || o.lb_style < 0 || o.lb_style > 1 ||
+        if (o.split_policy < 0 || o.split_policy > 3 || o.lb_style < 0 || o.lb_style > 1 ||
             o.value_codec < 0 || o.value_codec > 4) {
             COVE_THROW(COVE_ERR_INVALID_ARGUMENT, "unknown option value");
         }

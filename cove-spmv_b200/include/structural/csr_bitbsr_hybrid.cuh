@@ -241,6 +241,18 @@ class Plan {
     const cove_plan_info& info() const { return info_; }
     cove_plan* handle() const { return plan_; }
 
+    // One of the plan's device streams (cove_stream_id) copied to the host
+    // as V elements; an absent stream is an error.
+    template <typename V>
+    std::vector<V> stream(int which) const {
+        size_t bytes = 0;
+        cove_check(cove_plan_stream(plan_, which, nullptr, 0, &bytes, nullptr));
+        if (bytes % sizeof(V) != 0) throw std::runtime_error("plan stream size is not a whole number of elements");
+        std::vector<V> out(bytes / sizeof(V));
+        if (bytes) cove_check(cove_plan_stream(plan_, which, out.data(), bytes, &bytes, nullptr));
+        return out;
+    }
+
     // y = A x on the dispatched route (or `route`), synchronous like the
     // reference wrappers; iter_ms as in their CudaEventTimer.
     void spmv(const thrust::device_vector<T>& x, thrust::device_vector<T>& y, int route = -1,

@@ -74,7 +74,11 @@ typedef enum {
 typedef enum {
     COVE_SPLIT_COST_GATED = 0,
     COVE_SPLIT_THRESHOLD = 1,
-    COVE_SPLIT_NONE = 2           /* BitBSR only, no residual (family runner operators) */
+    COVE_SPLIT_NONE = 2,          /* BitBSR only, no residual (family runner operators) */
+    COVE_SPLIT_MASK = 3           /* move a block of population p <= threshold iff bit p of
+                                     move_mask is set: any predicate of
+                                     convert_bitbsr_to_csr_bitbsr_split_if
+                                     (csr_bitbsr_split.hpp:405-471), tabulated */
 } cove_split_policy;
 
 /* Work-item layout flavour. */
@@ -123,6 +127,7 @@ typedef struct {
     int32_t gate_enable;               /* evaluate the gate and fall back on failure */
     int32_t keep_full_bitbsr;          /* keep the un-split BitBSR for cove_plan_stream */
     int32_t keep_lossless;             /* keep raw values after a joint route passes */
+    uint64_t move_mask;                /* COVE_SPLIT_MASK only: bits 0..32, by block population */
 } cove_plan_opts;
 
 typedef struct cove_plan cove_plan;

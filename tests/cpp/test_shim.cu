@@ -4,7 +4,9 @@
 // conversion, packed words and work-item known answers, BitBSR-only
 // operators, the hybrid/joint launchers, and the device pipeline handle.
 // Built and run by tests/test_gpu_shim.py (needs a GPU).
+#include "structural/convert.hpp"
 #include "structural/csr_bitbsr_hybrid.cuh"
+#include "structural/csr_bitbsr_split.hpp"
 #include "structural/gpu_value_codecs.cuh"
 
 #include <cuda_fp16.h>
@@ -497,6 +499,76 @@ void test_family_builders() {
 
 }  // namespace
 
+// Host convert_to_bitbsr and the split API (csr_bitbsr_split.hpp) over the
+// device plan: the parts reproduce A x, the counters partition the blocks,
+// and a predicate on block population is applied as given.
+void test_host_convert_and_split_api() {
+    using namespace structural;
+    const auto csr = kat_9x4404();
+    const auto full = convert_to_bitbsr(csr, 8, 4);
+    GpuBitBsrWorkspace<double> ws;
+    DeviceBitBsrMatrix<double> dev;
+    convert_to_bitbsr_gpu_warp_direct_8x4_device(csr, ws, dev);
+    const auto h = dev.to_host();
+    CHECK(full.block_col_idx == h.block_col_idx && full.bitmap_words == h.bitmap_words && full.values == h.values);
+    CHECK(full.block_row_ptr == h.block_row_ptr && full.block_val_ptr == h.block_val_ptr);
+    bool threw = false;
+    try {
+        convert_to_bitbsr(csr, 2, 2);
+    } catch (const std::runtime_error&) {
+        threw = true;
+    }
+    CHECK(threw);
+
+    std::vector<double> x(csr.cols);
+    for (int i = 0; i < csr.cols; ++i) x[i] = static_cast<double>(i % 7) - 3.0;
+    const auto y0 = cpu_spmv(csr, x);
+    auto split_product = [&](const CsrBitBsrSplitMatrix<double>& s) {
+        std::vector<double> y = cpu_spmv(s.residual, x);
+        const auto& b = s.bitbsr;
+        for (int br = 0; br < b.num_block_rows; ++br)
+            for (int k = b.block_row_ptr[br]; k < b.block_row_ptr[br + 1]; ++k)
+                for (int bit = 0; bit < 32; ++bit)
+                    if (b.bitmap_words[k] >> bit & 1u)
+                        y[br * 8 + bit / 4] += b.values[b.block_val_ptr[k] + popcount_word(b.bitmap_words[k] &
+                                                                                          ((1u << bit) - 1u))] *
+                                               x[b.block_col_idx[k] * 4 + bit % 4];
+        return y;
+    };
+    std::vector<int> pop;
+    for (int b = 0; b < full.num_blocks(); ++b) pop.push_back(full.block_val_ptr[b + 1] - full.block_val_ptr[b]);
+
+    const CsrBitBsrSplitCostModel model;  // moves populations <= 9
+    const auto g = convert_to_csr_bitbsr_split_cost_gated(csr, 8, 4, 32, model);
+    CHECK(g.kept_blocks + g.residual_blocks == full.num_blocks() && g.residual_blocks == full.num_blocks());
+    CHECK(g.cost_skipped_blocks == 0 && g.kept_nnz + g.residual_nnz == full.nnz());
+    close(split_product(g), y0, 0.0);
+
+    const auto t = convert_bitbsr_to_csr_bitbsr_split(full, 1);  // only single-entry blocks move
+    int singles = 0;
+    for (int p : pop) singles += p <= 1;
+    CHECK(t.residual_blocks == singles && t.kept_blocks == full.num_blocks() - singles && t.cost_skipped_blocks == 0);
+    close(split_product(t), y0, 0.0);
+
+    const auto e = convert_bitbsr_to_csr_bitbsr_split_if(full, 32, [](Offset p) { return p % 2 == 0; });
+    int even = 0, odd_nnz = 0;
+    for (int p : pop) {
+        even += p % 2 == 0;
+        odd_nnz += p % 2 ? p : 0;
+    }
+    CHECK(e.residual_blocks == even && e.cost_skipped_blocks == full.num_blocks() - even);
+    CHECK(e.cost_skipped_nnz == odd_nnz && e.kept_nnz == odd_nnz);
+    close(split_product(e), y0, 0.0);
+
+    threw = false;
+    try {
+        convert_bitbsr_to_csr_bitbsr_split(full, -1);
+    } catch (const std::runtime_error& err) {
+        threw = std::strcmp(err.what(), "CSR+BitBSR residual threshold must be non-negative") == 0;
+    }
+    CHECK(threw);
+}
+
 int main() {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
@@ -508,6 +580,7 @@ int main() {
     test_family_value_codecs();
     test_family_builders();
     test_hybrid_launchers_and_plan();
+    test_host_convert_and_split_api();
     std::printf("shim tests passed\n");
     return 0;
 }

@@ -174,6 +174,37 @@ def test_reference_cases_position_streams(ref_cases, split_key):
         assert_lossless(y, rows, rp, ci, v, x, d[f"{name}/y_canonical"])
 
 
+def _mask_for(opts):
+    """CsrBitBsrSplitCostModel::should_move_to_residual (csr_bitbsr_split.hpp:66-73)
+    tabulated over block populations 0..32, as the split API's predicate."""
+    if opts.get("split_policy") == "threshold":
+        return (1 << 33) - 1
+    bb, bn, cb, cn = opts.get("cost_bitmap_block", 10.0), 0.0, 0.0, 1.0
+    return sum(1 << p for p in range(33) if cb + cn * p < bb + bn * p)
+
+
+@pytest.mark.parametrize("split_key", sorted(SPLIT_OPTS))
+def test_reference_cases_mask_policy(ref_cases, split_key):
+    """COVE_SPLIT_MASK with the tabulated predicate gives the reference's split."""
+    d = ref_cases
+    opts = SPLIT_OPTS[split_key]
+    for name in case_names(d):
+        rows, cols = (int(v) for v in d[f"{name}/shape"])
+        rp, ci, v = d[f"{name}/row_ptr"], d[f"{name}/col_idx"], d[f"{name}/values"]
+        p = plan_for(rows, cols, rp, ci, v, split_policy="mask", move_mask=_mask_for(opts),
+                     residual_threshold=opts["residual_threshold"])
+        ref = plan_for(rows, cols, rp, ci, v, **opts)
+        q = f"{name}/{split_key}/"
+        for stream, key in (("kept_block_row_ptr", "kept/block_row_ptr"), ("kept_block_col_idx", "kept/block_col_idx"),
+                            ("kept_bitmap", "kept/bitmap"), ("kept_block_val_ptr", "kept/block_val_ptr"),
+                            ("kept_values", "kept/values"), ("res_row_ptr", "res/row_ptr"),
+                            ("res_col_idx", "res/col_idx"), ("res_values", "res/values")):
+            assert np.array_equal(p.stream(stream), d[q + key]), (name, stream)
+        for k in ("kept_blocks", "residual_blocks", "cost_skipped_blocks", "kept_nnz", "residual_nnz",
+                  "cost_skipped_nnz"):
+            assert getattr(p.info, k) == getattr(ref.info, k), (name, k)
+
+
 def test_reference_cases_value_codecs(ref_cases):
     d = ref_cases
     for name in case_names(d):
