@@ -11,6 +11,7 @@
 #include "structural/gpu_value_codecs.cuh"
 #include "structural/matrix_market.hpp"
 #include "structural/operators/bitbsr_spmv_8x4_dispatch.cuh"
+#include "structural/spmv_cli_options.hpp"
 #include "structural/spmv_operator_plan.hpp"
 
 #include <cuda_runtime.h>
@@ -36,157 +37,11 @@ using structural::Offset;
 using Layout = structural::BitBsrSpmvLayoutKind8x4;
 using Codec = structural::BitBsrValueCodecKind8x4;
 
-// ---- options (spmv_cli_options.hpp) -----------------------------------------------
+// ---- options: structural/spmv_cli_options.hpp ------------------------------------
 
-struct Options {
-    std::string matrix_path;
-    std::string precision = "double";
-    std::string layout = "col_bitmap64_flag_lb";
-    std::string value_codec = "original";
-    int lb_chunk_blocks = 32;
-    int lb_split_threshold_blocks = -1;
-    std::string lb_policy = "manual";
-    bool lb_override = false;  // --lb-chunk-blocks or --lb-split-threshold-blocks given
-    std::string cusparse_alg = "default";
-    int warmup = 5;
-    int iterations = 20;
-    bool verify_cpu = false;
-};
+using Options = structural::SpmvCliOptions;
 
-void usage(const char* argv0, std::ostream& os) {
-    os << "usage: " << argv0 << " MATRIX.mtx [--precision float|double]"
-       << " [--layout col_bitmap64|col_bitmap64_flag_lb|cusparse_csr]"
-       << " [--value-codec original|all_one|const_c|sign2|sign2_scale|dict2|dict4|dict16|"
-          "dict256_u8|dict65536_u16|auto_lossless|fp16|bf16|bfp8|bfp8_outlier|bfp4|codebook256_u8|"
-          "global_logkmeans16|global_logkmeans32|global_logkmeans64|global_logkmeans128]"
-       << " [--lb-policy manual|binary_implicit_one] [--lb-chunk-blocks N]"
-       << " [--lb-split-threshold-blocks N] [--cusparse-alg default|csr_alg1|csr_alg2]"
-       << " [--warmup N] [--iters N] [--verify-cpu]\n";
-}
-
-// Accepted spellings -> canonical names (the reference's alias tables).
-std::string canonical_layout(const std::string& s, std::string& alg) {
-    static const std::map<std::string, std::string> names = {
-        {"col_bitmap", "col_bitmap64"}, {"packed_abs", "col_bitmap64"}, {"abs_packed", "col_bitmap64"},
-        {"col_bitmap64", "col_bitmap64"}, {"col_bitmap64_packed", "col_bitmap64"},
-        {"col_bitmap_flag_lb", "col_bitmap64_flag_lb"}, {"packed_abs_flag_lb", "col_bitmap64_flag_lb"},
-        {"abs_packed_flag_lb", "col_bitmap64_flag_lb"}, {"col_bitmap64_flag_lb", "col_bitmap64_flag_lb"},
-        {"col_bitmap64_packed_flag_lb", "col_bitmap64_flag_lb"}, {"cusparse", "cusparse_csr"},
-        {"cusparse_spmv", "cusparse_csr"}, {"cusparse_csr", "cusparse_csr"}};
-    const auto it = names.find(s);
-    if (it != names.end()) return it->second;
-    if (s == "cusparse_csr_alg1" || s == "cusparse_alg1") {
-        alg = "csr_alg1";
-        return "cusparse_csr";
-    }
-    if (s == "cusparse_csr_alg2" || s == "cusparse_alg2") {
-        alg = "csr_alg2";
-        return "cusparse_csr";
-    }
-    throw std::runtime_error("layout must be col_bitmap64, col_bitmap64_flag_lb, or cusparse_csr");
-}
-
-std::string canonical_codec(const std::string& s) {
-    static const char* const kCanonical[] = {
-        "original", "all_one", "const_c", "sign2", "sign2_scale", "dict4", "dict2", "dict16", "dict256_u8",
-        "dict65536_u16", "auto_lossless", "fp16", "bf16", "bfp8", "bfp8_outlier", "bfp4", "codebook256_u8",
-        "global_logkmeans16", "global_logkmeans32", "global_logkmeans64", "global_logkmeans128"};
-    for (const char* c : kCanonical)
-        if (s == c) return s;
-    static const std::map<std::string, std::vector<std::string>> aliases = {
-        {"original", {"raw", "orig", "origin"}},
-        {"all_one", {"one", "pattern", "implicit1", "implicit_one"}},
-        {"const_c", {"dict1", "const", "constant", "constant_c"}},
-        {"sign2", {"sign", "sign_i8", "sign_tile32", "tile_sign"}},
-        {"sign2_scale", {"scaled_sign", "scaled_sign2", "sign_scale", "sign2_c"}},
-        {"dict2", {"code1", "u1", "unique2_tile32", "tile1", "unique2"}},
-        {"dict4", {"code2", "u2", "unique4_tile64", "ternary", "ternary3", "tile2", "unique4"}},
-        {"dict16", {"u4", "unique_u8", "unique16_tile128", "tile4", "unique16"}},
-        {"dict256_u8", {"dict256", "unique256", "unique256_tile256", "dict256_tile256", "exact_u8"}},
-        {"dict65536_u16",
-         {"dict65536", "dict_u16", "unique65536", "unique65536_tile512", "dict65536_tile512", "tile16", "exact_u16"}},
-        {"codebook256_u8", {"k256", "k256_uint8", "uint8", "u8", "k256_tile256", "tile8", "k256_u8"}},
-        {"fp16", {"half", "fp16_tile512"}},
-        {"bf16", {"bfloat16", "bf16_tile512"}},
-        {"bfp8", {"bfp8_blkscale", "int8_blkscale", "int8_8x4"}},
-        {"bfp8_outlier", {"bfp8_outlier_blkscale", "bfp8_outlier_lb", "int8_outlier", "bfp8_2pass"}},
-        {"bfp4", {"bfp4_blkscale", "int4_blkscale", "int4_8x4"}},
-        {"global_logkmeans16", {"logkmeans16", "log_kmeans16"}},
-        {"global_logkmeans32", {"logkmeans32", "log_kmeans32"}},
-        {"global_logkmeans64", {"logkmeans64", "log_kmeans64"}},
-        {"global_logkmeans128", {"logkmeans128", "log_kmeans128"}}};
-    for (const auto& [name, list] : aliases)
-        if (std::find(list.begin(), list.end(), s) != list.end()) return name;
-    throw std::runtime_error(
-        "value-codec must be original, all_one, const_c, sign2, sign2_scale, dict2, dict4, dict16, dict256_u8, "
-        "dict65536_u16, auto_lossless, fp16, bf16, codebook256_u8, or global_logkmeans{16,32,64,128}");
-}
-
-Options parse(int argc, char** argv) {
-    Options o;
-    if (argc < 2) {
-        usage(argv[0], std::cerr);
-        std::exit(2);
-    }
-    o.matrix_path = argv[1];
-    for (int i = 2; i < argc; ++i) {
-        const std::string a = argv[i];
-        const bool more = i + 1 < argc;
-        if (a == "--precision" && more) {
-            o.precision = argv[++i];
-            if (o.precision != "float" && o.precision != "double")
-                throw std::runtime_error("precision must be float or double");
-        } else if (a == "--layout" && more) {
-            o.layout = canonical_layout(argv[++i], o.cusparse_alg);
-        } else if (a == "--value-codec" && more) {
-            o.value_codec = canonical_codec(argv[++i]);
-        } else if ((a == "--lb-chunk-blocks" || a == "--chunk-blocks") && more) {
-            o.lb_chunk_blocks = std::stoi(argv[++i]);
-            o.lb_override = true;
-        } else if ((a == "--lb-split-threshold-blocks" || a == "--split-threshold-blocks" ||
-                    a == "--lb-split-threshold") && more) {
-            o.lb_split_threshold_blocks = std::stoi(argv[++i]);
-            o.lb_override = true;
-        } else if (a == "--lb-policy" && more) {
-            const std::string p = argv[++i];
-            if (p == "manual" || p == "binary_implicit_one") o.lb_policy = p;
-            else if (p == "binary" || p == "implicit_one" || p == "all_one" || p == "binary_one")
-                o.lb_policy = "binary_implicit_one";
-            else throw std::runtime_error("lb-policy must be manual or binary_implicit_one");
-        } else if (a == "--cusparse-alg" && more) {
-            const std::string g = argv[++i];
-            if (g == "default" || g == "csr_alg1" || g == "csr_alg2") o.cusparse_alg = g;
-            else if (g == "alg1") o.cusparse_alg = "csr_alg1";
-            else if (g == "alg2") o.cusparse_alg = "csr_alg2";
-            else throw std::runtime_error("cusparse-alg must be default, csr_alg1, or csr_alg2");
-        } else if (a == "--warmup" && more) {
-            o.warmup = std::stoi(argv[++i]);
-        } else if ((a == "--iters" || a == "--iterations") && more) {
-            o.iterations = std::stoi(argv[++i]);
-        } else if (a == "--verify-cpu") {
-            o.verify_cpu = true;
-        } else if (a == "--help" || a == "-h") {
-            usage(argv[0], std::cerr);
-            std::exit(0);
-        } else {
-            throw std::runtime_error("unknown or incomplete argument: " + a);
-        }
-    }
-    if (o.warmup < 0 || o.iterations <= 0)
-        throw std::runtime_error("warmup must be non-negative and iterations must be positive");
-    if (o.lb_chunk_blocks <= 0) throw std::runtime_error("lb-chunk-blocks must be positive");
-    if (o.lb_split_threshold_blocks < 0) o.lb_split_threshold_blocks = o.lb_chunk_blocks;
-    if (o.lb_split_threshold_blocks <= 0) throw std::runtime_error("lb-split-threshold-blocks must be positive");
-    return o;
-}
-
-Layout layout_kind(const std::string& s) {
-    if (s == "col_bitmap64") return Layout::ColBitmap64;
-    if (s == "col_bitmap64_flag_lb") return Layout::ColBitmap64FlagLb;
-    return Layout::CusparseCsr;
-}
-
-// canonical codec name <-> enum, in the enum's order
+// report name of each value codec (value_codec_effective), in the enum's order
 const std::vector<std::pair<Codec, const char*>>& codec_names() {
     static const std::vector<std::pair<Codec, const char*>> t = {
         {Codec::Raw, "original"},          {Codec::ImplicitOne, "all_one"},
@@ -200,11 +55,6 @@ const std::vector<std::pair<Codec, const char*>>& codec_names() {
         {Codec::GlobalLogKmeans16, "global_logkmeans16"}, {Codec::GlobalLogKmeans32, "global_logkmeans32"},
         {Codec::GlobalLogKmeans64, "global_logkmeans64"}, {Codec::GlobalLogKmeans128, "global_logkmeans128"}};
     return t;
-}
-Codec codec_kind(const std::string& s) {
-    for (const auto& [k, n] : codec_names())
-        if (s == n) return k;
-    throw std::runtime_error("internal error: unknown normalized value codec");
 }
 const char* codec_name(Codec c) {
     for (const auto& [k, n] : codec_names())
@@ -592,14 +442,14 @@ void build_values(const structural::BitBsrMatrix<T>& b, Codec codec, structural:
 
 template <typename T>
 int run(const Options& o) {
-    const Layout layout = layout_kind(o.layout);
+    const Layout layout = structural::spmv_layout_kind_from_name(o.layout);
     const bool auto_lossless = o.value_codec == "auto_lossless";
     if (auto_lossless && layout == Layout::CusparseCsr)
         throw std::runtime_error("auto_lossless value codec is only supported for BitBSR layouts");
-    Codec codec = auto_lossless ? Codec::Raw : codec_kind(o.value_codec);
+    Codec codec = auto_lossless ? Codec::Raw : structural::spmv_value_codec_kind_from_name(o.value_codec);
     // before loading the matrix; auto_lossless re-derives it for the chosen codec
     SpmvOperatorSpec spec = structural::make_spmv_operator_spec(
-        layout, codec, auto_lossless ? structural::LoadBalancePolicy::Manual : requested_policy(o), o.lb_override);
+        layout, codec, auto_lossless ? structural::LoadBalancePolicy::Manual : requested_policy(o), structural::spmv_has_manual_load_balance_override(o));
     if (layout == Layout::CusparseCsr) return run_cusparse<T>(o, spec);
 
     Timing tm;
@@ -618,7 +468,7 @@ int run(const Options& o) {
         const auto h = timed_host([&] { return structural::build_device_exact_value_histogram(dev, &tm.auto_event); },
                                   tm.auto_host);
         codec = structural::select_auto_lossless_value_codec(h);
-        spec = structural::make_spmv_operator_spec(layout, codec, requested_policy(o), o.lb_override);
+        spec = structural::make_spmv_operator_spec(layout, codec, requested_policy(o), structural::spmv_has_manual_load_balance_override(o));
         r.auto_unique_count = h.unique_count;
         r.auto_unique_overflow = h.unique_overflow;
         r.auto_raw_bytes = h.raw_payload_bytes;
@@ -628,7 +478,7 @@ int run(const Options& o) {
     thrust::device_vector<T> d_x(x.begin(), x.end()), d_y;
     // load-balance chunking: the requested policy unless chunk sizes were given
     int chunk = o.lb_chunk_blocks, split = o.lb_split_threshold_blocks;
-    const bool binary_lb = structural::effective_requested_load_balance_policy(requested_policy(o), o.lb_override) ==
+    const bool binary_lb = structural::effective_requested_load_balance_policy(requested_policy(o), structural::spmv_has_manual_load_balance_override(o)) ==
                            structural::LoadBalancePolicy::BinaryImplicitOne;
     if (binary_lb) {  // the spec above already required flag_lb + all_one
         const auto p = structural::select_binary_implicit_one_load_balance_policy(dev.num_blocks, dev.rows);
@@ -713,7 +563,7 @@ int run(const Options& o) {
 
 int main(int argc, char** argv) {
     try {
-        const Options o = parse(argc, argv);
+        const Options o = structural::parse_spmv_cli_options(argc, argv);
         return o.precision == "float" ? run<float>(o) : run<double>(o);
     } catch (const std::exception& e) {
         std::cerr << "error: " << e.what() << "\n";
