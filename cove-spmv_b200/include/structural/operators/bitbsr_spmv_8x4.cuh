@@ -136,4 +136,196 @@ void spmv_bitbsr_gpu_8x4_bfp8_outlier_flag_load_balance_device(
     gpu_detail::run_bitbsr_route(bitbsr, packed_meta, v, x, y, device_ms);
 }
 
+// ---- the other per-codec operators (bitbsr_spmv_8x4_{raw,lossless,lossy}.cuh) ----
+//
+// Each codec has a load-balanced form (`..._flag_load_balance_<codec>`, with
+// the layout argument, checked as above) and a plain form (no layout); both
+// run the same route.  `..._device` takes device x and y; the form without
+// the suffix takes a host x and returns a host y.
+
+namespace gpu_detail {
+
+template <typename T>
+void check_plain_inputs(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<std::uint64_t>& packed_meta,
+                        const thrust::device_vector<T>& x) {
+    validate_bitbsr_8x4_shape(m);
+    if (static_cast<Index>(x.size()) != m.cols) throw std::runtime_error("GPU BitBSR SpMV input vector size mismatch");
+    if (static_cast<Offset>(packed_meta.size()) != m.num_blocks)
+        throw std::runtime_error("GPU BitBSR col_bitmap_packed layout size mismatch");
+}
+
+// Checks (with the layout when given) and runs one route.
+template <typename T>
+void run_codec(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<std::uint64_t>& packed_meta,
+               const BitBsrLoadBalanceLayout8x4* layout, const cove_values_desc& v, const thrust::device_vector<T>& x,
+               thrust::device_vector<T>& y, float* device_ms) {
+    if (layout) check_flag_lb_inputs(m, packed_meta, *layout, x);
+    else check_plain_inputs(m, packed_meta, x);
+    run_bitbsr_route(m, packed_meta, v, x, y, device_ms);
+}
+
+template <typename T>
+cove_values_desc sign_desc(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<std::uint32_t>& masks,
+                           double scale) {
+    if (static_cast<Offset>(masks.size()) != m.num_blocks)
+        throw std::runtime_error("GPU BitBSR sign tile mask count mismatch");
+    cove_values_desc v{};
+    v.route = COVE_ROUTE_SIGN2;
+    v.value_scale = scale;
+    v.sign_masks = raw(masks);
+    return v;
+}
+
+template <typename T>
+cove_values_desc tile_desc(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<std::uint32_t>& words,
+                           const thrust::device_vector<T>& codebook, int bits) {
+    if (words.size() != static_cast<size_t>(m.num_blocks) * bits)
+        throw std::runtime_error("GPU BitBSR tile code word count mismatch");
+    cove_values_desc v{};
+    v.route = COVE_ROUTE_TILE_CODE;
+    v.tile_bits = bits;
+    v.tile_code_words = raw(words);
+    v.codebook = raw(codebook);
+    v.codebook_size = static_cast<int64_t>(codebook.size());
+    return v;
+}
+
+template <typename T, typename F>
+std::vector<T> on_host(const std::vector<T>& x, F&& device_call) {
+    const thrust::device_vector<T> dx(x.begin(), x.end());
+    thrust::device_vector<T> dy;
+    device_call(dx, dy);
+    std::vector<T> y(dy.size());
+    thrust::copy(dy.begin(), dy.end(), y.begin());
+    return y;
+}
+
+}  // namespace gpu_detail
+
+// raw values, plain form and the host forms
+template <typename T>
+void spmv_bitbsr_gpu_8x4_col_bitmap_packed_device(const DeviceBitBsrMatrix<T>& bitbsr,
+                                                  const thrust::device_vector<std::uint64_t>& packed_meta,
+                                                  const thrust::device_vector<T>& x, thrust::device_vector<T>& y,
+                                                  float* device_ms = nullptr) {
+    cove_values_desc v{};
+    v.route = COVE_ROUTE_HYBRID;
+    v.kept = gpu_detail::raw(bitbsr.values);
+    gpu_detail::run_codec(bitbsr, packed_meta, nullptr, v, x, y, device_ms);
+}
+
+template <typename T>
+thrust::device_vector<T> spmv_bitbsr_gpu_8x4_col_bitmap_packed_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const thrust::device_vector<T>& x, float* device_ms = nullptr) {
+    thrust::device_vector<T> y;
+    spmv_bitbsr_gpu_8x4_col_bitmap_packed_device(bitbsr, packed_meta, x, y, device_ms);
+    return y;
+}
+
+template <typename T>
+std::vector<T> spmv_bitbsr_gpu_8x4_col_bitmap_packed(const DeviceBitBsrMatrix<T>& bitbsr,
+                                                     const thrust::device_vector<std::uint64_t>& packed_meta,
+                                                     const std::vector<T>& x, float* device_ms = nullptr) {
+    return gpu_detail::on_host(x, [&](const thrust::device_vector<T>& dx, thrust::device_vector<T>& dy) {
+        spmv_bitbsr_gpu_8x4_col_bitmap_packed_device(bitbsr, packed_meta, dx, dy, device_ms);
+    });
+}
+
+template <typename T>
+std::vector<T> spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const BitBsrLoadBalanceLayout8x4& layout, const std::vector<T>& x, float* device_ms = nullptr) {
+    return gpu_detail::on_host(x, [&](const thrust::device_vector<T>& dx, thrust::device_vector<T>& dy) {
+        spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_device(bitbsr, packed_meta, layout, dx, dy, device_ms);
+    });
+}
+
+// The named forms of one codec: NAME_device / NAME (host) in the plain and
+// the load-balanced variants.  PARAMS are the codec's payload parameters,
+// ARGS the same names, DESC the cove_values_desc built from them.
+#define COVE_SHIM_CODEC_OPERATORS(NAME, PARAMS, ARGS, DESC)                                                        \
+    template <typename T>                                                                                          \
+    void spmv_bitbsr_gpu_8x4_col_bitmap_packed_##NAME##_device(                                                    \
+        const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta PARAMS,       \
+        const thrust::device_vector<T>& x, thrust::device_vector<T>& y, float* device_ms = nullptr) {             \
+        gpu_detail::run_codec(bitbsr, packed_meta, nullptr, DESC, x, y, device_ms);                               \
+    }                                                                                                              \
+    template <typename T>                                                                                          \
+    std::vector<T> spmv_bitbsr_gpu_8x4_col_bitmap_packed_##NAME(                                                   \
+        const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta PARAMS,       \
+        const std::vector<T>& x, float* device_ms = nullptr) {                                                    \
+        return gpu_detail::on_host(x, [&](const thrust::device_vector<T>& dx, thrust::device_vector<T>& dy) {     \
+            spmv_bitbsr_gpu_8x4_col_bitmap_packed_##NAME##_device(bitbsr, packed_meta ARGS, dx, dy, device_ms);   \
+        });                                                                                                        \
+    }                                                                                                              \
+    template <typename T>                                                                                          \
+    void spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_##NAME##_device(                                  \
+        const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,              \
+        const BitBsrLoadBalanceLayout8x4& layout PARAMS, const thrust::device_vector<T>& x,                        \
+        thrust::device_vector<T>& y, float* device_ms = nullptr) {                                                \
+        gpu_detail::run_codec(bitbsr, packed_meta, &layout, DESC, x, y, device_ms);                               \
+    }                                                                                                              \
+    template <typename T>                                                                                          \
+    std::vector<T> spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_##NAME(                                 \
+        const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,              \
+        const BitBsrLoadBalanceLayout8x4& layout PARAMS, const std::vector<T>& x, float* device_ms = nullptr) {    \
+        return gpu_detail::on_host(x, [&](const thrust::device_vector<T>& dx, thrust::device_vector<T>& dy) {     \
+            spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_##NAME##_device(bitbsr, packed_meta, layout    \
+                                                                                        ARGS, dx, dy, device_ms); \
+        });                                                                                                        \
+    }
+
+#define COVE_SHIM_COMMA ,
+#define COVE_SHIM_TILE_PARAMS \
+    COVE_SHIM_COMMA const thrust::device_vector<std::uint32_t>& tile_code_words COVE_SHIM_COMMA \
+        const thrust::device_vector<T>& codebook
+#define COVE_SHIM_TILE_ARGS COVE_SHIM_COMMA tile_code_words COVE_SHIM_COMMA codebook
+
+namespace gpu_detail {
+inline cove_values_desc route_only(int route) {
+    cove_values_desc v{};
+    v.route = route;
+    return v;
+}
+inline cove_values_desc constant(double c) {
+    cove_values_desc v{};
+    v.route = COVE_ROUTE_CONST_C;
+    v.value_scale = c;
+    return v;
+}
+}  // namespace gpu_detail
+
+// every value 1 / every value C (bitbsr_spmv_8x4_lossless.cuh)
+COVE_SHIM_CODEC_OPERATORS(implicit_one, , , gpu_detail::route_only(COVE_ROUTE_IMPLICIT_ONE))
+COVE_SHIM_CODEC_OPERATORS(const_c, COVE_SHIM_COMMA T value, COVE_SHIM_COMMA value,
+                          gpu_detail::constant(static_cast<double>(value)))
+// +-1 and +-C by a sign mask per block
+COVE_SHIM_CODEC_OPERATORS(sign_tile32, COVE_SHIM_COMMA const thrust::device_vector<std::uint32_t>& sign_masks,
+                          COVE_SHIM_COMMA sign_masks, gpu_detail::sign_desc(bitbsr, sign_masks, 1.0))
+COVE_SHIM_CODEC_OPERATORS(sign2_scale_tile32,
+                          COVE_SHIM_COMMA const thrust::device_vector<std::uint32_t>& sign_masks COVE_SHIM_COMMA T scale,
+                          COVE_SHIM_COMMA sign_masks COVE_SHIM_COMMA scale,
+                          gpu_detail::sign_desc(bitbsr, sign_masks, static_cast<double>(scale)))
+// per-cell codes into a codebook: 1, 2, 4, 8, 16 bits
+COVE_SHIM_CODEC_OPERATORS(dict2_tile32, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 1))
+COVE_SHIM_CODEC_OPERATORS(unique4_tile64, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 2))
+COVE_SHIM_CODEC_OPERATORS(unique16_tile128, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 4))
+COVE_SHIM_CODEC_OPERATORS(dict256_tile256, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 8))
+COVE_SHIM_CODEC_OPERATORS(k256_tile256, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 8))
+COVE_SHIM_CODEC_OPERATORS(logkmeans_tile256, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 8))
+COVE_SHIM_CODEC_OPERATORS(dict65536_tile512, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 16))
+
+#undef COVE_SHIM_TILE_ARGS
+#undef COVE_SHIM_TILE_PARAMS
+#undef COVE_SHIM_COMMA
+#undef COVE_SHIM_CODEC_OPERATORS
+
 }  // namespace structural
