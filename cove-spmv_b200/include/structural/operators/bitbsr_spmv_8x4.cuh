@@ -176,11 +176,17 @@ cove_values_desc sign_desc(const DeviceBitBsrMatrix<T>& m, const thrust::device_
     return v;
 }
 
+// Codes of `bits` bits per cell into a codebook of at most max_codebook
+// entries (validate_tile_code_value_codec, common.cuh:942-964).
 template <typename T>
 cove_values_desc tile_desc(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<std::uint32_t>& words,
-                           const thrust::device_vector<T>& codebook, int bits) {
+                           const thrust::device_vector<T>& codebook, int bits, int max_codebook, const char* name) {
     if (words.size() != static_cast<size_t>(m.num_blocks) * bits)
-        throw std::runtime_error("GPU BitBSR tile code word count mismatch");
+        throw std::runtime_error(std::string("GPU BitBSR ") + name + " tile code word size mismatch");
+    if (codebook.size() > static_cast<size_t>(max_codebook))
+        throw std::runtime_error(std::string("GPU BitBSR ") + name + " codebook is too large");
+    if (m.nnz > 0 && codebook.empty())
+        throw std::runtime_error(std::string("GPU BitBSR ") + name + " codebook is empty");
     cove_values_desc v{};
     v.route = COVE_ROUTE_TILE_CODE;
     v.tile_bits = bits;
@@ -288,6 +294,29 @@ inline cove_values_desc route_only(int route) {
     v.route = route;
     return v;
 }
+template <typename T>
+cove_values_desc nnz16_desc(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<std::uint16_t>& values16,
+                            bool bf16, const char* name) {
+    if (static_cast<Offset>(values16.size()) != m.nnz)
+        throw std::runtime_error(std::string("GPU BitBSR ") + name + " per-nnz value size mismatch");
+    cove_values_desc v{};
+    v.route = bf16 ? COVE_ROUTE_BF16_NNZ : COVE_ROUTE_FP16_NNZ;
+    v.kept = raw(values16);
+    return v;
+}
+template <typename T>
+cove_values_desc bfp4_desc(const DeviceBitBsrMatrix<T>& m, const thrust::device_vector<std::uint8_t>& packed_int4,
+                           const thrust::device_vector<std::uint16_t>& block_scale_bf16) {
+    if (static_cast<Offset>(packed_int4.size()) != (m.nnz + 1) / 2)
+        throw std::runtime_error("GPU BitBSR bfp4_blkscale int4 value size mismatch");
+    if (static_cast<Offset>(block_scale_bf16.size()) != m.num_blocks)
+        throw std::runtime_error("GPU BitBSR bfp4_blkscale per-block scale size mismatch");
+    cove_values_desc v{};
+    v.route = COVE_ROUTE_BFP4;
+    v.kept = raw(packed_int4);
+    v.block_scale = raw(block_scale_bf16);
+    return v;
+}
 inline cove_values_desc constant(double c) {
     cove_values_desc v{};
     v.route = COVE_ROUTE_CONST_C;
@@ -309,21 +338,84 @@ COVE_SHIM_CODEC_OPERATORS(sign2_scale_tile32,
                           gpu_detail::sign_desc(bitbsr, sign_masks, static_cast<double>(scale)))
 // per-cell codes into a codebook: 1, 2, 4, 8, 16 bits
 COVE_SHIM_CODEC_OPERATORS(dict2_tile32, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
-                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 1))
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 1, 2, "dict2_tile32"))
 COVE_SHIM_CODEC_OPERATORS(unique4_tile64, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
-                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 2))
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 2, 4, "unique4_tile64"))
 COVE_SHIM_CODEC_OPERATORS(unique16_tile128, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
-                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 4))
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 4, 16, "unique16_tile128"))
 COVE_SHIM_CODEC_OPERATORS(dict256_tile256, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
-                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 8))
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 8, 256, "dict256_tile256"))
 COVE_SHIM_CODEC_OPERATORS(k256_tile256, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
-                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 8))
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 8, 256, "k256_tile256"))
 COVE_SHIM_CODEC_OPERATORS(logkmeans_tile256, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
-                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 8))
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 8, 256, "logkmeans_tile256"))
 COVE_SHIM_CODEC_OPERATORS(dict65536_tile512, COVE_SHIM_TILE_PARAMS, COVE_SHIM_TILE_ARGS,
-                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 16))
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, 16, 65536, "dict65536_tile512"))
+
+// 16-bit values per nonzero (bitbsr_spmv_8x4_lossy.cuh:35-58, 132-158)
+COVE_SHIM_CODEC_OPERATORS(fp16_nnz, COVE_SHIM_COMMA const thrust::device_vector<std::uint16_t>& values16,
+                          COVE_SHIM_COMMA values16, gpu_detail::nnz16_desc(bitbsr, values16, false, "fp16_nnz"))
+COVE_SHIM_CODEC_OPERATORS(bf16_nnz, COVE_SHIM_COMMA const thrust::device_vector<std::uint16_t>& values16,
+                          COVE_SHIM_COMMA values16, gpu_detail::nnz16_desc(bitbsr, values16, true, "bf16_nnz"))
+// packed signed 4-bit mantissas times a bf16 scale per block
+COVE_SHIM_CODEC_OPERATORS(bfp4_blkscale,
+                          COVE_SHIM_COMMA const thrust::device_vector<std::uint8_t>& packed_int4 COVE_SHIM_COMMA
+                              const thrust::device_vector<std::uint16_t>& block_scale_bf16,
+                          COVE_SHIM_COMMA packed_int4 COVE_SHIM_COMMA block_scale_bf16,
+                          gpu_detail::bfp4_desc(bitbsr, packed_int4, block_scale_bf16))
 
 #undef COVE_SHIM_TILE_ARGS
+
+template <bool Bf16, typename T>
+void spmv_bitbsr_gpu_8x4_col_bitmap_packed_round16_nnz_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const thrust::device_vector<std::uint16_t>& values16, const char* codec_name, const thrust::device_vector<T>& x,
+    thrust::device_vector<T>& y, float* device_ms = nullptr) {
+    gpu_detail::run_codec(bitbsr, packed_meta, nullptr, gpu_detail::nnz16_desc(bitbsr, values16, Bf16, codec_name), x, y,
+                          device_ms);
+}
+
+template <typename T>
+void spmv_bitbsr_gpu_8x4_col_bitmap_packed_bfp8_blkscale_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const thrust::device_vector<signed char>& int8_values, const thrust::device_vector<std::uint16_t>& block_scale_bf16,
+    const thrust::device_vector<T>& x, thrust::device_vector<T>& y, float* device_ms = nullptr) {
+    gpu_detail::check_bfp8_payload(bitbsr, int8_values, block_scale_bf16, "bfp8_blkscale");
+    cove_values_desc v{};
+    v.route = COVE_ROUTE_BFP8;
+    v.kept = gpu_detail::raw(int8_values);
+    v.block_scale = gpu_detail::raw(block_scale_bf16);
+    gpu_detail::run_codec(bitbsr, packed_meta, nullptr, v, x, y, device_ms);
+}
+
+// Codes of BitsPerCode (1, 2, 4, 8 or 16) bits per cell (common.cuh:1180-1300).
+template <int BitsPerCode, typename T>
+void spmv_bitbsr_gpu_8x4_col_bitmap_packed_code_tile_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const thrust::device_vector<std::uint32_t>& tile_code_words, const thrust::device_vector<T>& codebook,
+    int max_codebook_size, const char* codec_name, const thrust::device_vector<T>& x, thrust::device_vector<T>& y,
+    float* device_ms = nullptr) {
+    static_assert(BitsPerCode == 1 || BitsPerCode == 2 || BitsPerCode == 4 || BitsPerCode == 8 || BitsPerCode == 16,
+                  "tile codes are 1, 2, 4, 8 or 16 bits");
+    gpu_detail::run_codec(bitbsr, packed_meta, nullptr,
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, BitsPerCode, max_codebook_size,
+                                                codec_name),
+                          x, y, device_ms);
+}
+
+template <int BitsPerCode, typename T>
+void spmv_bitbsr_gpu_8x4_col_bitmap_packed_flag_load_balance_code_tile_device(
+    const DeviceBitBsrMatrix<T>& bitbsr, const thrust::device_vector<std::uint64_t>& packed_meta,
+    const BitBsrLoadBalanceLayout8x4& layout, const thrust::device_vector<std::uint32_t>& tile_code_words,
+    const thrust::device_vector<T>& codebook, int max_codebook_size, const char* codec_name,
+    const thrust::device_vector<T>& x, thrust::device_vector<T>& y, float* device_ms = nullptr) {
+    static_assert(BitsPerCode == 1 || BitsPerCode == 2 || BitsPerCode == 4 || BitsPerCode == 8 || BitsPerCode == 16,
+                  "tile codes are 1, 2, 4, 8 or 16 bits");
+    gpu_detail::run_codec(bitbsr, packed_meta, &layout,
+                          gpu_detail::tile_desc(bitbsr, tile_code_words, codebook, BitsPerCode, max_codebook_size,
+                                                codec_name),
+                          x, y, device_ms);
+}
 #undef COVE_SHIM_TILE_PARAMS
 #undef COVE_SHIM_COMMA
 #undef COVE_SHIM_CODEC_OPERATORS
