@@ -467,7 +467,7 @@ int run(const Options& o) {
     if (auto_lossless) {
         const auto h = timed_host([&] { return structural::build_device_exact_value_histogram(dev, &tm.auto_event); },
                                   tm.auto_host);
-        codec = structural::select_auto_lossless_value_codec(h);
+        codec = structural::cove::select_auto_lossless_value_codec(h);
         spec = structural::make_spmv_operator_spec(layout, codec, requested_policy(o), structural::spmv_has_manual_load_balance_override(o));
         r.auto_unique_count = h.unique_count;
         r.auto_unique_overflow = h.unique_overflow;

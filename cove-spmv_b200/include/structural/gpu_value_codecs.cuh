@@ -88,9 +88,13 @@ DeviceExactValueHistogram build_device_exact_value_histogram(const DeviceBitBsrM
     return h;
 }
 
-// The smallest exact codec whose payload beats the raw values
-// (select_auto_lossless_value_codec, main_gpu_spmv.cu:127-174), as the
-// operator's codec kind.
+namespace cove {
+
+// The smallest exact codec whose payload beats the raw values, as the
+// operator's codec kind.  The reference keeps this choice inside its CLI
+// (select_auto_lossless_value_codec, main_gpu_spmv.cu:127-174, file-local),
+// so it lives in this shim's own namespace: reference sources that define
+// theirs still compile against the shim.
 inline BitBsrValueCodecKind8x4 select_auto_lossless_value_codec(const DeviceExactValueHistogram& h) {
     using K = BitBsrValueCodecKind8x4;
     if (h.nnz == 0) return K::Raw;
@@ -107,6 +111,8 @@ inline BitBsrValueCodecKind8x4 select_auto_lossless_value_codec(const DeviceExac
         return K::Dict65536U16;
     return K::Raw;
 }
+
+}  // namespace cove
 
 // ---- per-cell walk ---------------------------------------------------------------
 
@@ -571,6 +577,61 @@ template <typename T>
 Bfp4BlkScaleValueCodec build_checked_bfp4_blkscale_value_codec(const BitBsrMatrix<T>& bitbsr) {
     validate_tile_shape_8x4(bitbsr);
     return build_bfp4_blkscale_value_codec(bitbsr);
+}
+
+template <typename T>
+T build_checked_const_c_value(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_const_c_value(bitbsr);
+}
+
+template <typename T>
+Sign2ScaleTile32ValueCodec<T> build_checked_sign2_scale_tile32_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_sign2_scale_tile32_value_codec(bitbsr);
+}
+
+template <typename T>
+Dict2Tile32ValueCodec<T> build_checked_dict2_tile32_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_dict2_tile32_value_codec(bitbsr);
+}
+
+template <typename T>
+Unique4Tile64ValueCodec<T> build_checked_unique4_tile64_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_unique4_tile64_value_codec(bitbsr);
+}
+
+template <typename T>
+Unique16Tile128ValueCodec<T> build_checked_unique16_tile128_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_unique16_tile128_value_codec(bitbsr);
+}
+
+template <typename T>
+Dict256Tile256ValueCodec<T> build_checked_dict256_tile256_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_dict256_tile256_value_codec(bitbsr);
+}
+
+template <typename T>
+Dict65536Tile512ValueCodec<T> build_checked_dict65536_tile512_value_codec(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_dict65536_tile512_value_codec(bitbsr);
+}
+
+template <typename T>
+K256Tile256BuildResult<T> build_checked_k256_tile256_build_result(const BitBsrMatrix<T>& bitbsr) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_k256_tile256_build_result(bitbsr);
+}
+
+template <typename T>
+LogKmeansTile256BuildResult<T> build_checked_logkmeans_tile256_build_result(const BitBsrMatrix<T>& bitbsr,
+                                                                            int requested_k) {
+    validate_tile_shape_8x4(bitbsr);
+    return build_logkmeans_tile256_build_result(bitbsr, requested_k);
 }
 
 }  // namespace structural

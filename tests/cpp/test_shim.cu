@@ -485,7 +485,7 @@ void test_family_builders() {
         DeviceBitBsrMatrix<double> dev;
         golden_bitbsr(kinds[i], &dev);
         const auto h = build_device_exact_value_histogram(dev);
-        CHECK(select_auto_lossless_value_codec(h) == want[i]);
+        CHECK(cove::select_auto_lossless_value_codec(h) == want[i]);
     }
     // an all-one matrix
     auto ones = golden_bitbsr(4);
@@ -493,7 +493,7 @@ void test_family_builders() {
     for (auto& v : one.values) v = 1.0;
     structural::GpuBitBsrWorkspace<double> ws;
     const auto d1 = convert_to_bitbsr_gpu_warp_direct_8x4_device(one, ws);
-    CHECK(select_auto_lossless_value_codec(build_device_exact_value_histogram(d1)) == K::ImplicitOne);
+    CHECK(cove::select_auto_lossless_value_codec(build_device_exact_value_histogram(d1)) == K::ImplicitOne);
     (void)ones;
 }
 

@@ -1,8 +1,8 @@
 """The reference's own tests and drivers built unchanged against this
 repository's structural:: shim and libcove_b200 (oracle/Makefile, the
 refshim_* programs in oracle/_ref): its option-handling test passes on
-CPU, and its CG bench and convert CLI load the library and answer without
-a GPU.  Its GPU converter test, refshim_test_gpu_convert, builds the same
+CPU, and its CG bench, convert CLI and family runner load the library and
+answer without a GPU.  Its GPU converter test, refshim_test_gpu_convert, builds the same
 way; it needs a GPU.  These programs exist only where the reference
 checkout was present at build time."""
 import os
@@ -12,7 +12,7 @@ import pytest
 
 ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
 REF = os.path.join(ROOT, "oracle", "_ref")
-NAMES = ("test_spmv_cli_options", "test_gpu_convert", "bench_cg_solve", "main_gpu_convert")
+NAMES = ("test_spmv_cli_options", "test_gpu_convert", "bench_cg_solve", "main_gpu_convert", "main_gpu_spmv")
 
 pytestmark = pytest.mark.skipif(not os.path.exists(os.path.join(REF, "libcove_ref.so")),
                                 reason="built only where the reference checkout exists")
@@ -38,3 +38,9 @@ def test_reference_drivers_load_the_library():
     assert p.returncode == 2 and "usage:" in p.stderr and "synth:N:halfbw:delta" in p.stderr
     p = subprocess.run([_bin("main_gpu_convert")], capture_output=True, text=True, timeout=60)
     assert p.returncode == 2 and "usage:" in p.stderr and "--mode warp_direct" in p.stderr
+    # the reference's family runner: its options now go through the shim's parser
+    p = subprocess.run([_bin("main_gpu_spmv")], capture_output=True, text=True, timeout=60)
+    assert p.returncode == 2 and "usage:" in p.stderr and "global_logkmeans128" in p.stderr
+    p = subprocess.run([_bin("main_gpu_spmv"), "m.mtx", "--layout", "sell"], capture_output=True, text=True,
+                       timeout=60)
+    assert p.returncode != 0 and "layout must be col_bitmap64, col_bitmap64_flag_lb, or cusparse_csr" in p.stderr
