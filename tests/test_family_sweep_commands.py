@@ -24,3 +24,15 @@ def test_sweep_commands_pass_option_handling(tmp_path):
         if p.returncode == 0 or "cannot open MatrixMarket file" not in p.stderr:
             bad.append((r["operator"], r["precision"], p.returncode, p.stderr.strip()[-200:]))
     assert not bad, bad[:5]
+
+
+def test_joint_sweep_commands_pass_option_handling(tmp_path):
+    """run_joint_sweep.py:75-79 builds [bin, matrix, --mode fused_lb,
+    --long-row-split 256, --value-codec C, --warmup W, --iters I, --verify-cpu]
+    for its default codecs bfp8, bfp8_outlier and auto (:35)."""
+    exe = os.path.join(BIN_DIR, "struct_gpu_csr_bitbsr_spmv")
+    for codec in ("bfp8", "bfp8_outlier", "auto"):
+        p = subprocess.run([exe, str(tmp_path / "absent.mtx"), "--mode", "fused_lb", "--long-row-split", "256",
+                            "--value-codec", codec, "--warmup", "5", "--iters", "30", "--verify-cpu"],
+                           capture_output=True, text=True, timeout=60)
+        assert p.returncode != 0 and "cannot open MatrixMarket file" in p.stderr, (codec, p.stderr)
