@@ -538,7 +538,7 @@ const char* cove_status_string(cove_status s) {
     return "unknown status";
 }
 
-const char* cove_version(void) { return "cove-b200 0.1.0 (sm_100a)"; }
+const char* cove_version(void) { return "cove-b200 0.2.0 (sm_100a)"; }
 
 void cove_plan_opts_default(cove_plan_opts* o) {
     if (!o) return;

@@ -194,7 +194,8 @@ typedef enum {
 /* Message of the last failing call on this host thread ("" if none). */
 COVE_API const char* cove_last_error(void);
 COVE_API const char* cove_status_string(cove_status s);
-/* Library version string. */
+/* Library version string.  0.2: cove_plan_opts ends with move_mask
+ * (COVE_SPLIT_MASK); callers built against 0.1 must be rebuilt. */
 COVE_API const char* cove_version(void);
 
 /* ---- plan (converter + split + layout + codecs + gate) --------------- */
