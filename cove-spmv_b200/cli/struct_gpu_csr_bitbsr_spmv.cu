@@ -4,10 +4,12 @@
 // report), so the reference's sweep scripts (run_joint_sweep.py, the family
 // sweep's parse_key_values) can drive this build unchanged.
 //
-// Built: --mode fused_lb with the CSR residual (the hot path).  The
-// reference's other layouts of this CLI (--mode two_pass, --residual-format
-// brcoo|sell) are not part of this library and are rejected with an error;
-// the cuSPARSE CSR baseline is the cusparse_csr layout of struct_gpu_spmv.
+// Built: --mode fused_lb with the CSR residual (the hot path; the reference's
+// CLI accepts only the CSR residual too).  Its --mode two_pass is not part
+// of this library: it is refused once the matrix is read, where the
+// reference would start it.  Option checks and messages are the
+// reference's, in its order.  The cuSPARSE CSR baseline is the cusparse_csr
+// layout of struct_gpu_spmv.
 // Everything runs through the C ABI (cove_b200.h): the plan
 // is built on the GPU, x is the reference's canonical input vector, y is
 // timed with CUDA events, and --verify-cpu compares against a CPU CSR SpMV.
@@ -49,17 +51,22 @@ struct Options {
 };
 
 void usage(const char* argv0) {
-    std::cerr << "usage: " << argv0 << " MATRIX.mtx [--precision float|double] [--mode fused_lb]"
+    // the reference's text (--value-codec is accepted too, as there)
+    std::cerr << "usage: " << argv0 << " MATRIX.mtx [--precision float|double] [--mode fused_lb|two_pass]"
               << " [--split-policy threshold|cost_gated] [--residual-format csr] [--br 8] [--bc 4]"
               << " [--residual-threshold N] [--long-row-split N]"
               << " [--cost-bitmap-block X] [--cost-bitmap-nnz X] [--cost-csr-block X] [--cost-csr-nnz X]"
               << " [--lb-chunk-blocks N] [--lb-split-threshold-blocks N]"
-              << " [--value-codec original|auto|dict|bfp8|bfp8_outlier] [--operator-label NAME]"
+              << " [--cusparse-alg default|csr_alg1|csr_alg2] [--operator-label NAME]"
               << " [--warmup N] [--iters N] [--verify-cpu]\n";
 }
 
 int to_int(const std::string& s) { return std::stoi(s); }
 double to_double(const std::string& s) { return std::stod(s); }
+
+// The joint codecs (:1222-1223); any other --value-codec runs the lossless
+// hybrid alone, as the reference does.
+bool joint_codec(const std::string& c) { return c == "auto" || c == "dict" || c == "bfp8" || c == "bfp8_outlier"; }
 
 Options parse_options(int argc, char** argv) {
     Options o;
@@ -76,10 +83,25 @@ Options parse_options(int argc, char** argv) {
         const std::string a = argv[i];
         const bool has = i + 1 < argc;
         auto val = [&]() { return std::string(argv[++i]); };
-        if (a == "--precision" && has) o.precision = val();
-        else if (a == "--mode" && has) o.mode = val();
-        else if (a == "--split-policy" && has) o.split_policy = val();
-        else if (a == "--residual-format" && has) o.residual_format = val();
+        // values checked as they are read, with the reference's aliases and
+        // messages (main_gpu_csr_bitbsr_spmv.cu:85-106, 128-141)
+        if (a == "--precision" && has) {
+            o.precision = val();
+            if (o.precision != "float" && o.precision != "double")
+                throw std::runtime_error("precision must be float or double");
+        } else if (a == "--mode" && has) {
+            o.mode = val();
+            if (o.mode == "fused") o.mode = "fused_lb";
+            if (o.mode != "fused_lb" && o.mode != "two_pass") throw std::runtime_error("mode must be fused_lb or two_pass");
+        } else if (a == "--split-policy" && has) {
+            o.split_policy = val();
+            if (o.split_policy == "cost" || o.split_policy == "auto") o.split_policy = "cost_gated";
+            if (o.split_policy != "threshold" && o.split_policy != "cost_gated")
+                throw std::runtime_error("split-policy must be threshold or cost_gated");
+        } else if (a == "--residual-format" && has) {
+            o.residual_format = val();
+            if (o.residual_format != "csr") throw std::runtime_error("residual-format must be csr");
+        }
         else if (a == "--br" && has) o.block_rows = to_int(val());
         else if (a == "--bc" && has) o.block_cols = to_int(val());
         else if ((a == "--residual-threshold" || a == "--threshold") && has) o.residual_threshold = to_int(val());
@@ -92,7 +114,13 @@ Options parse_options(int argc, char** argv) {
         else if ((a == "--lb-chunk-blocks" || a == "--chunk-blocks") && has) o.lb_chunk_blocks = to_int(val());
         else if ((a == "--lb-split-threshold-blocks" || a == "--split-threshold-blocks" ||
                   a == "--lb-split-threshold") && has) o.lb_split_threshold_blocks = to_int(val());
-        else if (a == "--cusparse-alg" && has) o.cusparse_alg = val();
+        else if (a == "--cusparse-alg" && has) {
+            o.cusparse_alg = val();
+            if (o.cusparse_alg == "alg1") o.cusparse_alg = "csr_alg1";
+            if (o.cusparse_alg == "alg2") o.cusparse_alg = "csr_alg2";
+            if (o.cusparse_alg != "default" && o.cusparse_alg != "csr_alg1" && o.cusparse_alg != "csr_alg2")
+                throw std::runtime_error("cusparse-alg must be default, csr_alg1, or csr_alg2");
+        }
         else if (a == "--operator-label" && has) o.operator_label = val();
         else if (a == "--warmup" && has) o.warmup = to_int(val());
         else if ((a == "--iters" || a == "--iterations") && has) o.iterations = to_int(val());
@@ -109,25 +137,12 @@ Options parse_options(int argc, char** argv) {
         throw std::runtime_error("CSR+BitBSR GPU probe currently supports only 8x4 blocks");
     if (o.residual_threshold < 0) throw std::runtime_error("residual-threshold must be non-negative");
     if (o.cost_bitmap_block < 0 || o.cost_bitmap_nnz < 0 || o.cost_csr_block < 0 || o.cost_csr_nnz < 0)
-        throw std::runtime_error("split cost model weights must be non-negative");
+        throw std::runtime_error("CSR+BitBSR split cost model must be non-negative");
     if (o.warmup < 0 || o.iterations <= 0)
         throw std::runtime_error("warmup must be non-negative and iterations must be positive");
     if (o.lb_chunk_blocks <= 0) throw std::runtime_error("lb-chunk-blocks must be positive");
     if (o.lb_split_threshold_blocks < 0) o.lb_split_threshold_blocks = o.lb_chunk_blocks;
     if (o.lb_split_threshold_blocks <= 0) throw std::runtime_error("lb-split-threshold-blocks must be positive");
-    if (o.precision != "double" && o.precision != "float")
-        throw std::runtime_error("precision must be float or double");
-    if (o.split_policy != "cost_gated" && o.split_policy != "threshold")
-        throw std::runtime_error("unsupported split policy: " + o.split_policy);
-    if (o.mode != "fused_lb")
-        throw std::runtime_error("mode " + o.mode + " is not part of this build (fused_lb only)");
-    if (o.residual_format != "csr")
-        throw std::runtime_error("residual format " + o.residual_format +
-                                 " is not part of this build (csr only)");
-    if (o.long_row_split < 0) throw std::runtime_error("long-row-split must be non-negative");
-    const std::string& c = o.value_codec;
-    if (c != "original" && c != "auto" && c != "dict" && c != "bfp8" && c != "bfp8_outlier")
-        throw std::runtime_error("unsupported value codec: " + c);
     return o;
 }
 
@@ -193,6 +208,7 @@ int run(const Options& o) {
     const auto t_load = std::chrono::steady_clock::now();
     const auto loaded = structural::read_matrix_market_with_info<T>(o.matrix_path);
     const double load_ms = host_ms_since(t_load);
+    if (o.mode == "two_pass") throw std::runtime_error("mode two_pass is not part of this build (fused_lb only)");
     const auto& A = loaded.matrix;
 
     const auto t_ctx = std::chrono::steady_clock::now();
@@ -231,7 +247,7 @@ int run(const Options& o) {
     po.lb_chunk_blocks = o.lb_chunk_blocks;
     po.lb_split_threshold_blocks = o.lb_split_threshold_blocks;
     po.lb_style = COVE_LB_HYBRID;
-    po.long_row_split = o.long_row_split;
+    po.long_row_split = std::max(0, o.long_row_split);  // <= 0: no long-row chunks, as :1159
     po.value_codec = o.value_codec == "auto" ? COVE_CODEC_AUTO
                      : o.value_codec == "dict" ? COVE_CODEC_DICT
                      : o.value_codec == "bfp8" ? COVE_CODEC_BFP8
@@ -282,7 +298,7 @@ int run(const Options& o) {
         verified = err[0] <= abs_tol || err[1] <= rel_tol;
     }
 
-    if (o.value_codec != "original") {
+    if (joint_codec(o.value_codec)) {
         const auto [joint_min_ms, joint_sum_ms] =
             time_route(plan, info.joint_route, d_x.p, d_y.p, o.warmup, o.iterations);
         (void)joint_sum_ms;
