@@ -1,27 +1,32 @@
 #!/usr/bin/env python3
 """Benchmark of the COVE SpMV hot path on B200 (one process per GPU).
 
-Workload (default): the FEM-like 27-point stencil, 64^3 nodes x 3 DOF
-(n = 786,432, nnz = 61,731,000, fp64 values), x ~ U[-1,1] seed 1, planned with
-the joint value codec `auto` (-> BFP8 blocks + bf16 residual, gated at 1e-2
-on the canonical x).  One step = one SpMV y = A x on the dispatched route.
+Workload (default, `--workload lapl3d_cg`): the 3D 7-point Laplacian on a
+768^3 grid (n = 452,984,832, nnz = 3,167,354,880, fp64, diagonal 6 and
+neighbours -1), b ~ U[-1,1] seed 4, x0 = 0.  One step = one solve of 50
+textbook CG iterations (the recurrence of the reference's CG bench) with the
+SpMV on the plan's dispatched route.  Rows are cut into z-slabs across the
+ranks (strong scaling: the same matrix at every N); each rank's slab is one
+or more int32-safe row-block plans, the x halo (one grid plane to each
+neighbour) arrives by NCCL send/recv overlapped with the interior rows, and
+the two dot products per iteration are NCCL allreduces.  `value` is the SpMV
+throughput inside the solve: 2 nnz / (device time of one SpMV, halo
+included), max over ranks, aggregated over the whole job.
 
-With --gpus N > 1 (torchrun, one rank per GPU) the FEM grid grows to
-64 x 64 x 64N nodes, partitioned into z-slabs of 64 planes: every rank owns
-the same row count as the 1-GPU run (weak scaling), and a step is the NCCL
-x-halo exchange (one node plane to each neighbour) followed by the local
-SpMV.  `value` is the whole-job GFLOP/s (2 nnz_total / t).
-
---workload lapl3d_cg runs the 3D 7-point Laplacian CG (strong scaling).
---workload lapl2d_512 / rmat_22 run those single matrices (2D 5-point
-Laplacian 512^2 fp64; R-MAT 2^22 nodes fp32, x ~ U[0,1)) through the same
-step; with N > 1 every rank runs its own replica (no collective).
+Other workloads: `--workload fem27` (config 2, the FEM 64^3 x 3 dof matrix;
+one step = one SpMV; N > 1: weak-scaling z-slabs with an NCCL halo),
+`lapl2d_512` / `rmat_22` (configs 1 and 3, one SpMV per step; N > 1:
+independent replicas), `blocksparse` (config 4, 5.3e9 nnz in row-block
+plans).
 
 Timing: W warm-up steps, then K steps bracketed by barrier + synchronize;
-each step's SpMV is timed with CUDA events on the launching stream and the
-L2 is flushed (a 256 MiB write) between steps, outside the event pair.
-`--impl reference` times the reference's own CPU SpMV (spmv_csr, OpenMP)
-on the same workload instead.
+device times from CUDA events on the launching stream, the max over ranks
+per step.  `e2e` repeats the step through the C ABI with pinned host
+buffers (inputs copied in and the result copied out every step).
+`--impl reference` times the reference's own CPU SpMV (structural::spmv_csr,
+OpenMP, every host core) on a bounded sample of the same workload; its input
+is built by the oracle's restatement of the generators, so that arm never
+loads this repository's library.
 """
 from __future__ import annotations
 
@@ -40,6 +45,7 @@ sys.path.insert(0, os.path.join(ROOT, "cove-spmv_b200"))
 import numpy as np  # noqa: E402
 
 FEM = dict(nx=64, ny=64, nz=64, dof=3, seed=1)
+STEP_SLEEP_CYCLES = 600_000  # about 0.3 ms of device sleep ahead of each multi-rank step
 
 
 def peaks():
@@ -124,17 +130,24 @@ def fem_partition(rank, world):
                 window_begin=wb, window_len=we - wb)
 
 
-def cpu_reference_time(rows, cols, rp, ci, v, x, reps):
-    """The reference's spmv_csr (OpenMP) on this host; (best ms, threads, kind)."""
+def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
+    return O
+
+
+def cpu_reference_time(rows, cols, rp, ci, v, x, reps):
+    """The reference's spmv_csr (OpenMP, every host core) on this host;
+    (best ms, threads, kind)."""
+    O = _oracle()
     if O.ref_available():
+        cores = O.ref_use_all_cores()
         t = O.RefCsrTimer(rows, cols, rp, ci, v, x)
         t.run(1)
         _, ms = t.run(reps)
         t.close()
-        return ms, O.ref_threads(), "reference"
+        return ms, cores, "reference"
     best = 1e300
     for _ in range(reps):
         t0 = time.perf_counter()
@@ -143,46 +156,85 @@ def cpu_reference_time(rows, cols, rp, ci, v, x, reps):
     return best, 1, "port"
 
 
+LAPL3D = dict(n=768, seed=4, iters=50, stream=7, sample_planes=8)
+L2_NOTE_CG = "inputs larger than L2 (every CG vector is n x 8 B, the matrix 10s of GB); no flush"
+L2_NOTE_FLUSH = "flushed between steps (256 MiB write, outside the timed events)"
+
+
+def lapl3d_nnz(g):
+    return 7 * g ** 3 - 6 * g ** 2
+
+
+def lapl3d_workload(g, iters):
+    return (f"3D 7-point Laplacian {g}^3 (n={g ** 3}, nnz={lapl3d_nnz(g)}), "
+            f"{iters} textbook CG iterations per step")
+
+
+def bench_config(args):
+    """The `config` object, identical in both arms for one workload."""
+    if args.workload == "lapl3d_cg":
+        g = args.grid or LAPL3D["n"]
+        return {"workload": lapl3d_workload(g, args.cg_iters), "l2": L2_NOTE_CG}
+    if args.workload == "fem27":
+        return {"workload": "fem27 64x64x64 nodes x3 dof (n=786432, nnz=61731000), one SpMV per step",
+                "l2": L2_NOTE_FLUSH}
+    if args.workload == "blocksparse":
+        n = args.bs_n or BLOCKSPARSE["n"]
+        return {"workload": f"block-sparse 8x4 n={n} (p_block {BLOCKSPARSE['p_block']}, "
+                            f"p_entry {BLOCKSPARSE['p_entry']}, {BLOCKSPARSE['outlier_fraction']:g} outliers),"
+                            f" one SpMV per step", "l2": L2_NOTE_FLUSH}
+    return {"workload": f"{args.workload}, one SpMV per step", "l2": L2_NOTE_FLUSH}
+
+
+def reference_sample(args):
+    """Bounded CPU sample of the workload: (rows, cols, rp, ci, v, x, description)."""
+    O = _oracle()
+    if args.workload == "lapl3d_cg":
+        # 3.2e9 nnz do not fit host memory: the SpMV of the first grid planes
+        # (their columns reach one plane further), x = b's first entries
+        g = args.grid or LAPL3D["n"]
+        planes = min(LAPL3D["sample_planes"], g)
+        rows = planes * g * g
+        rp, ci, v = O.lapl3d_rows(g, g, g, 0, rows)
+        cols = min(g, planes + 1) * g * g
+        x = O.vector("uniform_pm1", LAPL3D["seed"], LAPL3D["stream"], 0, cols)
+        return rows, cols, rp, ci, v, x, f"the SpMV of grid planes [0, {planes}) ({ci.size} nnz)"
+    if args.workload == "fem27":
+        rp, ci, v = O.fem27_rows(64, 64, 64, 3, FEM["seed"], 0, 786432)
+        x = O.vector("uniform_pm1", FEM["seed"], 7, 0, 786432)
+        return 786432, 786432, rp, ci, v, x, "the whole matrix"
+    if args.workload == "lapl2d_512":
+        rp, ci, v = O.lapl2d(512, 512)
+        x = O.vector("uniform_pm1", 0, 7, 0, 512 * 512)
+        return 512 * 512, 512 * 512, rp, ci, v, x, "the whole matrix"
+    # R-MAT and block-sparse inputs come from the library's host generators
+    import cove_b200 as cb
+
+    if args.workload == "rmat_22":
+        rows, n, rp, ci, v, x = cb.workload("rmat_22")
+        return rows, n, rp, ci, v, x, "the whole matrix"
+    bs = BLOCKSPARSE
+    n = args.bs_n or bs["n"]
+    rp, ci, v = cb.synth_blocksparse_rows(n, 0, min(n, 32768), bs["p_block"], bs["p_entry"],
+                                          bs["outlier_fraction"], bs["seed"])
+    x = cb.synth_vector("normal", n, seed=bs["seed"])
+    return len(rp) - 1, n, rp, ci, v, x, f"rows [0, {len(rp) - 1}) ({ci.size} nnz)"
+
+
 def run_reference_arm(args):
+    """The reference's own CPU SpMV (structural::spmv_csr compiled from its
+    headers into oracle/_ref, OpenMP over every host core), one bounded
+    sample of the workload per step; rank 0 only."""
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    import cove_b200 as cb
-
-    if args.workload in ("lapl2d_512", "rmat_22"):
-        rows, n, rp, ci, v, x = cb.workload(args.workload)
-        wname = f"{args.workload} (rows={rows}, nnz={ci.size})"
-    elif args.workload == "blocksparse":
-        # 5.3e9 nnz do not fit host memory: a bounded sample of its first rows
-        bs = BLOCKSPARSE
-        n = args.bs_n or bs["n"]
-        rp, ci, v = cb.synth_blocksparse_rows(n, 0, min(n, 32768), bs["p_block"], bs["p_entry"],
-                                              bs["outlier_fraction"], bs["seed"])
-        rows = len(rp) - 1
-        x = cb.synth_vector("normal", n, seed=bs["seed"])
-        wname = f"block-sparse 8x4 n={n}, rows [0, {rows}) ({ci.size} nnz)"
-    elif args.workload == "lapl3d_cg":
-        # 3.2e9 nnz do not fit host memory: the SpMV of the first 8 grid planes
-        # (their columns reach one plane further)
-        g = args.grid or LAPL3D["n"]
-        planes = min(8, g)
-        rows, _, rp, ci, v = cb.synth_lapl3d(g, g, g, 0, planes * g * g, 0)
-        n = min(g, planes + 1) * g * g
-        x = cb.synth_vector("uniform_pm1", n, seed=LAPL3D["seed"])
-        wname = f"3D 7-point Laplacian {g}^3, the SpMV of planes [0, {planes}) ({ci.size} nnz)"
-    else:
-        part = fem_partition(0, 1)
-        rows, n, rp, ci, v = cb.synth_fem27_rows(part["nx"], part["ny"], part["nz"], part["dof"],
-                                                 FEM["seed"], part["row_begin"], part["row_end"], 0)
-        x = cb.synth_vector("uniform_pm1", n, seed=FEM["seed"])
-        wname = "fem27_64^3x3 (n=786432, nnz=61731000)"
+    O = _oracle()
+    rows, n, rp, ci, v, x, sample = reference_sample(args)
     nnz = int(ci.size)
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-
     kind = "reference" if O.ref_available() else "port"
     times = []
     if kind == "reference":
+        cores = O.ref_use_all_cores()
         t = O.RefCsrTimer(rows, n, rp, ci, v, x)
         for _ in range(args.warmup):
             t.run(1)
@@ -190,7 +242,6 @@ def run_reference_arm(args):
             _, ms = t.run(1)
             times.append(ms)
         t.close()
-        cores = O.ref_threads()
     else:
         for i in range(args.warmup + args.steps):
             t0 = time.perf_counter()
@@ -202,14 +253,14 @@ def run_reference_arm(args):
     gflops = 2.0 * nnz / (ms * 1e-3) / 1e9
     cg = args.workload == "lapl3d_cg"
     line = {
-        "impl": "reference", "metric": "cg_spmv_gflops" if cg else "spmv_gflops", "value": round(gflops, 3),
+        "impl": "reference", "metric": "spmv_gflops", "value": round(gflops, 3),
         "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong" if cg else "weak",
         "vs_baseline": None, "dtype": "f64" if v.dtype == np.float64 else "f32", "data": "synthetic",
-        "config": {"workload": wname, "sample": "one SpMV of the workload above per step"},
+        "config": bench_config(args),
         "cpu_baseline": {"value": round(gflops, 3), "unit": "GFLOP/s", "cores": cores,
                          "kind": kind,
-                         "sample": f"structural::spmv_csr on {wname}, one SpMV per step"},
+                         "sample": f"structural::spmv_csr, one SpMV per step of {sample}"},
         "e2e": {"value": round(gflops, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -305,6 +356,13 @@ def run_fem(args):
     w0 = time.perf_counter()
     for i in range(args.steps):
         flush.zero_()
+        if world > 1:
+            # every rank starts the step together: a barrier, then a short
+            # device sleep that covers the host's enqueue of the whole step
+            # (the NCCL halo included), so the events time the GPU's work and
+            # not a rank's host falling behind
+            dist.barrier()
+            torch.cuda._sleep(STEP_SLEEP_CYCLES)
         ev[i][0].record(stream)
         step(xw, y)
         ev[i][1].record(stream)
@@ -372,33 +430,28 @@ def run_fem(args):
         c1.record()
         torch.cuda.synchronize()
         copy_ms[name] = c0.elapsed_time(c1) / 10
-    tot = torch.tensor([ms, float(np.mean(e2e_ms)), float(nnz_local), rel, wall],
+    tot = torch.tensor(step_ms + [float(np.mean(e2e_ms)), float(nnz_local), rel, wall],
                        dtype=torch.float64, device=dev)
+    K = args.steps
     if world > 1:
-        mx = tot.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = tot.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms_all, e2e_all, rel_all = float(mx[0]), float(mx[1]), float(mx[3])
-        nnz_total = float(sm[2])
+        allv = [torch.empty_like(tot) for _ in range(world)]
+        dist.all_gather(allv, tot)
+        M = torch.stack(allv).cpu().numpy()
     else:
-        ms_all, e2e_all, rel_all, nnz_total = ms, float(np.mean(e2e_ms)), rel, float(nnz_local)
+        M = tot.cpu().numpy()[None, :]
+    step_max = M[:, :K].max(axis=0)  # per step, the slowest rank
+    ms_all = float(step_max.mean())
+    e2e_all, rel_all = float(M[:, K].max()), float(M[:, K + 2].max())
+    nnz_total = float(M[:, K + 1].sum())
 
     if rank == 0:
         hbm, peak_kind = peaks()
         alg_bytes = int(info.algorithmic_bytes[route])
-        achieved = alg_bytes / (ms * 1e-3) / 1e9
+        achieved = alg_bytes / (ms_all * 1e-3) / 1e9  # every rank holds the same rows
         gflops = 2.0 * nnz_total / (ms_all * 1e-3) / 1e9
         e2e_gflops = 2.0 * nnz_total / (e2e_all * 1e-3) / 1e9
-        traffic = None
-        prof = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(prof):
-            try:
-                with open(prof) as f:
-                    t = json.load(f)
-                traffic = t.get("fem27_64" if fem else args.workload, {}).get(cb.ROUTE_NAMES[route])
-            except Exception:
-                traffic = None
+        tr = load_traffic("fem27_64" if fem else args.workload, cb.ROUTE_NAMES[route])
+        traffic = int(round(tr["bytes"] * nnz_local / tr["nnz"])) if tr and tr.get("nnz") else None
         # the reference's CPU SpMV on the same matrix, bounded sample
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -427,12 +480,16 @@ def run_fem(args):
                                        if fem else f"{world} independent replicas"),
                        "plan_build_s": round(build_s, 3), "kernel_slots": info.kernel_slots,
                        "e2e_ms_mean": round(e2e_all, 4), "e2e_ms_median_rank0": round(e2e_median, 4),
+                       "ms_per_step_median": round(float(np.median(step_max)), 5),
+                       "ms_per_step_max": round(float(step_max.max()), 5),
                        "host_copy_ms_rank0": {k: round(v, 4) for k, v in copy_ms.items()},
                        "cusparse_csr_ms_rank0": round(vendor_ms, 5) if vendor_ms else None,
                        "parity_rel_vs_cpu": rel_all},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
-                         "algorithmic_bytes": alg_bytes, "traffic": traffic},
+                         "algorithmic_bytes": alg_bytes, "traffic": traffic,
+                         "traffic_source": (f"ncu DRAM bytes of one launch on {tr['case']} "
+                                            f"(profiles/traffic.json)") if traffic else None},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gflops, 3), "unit": "GFLOP/s",
                     "h2d_bytes_per_step": wl * esz, "d2h_bytes_per_step": rows * esz},
@@ -449,7 +506,6 @@ def run_fem(args):
     return 0
 
 
-LAPL3D = dict(n=768, seed=4, iters=50)
 MAX_SHARD_NNZ = 2_000_000_000  # one plan per shard keeps the int32 offsets of the format
 
 
@@ -465,6 +521,19 @@ def lapl3d_partition(rank, world, nx, ny, nz):
     we = min(nz, k1 + 1) * plane
     return dict(row_begin=k0 * plane, row_end=k1 * plane, window_begin=wb, window_len=we - wb,
                 shards=shards)
+
+
+def load_traffic(key, route):
+    """ncu DRAM bytes of one launch of the dominant kernel on a captured case,
+    with the nnz of that case (profiles/traffic.json), or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            t = json.load(f)
+        e = t.get(key, {}).get(route)
+    except Exception:
+        return None
+    return e
 
 
 def run_lapl3d_cg(args):
@@ -483,8 +552,10 @@ def run_lapl3d_cg(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
-    n1 = args.grid or LAPL3D["n"]
-    nx = ny = nz = n1
+    g = args.grid or LAPL3D["n"]
+    nx = ny = nz = g
+    n_global = g ** 3
+    iters = args.cg_iters
     part = lapl3d_partition(rank, world, nx, ny, nz)
     stream = torch.cuda.current_stream()
     sh = C.c_void_p(stream.cuda_stream)
@@ -509,9 +580,12 @@ def run_lapl3d_cg(args):
         del csr, rp, ci, v
         torch.cuda.empty_cache()
     build_s = time.perf_counter() - t0
+    route = plans[0].info.dispatched_route
+    alg_local = sum(int(p.info.algorithmic_bytes[p.info.dispatched_route]) for p in plans)
     rows_local = part["row_end"] - part["row_begin"]
+    p_off = part["row_begin"] - part["window_begin"]
     b = torch.empty(rows_local, dtype=torch.float64, device=dev)
-    cb.check(L.cove_synth_vector_device(0, LAPL3D["seed"], 7, part["row_begin"], rows_local,
+    cb.check(L.cove_synth_vector_device(0, LAPL3D["seed"], LAPL3D["stream"], part["row_begin"], rows_local,
                                         C.c_void_p(b.data_ptr()), sh))
     x = torch.zeros(rows_local, dtype=torch.float64, device=dev)
 
@@ -526,51 +600,138 @@ def run_lapl3d_cg(args):
     D = C.c_void_p()
     arr = (C.c_void_p * len(plans))(*[p.handle.value for p in plans])
     cb.check(L.cove_dist_create(rank, world, idbuf.ctypes.data_as(C.c_void_p), arr, len(plans),
-                                nx * ny * nz, part["row_begin"], part["row_end"],
+                                n_global, part["row_begin"], part["row_end"],
                                 part["window_begin"], part["window_len"], 300000, C.byref(D)))
-    res = cb.CgResult()
-    # warm-up solve (untimed), then the timed solve; each is LAPL3D iterations
-    iters = args.cg_iters
-    cb.check(L.cove_dist_cg_solve(D, C.c_void_p(b.data_ptr()), C.c_void_p(x.data_ptr()),
-                                  min(iters, args.warmup), C.byref(res), sh))
+
+    def solve(bd, xd):
+        res = cb.CgResult()
+        cb.check(L.cove_dist_cg_solve(D, C.c_void_p(bd.data_ptr()), C.c_void_p(xd.data_ptr()), iters,
+                                      C.byref(res), sh))
+        return res
+
+    for _ in range(args.warmup):
+        res = solve(b, x)
+    torch.cuda.synchronize()
+    # check of the solve: the true residual ||b - A x||^2 (one more distributed
+    # SpMV) against the recurrence's r.r, relative to r0.r0
+    xw = torch.zeros(part["window_len"], dtype=torch.float64, device=dev)
+    xw[p_off:p_off + rows_local].copy_(x)
+    yv = torch.empty(rows_local, dtype=torch.float64, device=dev)
+    cb.check(L.cove_dist_spmv(D, C.c_void_p(xw.data_ptr()), C.c_void_p(yv.data_ptr()), sh))
+    chk = ((b - yv) ** 2).sum().reshape(1)
+    del xw, yv
+    if world > 1:
+        dist.all_reduce(chk)
+    true_rs = float(chk[0])  # res.rs_final is already the global r.r
+    residual_gap = abs(true_rs - res.rs_final) / res.rs_initial if res.rs_initial else None
+
+    clk = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk.start()
+    time.sleep(0.3)
+    step_total, step_spmv, launches = [], [], 0
+    for _ in range(args.steps):
+        if world > 1:
+            dist.barrier()
+        res = solve(b, x)
+        step_total.append(res.ms_total)
+        step_spmv.append(res.ms_spmv)
+        launches += int(res.launches)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clk = ClockSampler(local)
-    clk.start()
-    time.sleep(0.3)
-    cb.check(L.cove_dist_cg_solve(D, C.c_void_p(b.data_ptr()), C.c_void_p(x.data_ptr()), iters,
-                                  C.byref(res), sh))
-    torch.cuda.synchronize()
     clocks = clk.stop()
-    # residual check of the solve: rs_final / rs_initial
-    vals = torch.tensor([res.ms_total, res.ms_spmv, float(nnz_local), res.rs_initial, res.rs_final],
-                        dtype=torch.float64, device=dev)
+    rs_ratio = res.rs_final / res.rs_initial if res.rs_initial else None
+
+    # end to end through the C ABI: b from pinned host memory in, the solution
+    # x out to pinned host memory, every step
+    e2e_steps = max(1, min(args.steps, 5))
+    bh = b.cpu().pin_memory()
+    xh = torch.empty(rows_local, dtype=torch.float64).pin_memory()
+    bd2 = torch.empty_like(b)
+    xd2 = torch.empty_like(x)
+    e2e = []
+    for i in range(1 + e2e_steps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t1 = time.perf_counter()
+        bd2.copy_(bh, non_blocking=True)
+        solve(bd2, xd2)
+        xh.copy_(xd2, non_blocking=True)
+        torch.cuda.synchronize()
+        if i >= 1:
+            e2e.append((time.perf_counter() - t1) * 1e3)
+    e2e_ok = bool(torch.equal(xh, x.cpu()))  # the same solve as the device-resident one
+
+    # per-step times of every rank; the step time is the max over ranks
+    loc = torch.tensor(step_total + step_spmv + e2e + [float(nnz_local), float(alg_local), float(launches),
+                                                       float(e2e_ok)], dtype=torch.float64, device=dev)
     if world > 1:
-        mx = vals.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = vals.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms_total, ms_spmv, nnz_total = float(mx[0]), float(mx[1]), float(sm[2])
+        allv = [torch.empty_like(loc) for _ in range(world)]
+        dist.all_gather(allv, loc)
+        M = torch.stack(allv).cpu().numpy()
     else:
-        ms_total, ms_spmv, nnz_total = res.ms_total, res.ms_spmv, float(nnz_local)
+        M = loc.cpu().numpy()[None, :]
+    K, E = args.steps, e2e_steps
+    tot = M[:, :K].max(axis=0)
+    spm = M[:, K:2 * K].max(axis=0)
+    e2e_max = M[:, 2 * K:2 * K + E].max(axis=0)
+    nnz_total = float(M[:, 2 * K + E].sum())
+    alg_total = float(M[:, 2 * K + E + 1].sum())
+    launches_total = int(M[:, 2 * K + E + 2].sum())
+    e2e_all_ok = bool(M[:, 2 * K + E + 3].min() > 0)
+
     if rank == 0:
-        per_iter = ms_total / iters
-        per_spmv = ms_spmv / iters
+        hbm, peak_kind = peaks()
+        ms_step = float(np.mean(tot))
+        ms_spmv = float(np.mean(spm)) / iters
+        gflops = 2.0 * nnz_total / (ms_spmv * 1e-3) / 1e9
+        achieved = alg_total / world / (ms_spmv * 1e-3) / 1e9
+        rname = cb.ROUTE_NAMES[route]
+        tr = load_traffic("lapl3d", rname)
+        traffic = None
+        if tr and tr.get("nnz"):
+            traffic = int(round(tr["bytes"] * (nnz_total / world) / tr["nnz"]))
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            rows_s, cols_s, rp_s, ci_s, v_s, x_s, sample = reference_sample(args)
+            cms, cores, kind = cpu_reference_time(rows_s, cols_s, rp_s, ci_s, v_s, x_s, 5)
+            cpu = {"value": round(2.0 * ci_s.size / (cms * 1e-3) / 1e9, 3), "unit": "GFLOP/s", "cores": cores,
+                   "kind": kind, "sample": f"best of 5 runs of structural::spmv_csr (OpenMP) on {sample}"}
+        e2e_ms = float(np.mean(e2e_max))
         line = {
-            "metric": "cg_spmv_gflops", "value": round(2.0 * nnz_total / (per_spmv * 1e-3) / 1e9, 3),
-            "unit": "GFLOP/s", "n_gpus": world, "steps": iters, "warmup": args.warmup,
-            "ms_per_step": round(per_iter, 5), "higher_is_better": True, "scaling": "strong",
+            "metric": "spmv_gflops", "value": round(gflops, 3), "unit": "GFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": f"3D 7-point Laplacian {nx}x{ny}x{nz} (n={nx * ny * nz}, nnz={int(nnz_total)}),"
-                                   f" {iters} textbook CG iterations",
-                       "route": cb.ROUTE_NAMES[plans[0].info.dispatched_route],
-                       "ms_per_iteration": round(per_iter, 5), "ms_per_spmv": round(per_spmv, 5),
-                       "cg_gflops_per_iteration": round((2.0 * nnz_total + 10.0 * nx * ny * nz) /
-                                                        (per_iter * 1e-3) / 1e9, 3),
-                       "rs_ratio": res.rs_final / res.rs_initial if res.rs_initial else None,
-                       "shards_per_rank": len(plans), "plan_build_s": round(build_s, 2),
-                       "parallelism": f"z-slab row blocks x{world}, NCCL halo + allreduce"},
+            "config": bench_config(args),
+            "details": {
+                "step": f"one solve of {iters} textbook CG iterations from x0 = 0",
+                "route": rname, "ms_per_iteration": round(ms_step / iters, 5),
+                "ms_per_spmv": round(ms_spmv, 5),
+                "ms_per_step_median": round(float(np.median(tot)), 4),
+                "ms_per_step_max": round(float(np.max(tot)), 4),
+                "iteration_gflops": round((2.0 * nnz_total + 10.0 * n_global) / (ms_step / iters * 1e-3) / 1e9, 3),
+                "rs_ratio": rs_ratio, "true_vs_recurrence_residual_gap": residual_gap,
+                "shards_per_rank": len(plans), "plan_build_s_rank0": round(build_s, 2),
+                "parallelism": "1 GPU" if world == 1 else f"z-slab row blocks x{world}, NCCL halo + allreduce",
+                "e2e_ms_per_step": round(e2e_ms, 3), "e2e_steps": E,
+                "e2e_result_equals_device_run": e2e_all_ok,
+                "gpu_launches_per_rank": launches // max(1, args.steps),
+            },
+            "roofline": {"bound": "hbm", "kernel": "the SpMV of one CG iteration (all its launches)",
+                         "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
+                         "algorithmic_bytes": int(alg_total / world), "traffic": traffic,
+                         "traffic_source": (f"ncu DRAM bytes of one launch on {tr['case']}, scaled by nnz "
+                                            f"(profiles/traffic.json)") if traffic else None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(2.0 * nnz_total * iters / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
+                    "h2d_bytes_per_step": n_global * 8, "d2h_bytes_per_step": n_global * 8},
+            "gpu_launches": launches_total,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
@@ -712,19 +873,23 @@ def run_blocksparse(args):
         torch.cuda.synchronize()
         if i >= args.warmup:
             e2e.append((time.perf_counter() - t1) * 1e3)
-    tot = torch.tensor([ms, float(np.mean(e2e)), float(nnz_local), rel], dtype=torch.float64, device=dev)
+    alg_local = sum(int(p.info.algorithmic_bytes[p.info.dispatched_route]) for p in plans)
+    tot = torch.tensor([ms, float(np.mean(e2e)), float(nnz_local), rel, float(alg_local)], dtype=torch.float64,
+                       device=dev)
     if world > 1:
         mx = tot.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         sm = tot.clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         ms_all, e2e_all, rel_all, nnz_total = float(mx[0]), float(mx[1]), float(mx[3]), float(sm[2])
+        alg_total = float(sm[4])
     else:
         ms_all, e2e_all, rel_all, nnz_total = ms, float(np.mean(e2e)), rel, float(nnz_local)
+        alg_total = float(alg_local)
     if rank == 0:
         hbm, peak_kind = peaks()
-        alg = sum(int(p.info.algorithmic_bytes[p.info.dispatched_route]) for p in plans)
-        achieved = alg / (ms * 1e-3) / 1e9
+        alg = int(alg_total / world)  # per GPU
+        achieved = alg / (ms_all * 1e-3) / 1e9
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             # bounded sample: the first 32,768 rows (~8e7 nnz) through the reference's spmv_csr
@@ -769,10 +934,10 @@ def run_blocksparse(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="fem27",
+    ap.add_argument("--workload", default="lapl3d_cg",
                     choices=["fem27", "lapl3d_cg", "lapl2d_512", "rmat_22", "blocksparse"])
     ap.add_argument("--bs-n", type=int, default=0, help="blocksparse: n (default 2^21)")
     ap.add_argument("--grid", type=int, default=0, help="lapl3d_cg: grid edge (default 768)")

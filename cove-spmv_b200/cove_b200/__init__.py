@@ -112,7 +112,8 @@ class ValuesDesc(C.Structure):
 
 class CgResult(C.Structure):
     _fields_ = [("iterations", C.c_int32), ("rs_initial", C.c_double),
-                ("rs_final", C.c_double), ("ms_total", C.c_double), ("ms_spmv", C.c_double)]
+                ("rs_final", C.c_double), ("ms_total", C.c_double), ("ms_spmv", C.c_double),
+                ("launches", C.c_int64)]
 
 
 class IrResult(C.Structure):

@@ -30,13 +30,21 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kDotCtas = 148 * 4;
 
-// partial sums of a . b over a fixed grid; partial[blockIdx.x]
-__global__ void dot_partial_kernel(int64_t n, const double* __restrict__ a,
-                                   const double* __restrict__ b, double* __restrict__ partial) {
-    double s = 0.0;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        s += a[i] * b[i];
+// ---- textbook CG vector passes ---------------------------------------------------
+// Each pass streams n-vectors once with 16-byte loads (kU independent pairs
+// in flight per thread) over the fixed kDotCtas x kThreads grid; the dot
+// partials of a pass are one per CTA in a fixed order, so every sum is
+// deterministic.  Vectors that are not 16-byte aligned take the scalar path.
+
+constexpr int kU = 4;
+constexpr int kVecCtasPerSm = kDotCtas / 148;  // the whole grid resident at once
+
+__device__ __forceinline__ bool al16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// the CTA's sum of s into partial[blockIdx.x]
+__device__ __forceinline__ void cta_partial(double s, double* __restrict__ partial) {
     __shared__ double sh[kThreads / 32];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -47,6 +55,51 @@ __global__ void dot_partial_kernel(int64_t n, const double* __restrict__ a,
         for (int w = 0; w < kThreads / 32; ++w) t += sh[w];
         partial[blockIdx.x] = t;
     }
+}
+
+// Visit every index of [0, n) once over the grid: with 16-byte aligned
+// vectors f2(j, nt) takes the U pairs j, j + nt, ... (pair j = elements 2j,
+// 2j + 1), the leftovers go elementwise to f1(i), as does everything when
+// the vectors are not aligned.
+template <int U, typename F2, typename F1>
+__device__ __forceinline__ void stream_pairs(int64_t n, bool vec, F2 f2, F1 f1) {
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    if (vec) {
+        const int64_t n2 = n >> 1;
+        int64_t j = tid;
+        for (; j + (U - 1) * nt < n2; j += U * nt) f2(j, nt);
+        for (; j < n2; j += nt) f1(2 * j), f1(2 * j + 1);
+        if ((n & 1) && tid == 0) f1(n - 1);
+    } else {
+        for (int64_t i = tid; i < n; i += nt) f1(i);
+    }
+}
+
+// partial sums of a . b; partial[blockIdx.x]
+__global__ void __launch_bounds__(kThreads, kVecCtasPerSm)
+dot_partial_kernel(int64_t n, const double* __restrict__ a, const double* __restrict__ b,
+                   double* __restrict__ partial) {
+    double s = 0.0;
+    const double2* a2 = reinterpret_cast<const double2*>(a);
+    const double2* b2 = reinterpret_cast<const double2*>(b);
+    stream_pairs<kU>(
+        n, al16(a) && al16(b),
+        [&](int64_t j, int64_t nt) {
+            double2 va[kU], vb[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                va[u] = a2[j + u * nt];
+                vb[u] = b2[j + u * nt];
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                s += va[u].x * vb[u].x;
+                s += va[u].y * vb[u].y;
+            }
+        },
+        [&](int64_t i) { s += a[i] * b[i]; });
+    cta_partial(s, partial);
 }
 
 __global__ void dot_final_kernel(const double* __restrict__ partial, int m,
@@ -63,42 +116,83 @@ __global__ void dot_final_kernel(const double* __restrict__ partial, int m,
     if (threadIdx.x == 0) *out = sh[0];
 }
 
-// x += alpha p; r -= alpha Ap; partial of r.r   (alpha = rs / pAp on device)
-__global__ void cg_update_kernel(int64_t n, const double* __restrict__ scal, int rs_slot,
-                                 const double* __restrict__ p, const double* __restrict__ ap,
-                                 double* __restrict__ x, double* __restrict__ r,
-                                 double* __restrict__ partial) {
-    const double rs = scal[rs_slot];
+__device__ __forceinline__ double cg_alpha(const double* __restrict__ scal, int rs_slot) {
     const double pap = scal[2];
-    const double alpha = pap != 0.0 ? rs / pap : 0.0;
-    double s = 0.0;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        x[i] += alpha * p[i];
-        const double ri = r[i] - alpha * ap[i];
-        r[i] = ri;
-        s += ri * ri;
-    }
-    __shared__ double sh[kThreads / 32];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double t = 0.0;
-        for (int w = 0; w < kThreads / 32; ++w) t += sh[w];
-        partial[blockIdx.x] = t;
-    }
+    return pap != 0.0 ? scal[rs_slot] / pap : 0.0;
 }
 
-// p = r + beta p, beta = rs_new / rs
-__global__ void cg_p_kernel(int64_t n, const double* __restrict__ scal, int rs_slot, int new_slot,
-                            const double* __restrict__ r, double* __restrict__ p) {
+// r -= alpha Ap and the partials of the new r.r   (alpha = rs / pAp on device)
+__global__ void __launch_bounds__(kThreads, kVecCtasPerSm)
+cg_r_kernel(int64_t n, const double* __restrict__ scal, int rs_slot, const double* __restrict__ ap,
+            double* __restrict__ r, double* __restrict__ partial) {
+    const double alpha = cg_alpha(scal, rs_slot);
+    double s = 0.0;
+    const double2* ap2 = reinterpret_cast<const double2*>(ap);
+    double2* r2 = reinterpret_cast<double2*>(r);
+    stream_pairs<kU>(
+        n, al16(ap) && al16(r),
+        [&](int64_t j, int64_t nt) {
+            double2 va[kU], vr[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                va[u] = ap2[j + u * nt];
+                vr[u] = r2[j + u * nt];
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                vr[u].x -= alpha * va[u].x;
+                vr[u].y -= alpha * va[u].y;
+                r2[j + u * nt] = vr[u];
+                s += vr[u].x * vr[u].x;
+                s += vr[u].y * vr[u].y;
+            }
+        },
+        [&](int64_t i) {
+            const double ri = r[i] - alpha * ap[i];
+            r[i] = ri;
+            s += ri * ri;
+        });
+    cta_partial(s, partial);
+}
+
+// x += alpha p (the p of this iteration), then p = r + beta p with
+// beta = rs_new / rs: the iteration's x update and the next direction in one
+// pass over x, p and r
+__global__ void __launch_bounds__(kThreads, kVecCtasPerSm)
+cg_xp_kernel(int64_t n, const double* __restrict__ scal, int rs_slot, int new_slot,
+             const double* __restrict__ r, double* __restrict__ p, double* __restrict__ x) {
+    const double alpha = cg_alpha(scal, rs_slot);
     const double rs = scal[rs_slot];
     const double beta = rs != 0.0 ? scal[new_slot] / rs : 0.0;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        p[i] = r[i] + beta * p[i];
+    const double2* r2 = reinterpret_cast<const double2*>(r);
+    double2* p2 = reinterpret_cast<double2*>(p);
+    double2* x2 = reinterpret_cast<double2*>(x);
+    constexpr int U = kU / 2;  // three streams: fewer pairs in flight keep it in 64 registers
+    stream_pairs<U>(
+        n, al16(r) && al16(p) && al16(x),
+        [&](int64_t j, int64_t nt) {
+            double2 vr[U], vp[U], vx[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                vp[u] = p2[j + u * nt];
+                vx[u] = x2[j + u * nt];
+                vr[u] = r2[j + u * nt];
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                vx[u].x += alpha * vp[u].x;
+                vx[u].y += alpha * vp[u].y;
+                x2[j + u * nt] = vx[u];
+                vp[u].x = vr[u].x + beta * vp[u].x;
+                vp[u].y = vr[u].y + beta * vp[u].y;
+                p2[j + u * nt] = vp[u];
+            }
+        },
+        [&](int64_t i) {
+            const double pi = p[i];
+            x[i] += alpha * pi;
+            p[i] = r[i] + beta * pi;
+        });
 }
 
 
@@ -377,15 +471,17 @@ void allreduce_scalar(cove_dist* d, double* v, cudaStream_t s) {
 // The route a plan runs for `route` (< 0: its dispatched route).
 int route_of(const cove_plan* P, int route) { return route < 0 ? P->dispatched_route : route; }
 
-// y_local = A_local x_window over the rank's plans (consecutive row blocks)
-float spmv_plans(const std::vector<cove_plan*>& plans, const double* xw, double* y,
-                 cudaStream_t s, int route = -1) {
+// y_local = A_local x_window over the rank's plans (consecutive row blocks);
+// returns the kernel launches
+int spmv_plans(const std::vector<cove_plan*>& plans, const double* xw, double* y,
+               cudaStream_t s, int route = -1) {
     int64_t off = 0;
+    int launches = 0;
     for (const cove_plan* P : plans) {
-        launch_hybrid_spmv(P->shape(), P->route_values(route_of(P, route)), xw, y + off, s);
+        launches += launch_hybrid_spmv(P->shape(), P->route_values(route_of(P, route)), xw, y + off, s);
         off += P->rows;
     }
-    return 0.0f;
+    return launches;
 }
 
 // y_local = A_local x_window on a partition: the block rows that read only
@@ -395,12 +491,12 @@ float spmv_plans(const std::vector<cove_plan*>& plans, const double* xw, double*
 // remaining waves (a short launch of its own would expose one block row's
 // serial load chain); the two passes write disjoint rows.  The compute
 // stream joins before any overflow pass.
-void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s, int route = -1) {
+int spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s, int route = -1) {
     if (!d->overlap) {
         halo(d, xw, s);
-        spmv_plans(d->plans, xw, y, s, route);
-        return;
+        return spmv_plans(d->plans, xw, y, s, route);
     }
+    int launches = 0;
     auto launch_ranges = [&](bool halo_rows, cudaStream_t st) {
         int64_t off = 0;
         for (size_t i = 0; i < d->plans.size(); ++i) {
@@ -413,7 +509,7 @@ void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s, int route = 
                 kr.part = 1;
                 kr.br_begin = r.b0;
                 kr.nbr = r.b1;
-                launch_hybrid_spmv(kr, rv, xw, y + off, st);
+                launches += launch_hybrid_spmv(kr, rv, xw, y + off, st);
             }
             off += P->rows;
         }
@@ -432,10 +528,11 @@ void spmv_dist(cove_dist* d, double* xw, double* y, cudaStream_t s, int route = 
         if (hybrid_spmv_launch_count(k, rv) > 1) {
             KernelShape ko = k;
             ko.part = 2;
-            launch_hybrid_spmv(ko, rv, xw, y + off, s);
+            launches += launch_hybrid_spmv(ko, rv, xw, y + off, s);
         }
         off += P->rows;
     }
+    return launches;
 }
 
 // Split each plan's block rows into runs that read only the rank's own
@@ -484,11 +581,32 @@ void dot(int64_t n, const double* a, const double* b, double* partial, double* o
     dot_final_kernel<<<1, kThreads, 0, s>>>(partial, kDotCtas, out);
 }
 
+// One textbook CG iteration after Ap = A p: p.Ap -> alpha; r -= alpha Ap and
+// the new r.r -> beta; x += alpha p and p = r + beta p.  Scalar slots: S[cur]
+// the iteration's r.r, S[cur ^ 1] the new one, S[2] p.Ap.  Ten n-vector
+// passes besides the SpMV.  Returns the kernel launches.
+int cg_vector_step(cove_dist* d, int64_t n, double* p, const double* ap, double* r, double* x,
+                   double* partial, double* S, int cur, cudaStream_t s) {
+    const int nxt = cur ^ 1;
+    dot(n, p, ap, partial, S + 2, s);
+    allreduce_scalar(d, S + 2, s);
+    cg_r_kernel<<<kDotCtas, kThreads, 0, s>>>(n, S, cur, ap, r, partial);
+    dot_final_kernel<<<1, kThreads, 0, s>>>(partial, kDotCtas, S + nxt);
+    allreduce_scalar(d, S + nxt, s);
+    cg_xp_kernel<<<kDotCtas, kThreads, 0, s>>>(n, S, cur, nxt, r, p, x);
+    return 5;
+}
+
 void cg_run(cove_dist* d, const std::vector<cove_plan*>& plans, int64_t n_local,
             int64_t p_off, int64_t wl, const double* b, double* x, int iters,
             cove_cg_result* res, cudaStream_t s) {
     for (const cove_plan* P : plans) {
         if (P->dtype != COVE_F64) COVE_THROW(COVE_ERR_UNSUPPORTED, "CG runs in fp64");
+    }
+    if (res) *res = cove_cg_result{};
+    if (n_local == 0 && !d) {  // nothing to solve (a partition's ranks all take the collective steps)
+        if (res) res->iterations = iters;
+        return;
     }
     DevBuf r, pw, ap, partial, scal;
     alloc_n<double>(r, n_local);
@@ -508,32 +626,23 @@ void cg_run(cove_dist* d, const std::vector<cove_plan*>& plans, int64_t n_local,
     wait_stream(d, s);
     double rs0 = 0.0;
     CUDA_OK(cudaMemcpy(&rs0, S, 8, cudaMemcpyDeviceToHost));
+    int64_t launches = 2;
 
     cudaEvent_t e0, e1;
     CUDA_OK(cudaEventCreate(&e0));
     CUDA_OK(cudaEventCreate(&e1));
     std::vector<cudaEvent_t> ev(2 * static_cast<size_t>(iters));
     for (auto& e : ev) CUDA_OK(cudaEventCreate(&e));
-    const int ug = static_cast<int>(std::min<int64_t>(grid_for(n_local, kThreads), kDotCtas));
     double spmv_ms = 0.0;
     CUDA_OK(cudaEventRecord(e0, s));
     for (int k = 0; k < iters; ++k) {
-        const int cur = k & 1, nxt = cur ^ 1;
         // the distributed SpMV: halo exchange overlapped with own-column rows
         CUDA_OK(cudaEventRecord(ev[2 * k], s));
-        if (d) {
-            spmv_dist(d, pw.as<double>(), ap.as<double>(), s);
-        } else {
-            spmv_plans(plans, pw.as<double>(), ap.as<double>(), s);
-        }
+        launches += d ? spmv_dist(d, pw.as<double>(), ap.as<double>(), s)
+                      : spmv_plans(plans, pw.as<double>(), ap.as<double>(), s);
         CUDA_OK(cudaEventRecord(ev[2 * k + 1], s));
-        dot(n_local, p, ap.as<double>(), partial.as<double>(), S + 2, s);
-        allreduce_scalar(d, S + 2, s);
-        cg_update_kernel<<<kDotCtas, kThreads, 0, s>>>(n_local, S, cur, p, ap.as<double>(), x,
-                                                      r.as<double>(), partial.as<double>());
-        dot_final_kernel<<<1, kThreads, 0, s>>>(partial.as<double>(), kDotCtas, S + nxt);
-        allreduce_scalar(d, S + nxt, s);
-        cg_p_kernel<<<ug, kThreads, 0, s>>>(n_local, S, cur, nxt, r.as<double>(), p);
+        launches += cg_vector_step(d, n_local, p, ap.as<double>(), r.as<double>(), x, partial.as<double>(),
+                                   S, k & 1, s);
         CUDA_LAUNCH_OK();
     }
     CUDA_OK(cudaEventRecord(e1, s));
@@ -556,6 +665,7 @@ void cg_run(cove_dist* d, const std::vector<cove_plan*>& plans, int64_t n_local,
         res->rs_final = rsf;
         res->ms_total = total;
         res->ms_spmv = spmv_ms;
+        res->launches = launches;
     }
 }
 
@@ -588,7 +698,7 @@ struct MpSolver {
         CUDA_OK(cudaMemsetAsync(xw.p, 0, static_cast<size_t>(wl) * 8, s));
         CUDA_OK(cudaMemsetAsync(pw.p, 0, static_cast<size_t>(wl) * 8, s));
         CUDA_OK(cudaMemsetAsync(scal.p, 0, 16 * 8, s));
-        ug = static_cast<int>(std::min<int64_t>(grid_for(n, kThreads), kDotCtas));
+        ug = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid_for(n, kThreads), kDotCtas)));
     }
     void matvec(int route, double* window, double* y) {
         if (d) {
@@ -1008,22 +1118,56 @@ namespace {
 
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
-double* g_noalloc_base[kNoAllocMaxDevices] = {};
+struct NoAllocSlot {
+    double* base = nullptr;
+    unsigned long long ctx_id = 0;  // the context the address belongs to
+};
+NoAllocSlot g_noalloc[kNoAllocMaxDevices];
 
-// Device address of the scratch array on the current device, looked up once
-// per device (the host-side name is only a stand-in for the symbol).
+// Unique id of the current CUDA context (driver entry point, resolved at run
+// time so the library does not link the driver library); 0 if unavailable.
+unsigned long long current_context_id() {
+    using GetCurrent = int (*)(void**);
+    using GetId = int (*)(void*, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(f);
+    });
+    void* ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current && get_id && get_current(&ctx) == 0 && ctx && get_id(ctx, &id) == 0) return id;
+    return 0;
+}
+
+// Device address of the scratch array on the current device (the host-side
+// name is only a stand-in for the symbol).  It is looked up once per device
+// and looked up again if the device's context was replaced since
+// (cudaDeviceReset), since the array then lives at a new address.
 double* noalloc_scratch() {
     int dev = -1;
     CUDA_OK(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kNoAllocMaxDevices)
         COVE_THROW(COVE_ERR_UNSUPPORTED, "device ordinal beyond the no-allocation scratch table");
+    const unsigned long long ctx = current_context_id();  // 0 before the context exists
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_base[dev]) {
+    NoAllocSlot& slot = g_noalloc[dev];
+    if (!slot.base || slot.ctx_id != ctx || ctx == 0) {
         double* ptr = nullptr;
         CUDA_OK(cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), cove_cg_noalloc_scratch));
-        g_noalloc_base[dev] = ptr;
+        slot.base = ptr;
+        slot.ctx_id = ctx;
     }
-    return g_noalloc_base[dev];
+    return slot.base;
 }
 
 void cg_run_noalloc(const cove_plan* P, const double* b, double* x, int iters,
@@ -1046,14 +1190,10 @@ void cg_run_noalloc(const cove_plan* P, const double* b, double* x, int iters,
     CUDA_OK(cudaMemcpyAsync(S + 4, S + 0, sizeof(double), cudaMemcpyDeviceToDevice, s));
     const KernelShape shape = P->shape();
     const RouteValues vals = P->route_values(P->dispatched_route);
-    const int ug = static_cast<int>(std::min<int64_t>(grid_for(n, kThreads), kDotCtas));
+    int64_t launches = 2;
     for (int k = 0; k < iters; ++k) {
-        const int cur = k & 1, nxt = cur ^ 1;
-        launch_hybrid_spmv(shape, vals, p, ap, s);
-        dot(n, p, ap, partial, S + 2, s);
-        cg_update_kernel<<<kDotCtas, kThreads, 0, s>>>(n, S, cur, p, ap, x, r, partial);
-        dot_final_kernel<<<1, kThreads, 0, s>>>(partial, kDotCtas, S + nxt);
-        cg_p_kernel<<<ug, kThreads, 0, s>>>(n, S, cur, nxt, r, p);
+        launches += launch_hybrid_spmv(shape, vals, p, ap, s);
+        launches += cg_vector_step(nullptr, n, p, ap, r, x, partial, S, k & 1, s);
     }
     CUDA_LAUNCH_OK();
     double h[8];
@@ -1065,6 +1205,7 @@ void cg_run_noalloc(const cove_plan* P, const double* b, double* x, int iters,
         res->rs_final = h[iters & 1];
         res->ms_total = 0.0;
         res->ms_spmv = 0.0;
+        res->launches = launches;
     }
 }
 

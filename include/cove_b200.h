@@ -391,6 +391,7 @@ typedef struct {
     double rs_final;     /* r . r after the last iteration */
     double ms_total;     /* device time of the iterations (CUDA events) */
     double ms_spmv;      /* device time of the SpMV kernels alone (sum) */
+    int64_t launches;    /* kernel launches of this library in the call */
 } cove_cg_result;
 
 /*
@@ -452,7 +453,9 @@ COVE_API cove_status cove_fcg_solve(const cove_plan* plan, int32_t inner_route, 
  *    COVE_ERR_INVALID_ARGUMENT and a message naming the limit;
  *  - the first call on each device looks up the array's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture begins;
+ *    before any stream capture begins.  After cudaDeviceReset the next call
+ *    on that device looks the address up again (the array then lives in a
+ *    new context, starting from zero);
  *  - all calls on one device share the array: calls that overlap on the GPU
  *    (other streams, other host threads) race and give wrong results;
  *  - synchronizes `stream`; result->ms_total and ms_spmv are 0 (no timing).

@@ -108,6 +108,14 @@ def _setup(L):
     L.oc_canonical_x.argtypes = [i64, i32, vp]
     L.oc_joint_bfp8_spmv.argtypes = [C.POINTER(_OcBitBsr), vp, vp, vp, vp, vp, i64, vp, vp,
                                      vp, vp, vp]
+    u64 = C.c_uint64
+    L.oc_vector.argtypes = [i32, u64, u64, i64, i64, vp]
+    L.oc_lapl3d_rows.restype = i64
+    L.oc_lapl3d_rows.argtypes = [i32, i32, i32, i64, i64, i64, vp, vp, vp]
+    L.oc_lapl2d.restype = i64
+    L.oc_lapl2d.argtypes = [i32, i32, vp, vp, vp]
+    L.oc_fem27_rows.restype = i64
+    L.oc_fem27_rows.argtypes = [i32, i32, i32, i32, u64, i64, i64, i64, vp, vp, vp]
 
 
 def _setup_ref(R):
@@ -131,6 +139,7 @@ def _setup_ref(R):
     R.ref_csr_spmv_timed.restype = f64
     R.ref_csr_spmv_timed.argtypes = [vp, i32, vp]
     R.ref_omp_max_threads.restype = i32
+    R.ref_omp_set_threads.argtypes = [i32]
     R.ref_compare_vectors.argtypes = [vp, vp, i64, i32, vp]
     R.ref_canonical_x.argtypes = [i32, i32, vp]
 
@@ -525,6 +534,18 @@ def ref_threads() -> int:
     return int(_ref().ref_omp_max_threads())
 
 
+def ref_use_all_cores() -> int:
+    """Give the reference's OpenMP loops every core this process may run on,
+    whatever OMP_NUM_THREADS a launcher set (torchrun sets 1); returns the
+    thread count now in force."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    _ref().ref_omp_set_threads(max(1, n))
+    return ref_threads()
+
+
 def ref_float_to_bf16_bits(v: float) -> int:
     return int(_ref().ref_float_to_bf16_bits(C.c_float(v)))
 
@@ -541,3 +562,48 @@ def ref_canonical_x(n, dtype=np.float64):
     x = np.zeros(n, dtype)
     _ref().ref_canonical_x(n, x.itemsize, _p(x))
     return x
+
+
+# ---- seeded benchmark inputs (oracle_workloads.c) ------------------------------
+
+def vector(kind, seed, stream, begin, n):
+    """Seeded vector of global indices [begin, begin + n): kind "uniform_pm1"
+    (U[-1,1]), "uniform01" or "normal"; float64."""
+    k = {"uniform_pm1": 0, "uniform01": 1, "normal": 2}[kind]
+    out = np.empty(n, np.float64)
+    _lib().oc_vector(k, seed, stream, begin, n, _p(out))
+    return out
+
+
+def _gen_csr(count, fill, rows):
+    nnz = count()
+    rp = np.zeros(rows + 1, np.int64)
+    ci = np.empty(nnz, np.int32)
+    v = np.empty(nnz, np.float64)
+    fill(_p(rp), _p(ci), _p(v))
+    return rp, ci, v
+
+
+def lapl3d_rows(nx, ny, nz, row_begin, row_end, col_shift=0):
+    """Rows [row_begin, row_end) of the 3D 7-point Laplacian: (rp, ci, v)."""
+    L = _lib()
+    return _gen_csr(lambda: L.oc_lapl3d_rows(nx, ny, nz, row_begin, row_end, col_shift, None, None, None),
+                    lambda a, b, c: L.oc_lapl3d_rows(nx, ny, nz, row_begin, row_end, col_shift, a, b, c),
+                    row_end - row_begin)
+
+
+def lapl2d(nx, ny):
+    """The 2D 5-point Laplacian on nx x ny: (rp, ci, v)."""
+    L = _lib()
+    return _gen_csr(lambda: L.oc_lapl2d(nx, ny, None, None, None),
+                    lambda a, b, c: L.oc_lapl2d(nx, ny, a, b, c), nx * ny)
+
+
+def fem27_rows(nx, ny, nz, dof, seed, row_begin, row_end, col_shift=0):
+    """Rows [row_begin, row_end) of the FEM-like 27-point stencil: (rp, ci, v)."""
+    L = _lib()
+    return _gen_csr(lambda: L.oc_fem27_rows(nx, ny, nz, dof, seed, row_begin, row_end, col_shift,
+                                            None, None, None),
+                    lambda a, b, c: L.oc_fem27_rows(nx, ny, nz, dof, seed, row_begin, row_end, col_shift,
+                                                    a, b, c),
+                    row_end - row_begin)

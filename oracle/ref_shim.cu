@@ -304,6 +304,10 @@ REF_EXPORT double ref_csr_spmv_timed(void* hv, int32_t reps, void* y_out) {
 
 REF_EXPORT int32_t ref_omp_max_threads() { return omp_get_max_threads(); }
 
+// Thread count of the reference's OpenMP loops from here on (a launcher may
+// have set OMP_NUM_THREADS=1 in the environment).
+REF_EXPORT void ref_omp_set_threads(int32_t n) { omp_set_num_threads(n > 0 ? n : 1); }
+
 REF_EXPORT void ref_compare_vectors(const void* ref, const void* got, int64_t n, int32_t esz,
                                     double* out3) {
     if (esz == 8) {

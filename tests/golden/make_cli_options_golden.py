@@ -7,14 +7,15 @@ as a layout, codec, policy and algorithm, plus a few that must fail; the
 argument lists cover each option, alias and check.  The answers come from
 oracle/_ref/ref_cli_options (tests/cpp/cli_options_table.cu built against
 the reference's headers by oracle/Makefile).
-Usage: make -C oracle && python tests/golden/make_cli_options_golden.py
+Usage: make -C oracle && [REF_ROOT=<reference checkout>] python tests/golden/make_cli_options_golden.py
 """
 import os
 import re
 import subprocess
 
 ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), "..", ".."))
-REF_HEADER = "/root/reference/structural/include/structural/spmv_cli_options.hpp"
+REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")  # the reference checkout, as oracle/Makefile
+REF_HEADER = os.path.join(REF_ROOT, "structural/include/structural/spmv_cli_options.hpp")
 
 ARGS = [
     "m.mtx",

@@ -4,7 +4,7 @@ operator of its catalog (DEFAULT_OPERATORS), in fp64 and fp32, with the
 binary directory and the matrix as placeholders ("BIN/...", "MATRIX").
 The script is imported from the reference checkout, as the reference's own
 tests/test_gpu_spmv_family_sweep.py does.
-Usage: python tests/golden/make_family_sweep_golden.py
+Usage: [REF_ROOT=<reference checkout>] python tests/golden/make_family_sweep_golden.py
 """
 import importlib.util
 import json
@@ -13,7 +13,8 @@ from pathlib import Path
 from types import SimpleNamespace
 
 ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), "..", ".."))
-SCRIPT = Path("/root/reference/structural/scripts/run_gpu_spmv_family_sweep.py")
+REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")  # the reference checkout, as oracle/Makefile
+SCRIPT = Path(REF_ROOT) / "structural/scripts/run_gpu_spmv_family_sweep.py"
 
 
 def main():

@@ -48,5 +48,37 @@ def test_reference_arm_for_the_cg_workload_uses_its_metric():
                              "--warmup", "3")
     assert rc == 0, err
     d = json.loads(out.strip().splitlines()[-1])
-    assert (d["metric"], d["scaling"], d["unit"]) == ("cg_spmv_gflops", "strong", "GFLOP/s")
-    assert d["value"] > 0 and "planes [0, 8)" in d["config"]["workload"]
+    assert (d["metric"], d["scaling"], d["unit"]) == ("spmv_gflops", "strong", "GFLOP/s")
+    assert d["value"] > 0 and d["config"]["workload"].startswith("3D 7-point Laplacian 32^3")
+    assert "planes [0, 8)" in d["cpu_baseline"]["sample"]
+
+
+def test_default_workload_is_the_cg_strong_scaling_config():
+    import bench
+
+    args = bench.argparse.Namespace(workload="lapl3d_cg", grid=0, cg_iters=50, bs_n=0)
+    cfg = bench.bench_config(args)
+    assert cfg["workload"] == ("3D 7-point Laplacian 768^3 (n=452984832, nnz=3167354880), "
+                               "50 textbook CG iterations per step")
+    assert bench.lapl3d_nnz(768) == 3167354880
+
+
+def test_reference_arm_never_loads_the_library_and_uses_every_core():
+    """The reference arm builds its input with the oracle's generators, so the
+    product library is never mapped into its process; OpenMP gets every core
+    even when a launcher set OMP_NUM_THREADS=1."""
+    code = (
+        "import sys, json, argparse; sys.path.insert(0, '.'); import bench;"
+        "a = argparse.Namespace(workload='lapl3d_cg', grid=24, cg_iters=50, bs_n=0, steps=1, warmup=1);"
+        "bench.run_reference_arm(a);"
+        "maps = open('/proc/self/maps').read();"
+        "print(json.dumps({'lib': 'libcove_b200' in maps, 'mod': 'cove_b200' in sys.modules}))"
+    )
+    e = dict(os.environ, OMP_NUM_THREADS="1")
+    p = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300, env=e, cwd=ROOT)
+    assert p.returncode == 0, p.stderr
+    lines = [ln for ln in p.stdout.splitlines() if ln.strip()]
+    line, probe = json.loads(lines[0]), json.loads(lines[-1])
+    assert probe == {"lib": False, "mod": False}
+    if line["cpu_baseline"]["kind"] == "reference":
+        assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))

@@ -46,6 +46,47 @@ def test_noalloc_cg_matches_cg_solve_on_two_calls():
     plan.close()
 
 
+def test_noalloc_cg_leaves_free_device_memory_unchanged():
+    """The property the entry point exists for: after a first call on the
+    device, a call takes no device memory (cudaMemGetInfo's free bytes are the
+    same before and after it)."""
+    import torch
+
+    L = cb.lib()
+    rows, n, rp, ci, v = cb.synth_lapl2d(200, 150)
+    plan = cb.Plan(cb.DeviceCsr.from_numpy(rows, n, rp, ci, v), value_codec="auto")
+    b = torch.from_numpy(cb.synth_vector("uniform_pm1", rows, seed=5)).cuda()
+    x = torch.empty_like(b)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    res = cb.CgResult()
+    args = (plan.handle, C.c_void_p(b.data_ptr()), C.c_void_p(x.data_ptr()), 20, C.byref(res), stream)
+    cb.check(L.cove_cg_solve_noalloc(*args))  # first call on the device: its set-up
+    torch.cuda.synchronize()
+    before = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        cb.check(L.cove_cg_solve_noalloc(*args))
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == before
+    assert res.iterations == 20 and res.rs_final < res.rs_initial
+    plan.close()
+
+
+def test_noalloc_cg_with_an_empty_plan_returns_zero_residuals():
+    import torch
+
+    L = cb.lib()
+    plan = cb.Plan(cb.DeviceCsr.from_numpy(0, 0, np.zeros(1, np.int64), np.zeros(0, np.int32),
+                                           np.zeros(0, np.float64)), value_codec="original")
+    b = torch.zeros(1, dtype=torch.float64, device="cuda")
+    x = torch.zeros(1, dtype=torch.float64, device="cuda")
+    for fn in (L.cove_cg_solve_noalloc, L.cove_cg_solve):
+        res = cb.CgResult()
+        cb.check(fn(plan.handle, C.c_void_p(b.data_ptr()), C.c_void_p(x.data_ptr()), 5, C.byref(res),
+                    C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        assert res.iterations == 5 and res.rs_initial == 0.0 and res.rs_final == 0.0
+    plan.close()
+
+
 def test_noalloc_cg_rejects_plans_beyond_its_scratch():
     import torch
 
