@@ -581,7 +581,10 @@ def run_lapl3d_cg(args):
         torch.cuda.empty_cache()
     build_s = time.perf_counter() - t0
     route = plans[0].info.dispatched_route
-    alg_local = sum(int(p.info.algorithmic_bytes[p.info.dispatched_route]) for p in plans)
+    # every plan's algorithmic bytes count its x window once; the rank's shards
+    # share one window, read once per SpMV
+    alg_local = sum(int(p.info.algorithmic_bytes[p.info.dispatched_route]) - 8 * int(p.info.cols)
+                    for p in plans) + 8 * part["window_len"]
     rows_local = part["row_end"] - part["row_begin"]
     p_off = part["row_begin"] - part["window_begin"]
     b = torch.empty(rows_local, dtype=torch.float64, device=dev)

@@ -34,6 +34,11 @@ namespace {
 
 constexpr int kThreads = 128;  // measured best for the main passes (64-512 tried)
 
+// The kernels' dynamic shared memory (a shared codebook).  Decoders index it
+// through this name, so the compiler emits shared-memory loads; a generic
+// pointer to it would cost generic loads on every lookup.
+extern __shared__ __align__(16) unsigned char g_smem[];
+
 __device__ __forceinline__ float bf16_to_float(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }
@@ -120,23 +125,24 @@ struct DictDec {
     const IdxT* __restrict__ res;
     const T* __restrict__ codebook;
     int64_t size;
-    const T* cb;  // shared copy when Smem
-    __device__ __forceinline__ void prepare(void* smem) {
+    __device__ __forceinline__ void prepare(void*) {
         if constexpr (Smem) {
-            T* s = static_cast<T*>(smem);
+            T* s = reinterpret_cast<T*>(g_smem);
             for (int64_t i = threadIdx.x; i < size; i += blockDim.x) s[i] = codebook[i];
-            cb = s;
-        } else {
-            cb = codebook;
         }
+    }
+    // the codebook entry: from the shared copy (Smem) or global memory
+    __device__ __forceinline__ T entry(uint32_t i) const {
+        if constexpr (Smem) return reinterpret_cast<const T*>(g_smem)[i];
+        return __ldg(codebook + i);
     }
     __device__ __forceinline__ V load(int64_t p) const { return kept[p]; }
     __device__ __forceinline__ void prefetch_values(int64_t a, int64_t b) const {
         prefetch_l2(kept + a, (b - a) * static_cast<int64_t>(sizeof(V)));
     }
     __device__ __forceinline__ Acc block_ctx(int64_t) const { return Acc(1); }
-    __device__ __forceinline__ Acc decode(V raw, Acc, int) const { return static_cast<Acc>(cb[raw]); }
-    __device__ __forceinline__ Acc res_val(int64_t p) const { return static_cast<Acc>(cb[res[p]]); }
+    __device__ __forceinline__ Acc decode(V raw, Acc, int) const { return static_cast<Acc>(entry(raw)); }
+    __device__ __forceinline__ Acc res_val(int64_t p) const { return static_cast<Acc>(entry(res[p])); }
     __device__ __forceinline__ Acc xv(const T* __restrict__ x, int64_t c) const { return static_cast<Acc>(x[c]); }
 };
 
@@ -301,8 +307,7 @@ struct Bfp4Dec {
 template <typename T, typename Dec, int SLOTS>
 __global__ void __launch_bounds__(kThreads)
 hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    dec.prepare(smem);
+    dec.prepare(g_smem);
     __syncthreads();  // a shared codebook is complete before any lane reads it
     using Acc = typename Dec::Acc;
     using V = typename Dec::V;
@@ -430,8 +435,7 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
 template <typename T, typename Dec>
 __global__ void __launch_bounds__(kThreads)
 hybrid_row_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    dec.prepare(smem);
+    dec.prepare(g_smem);
     __syncthreads();  // a shared codebook is complete before any lane reads it
     using Acc = typename Dec::Acc;
     using V = typename Dec::V;
@@ -490,8 +494,7 @@ hybrid_overflow_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T*
                        int heavy_ctas, int chunk_ctas, int64_t num_out,
                        const int32_t* __restrict__ orow, const int32_t* __restrict__ ocol,
                        const T* __restrict__ oval) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    dec.prepare(smem);
+    dec.prepare(g_smem);
     __syncthreads();
     using Acc = typename Dec::Acc;
     using V = typename Dec::V;
@@ -629,13 +632,13 @@ int launch_typed(const KernelShape& k, const RouteValues& v, const void* x, void
         case COVE_ROUTE_DICT_U8: {
             DictDec<T, uint8_t, true> d{static_cast<const uint8_t*>(v.kept),
                                         static_cast<const uint8_t*>(v.res),
-                                        static_cast<const T*>(v.codebook), v.codebook_size, nullptr};
+                                        static_cast<const T*>(v.codebook), v.codebook_size};
             return launch_with<T>(k, d, static_cast<size_t>(v.codebook_size) * sizeof(T), v, x, y, s);
         }
         case COVE_ROUTE_DICT_U16: {
             DictDec<T, uint16_t, false> d{static_cast<const uint16_t*>(v.kept),
                                           static_cast<const uint16_t*>(v.res),
-                                          static_cast<const T*>(v.codebook), v.codebook_size, nullptr};
+                                          static_cast<const T*>(v.codebook), v.codebook_size};
             return launch_with<T>(k, d, 0, v, x, y, s);
         }
         case COVE_ROUTE_BFP8:

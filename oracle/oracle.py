@@ -115,6 +115,8 @@ def _setup(L):
     L.oc_lapl2d.restype = i64
     L.oc_lapl2d.argtypes = [i32, i32, vp, vp, vp]
     L.oc_fem27_rows.restype = i64
+    L.oc_write_mtx.restype = C.c_int
+    L.oc_write_mtx.argtypes = [C.c_char_p, i64, i64, vp, vp, vp, i32]
     L.oc_fem27_rows.argtypes = [i32, i32, i32, i32, u64, i64, i64, i64, vp, vp, vp]
 
 
@@ -607,3 +609,12 @@ def fem27_rows(nx, ny, nz, dof, seed, row_begin, row_end, col_shift=0):
                     lambda a, b, c: L.oc_fem27_rows(nx, ny, nz, dof, seed, row_begin, row_end, col_shift,
                                                     a, b, c),
                     row_end - row_begin)
+
+
+def write_mtx(path, rows, cols, row_ptr, col_idx, values):
+    """MatrixMarket file of a CSR; values round-trip exactly (%.17g / %.9g)."""
+    rp = np.ascontiguousarray(row_ptr, np.int64)
+    ci = np.ascontiguousarray(col_idx, np.int32)
+    v = np.ascontiguousarray(values)
+    if _lib().oc_write_mtx(str(path).encode(), rows, cols, _p(rp), _p(ci), _p(v), v.itemsize) != 0:
+        raise OSError(f"cannot write {path}")

@@ -13,6 +13,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdio.h>
 
 #define OC_EXPORT __attribute__((visibility("default")))
 
@@ -146,4 +147,25 @@ OC_EXPORT int64_t oc_fem27_rows(int32_t nx, int32_t ny, int32_t nz, int32_t dof,
         }
     }
     return p;
+}
+
+/* MatrixMarket coordinate file of a CSR (1-based, "general"), values with
+ * %.17g (esz 8) or %.9g (esz 4) so they read back exactly.  Returns 0, or -1
+ * when the file cannot be written. */
+OC_EXPORT int oc_write_mtx(const char* path, int64_t rows, int64_t cols, const int64_t* row_ptr,
+                           const int32_t* col, const void* val, int32_t esz) {
+    FILE* f = fopen(path, "w");
+    if (!f) return -1;
+    static char buf[1 << 20];
+    setvbuf(f, buf, _IOFBF, sizeof(buf));
+    fprintf(f, "%%%%MatrixMarket matrix coordinate real general\n");
+    fprintf(f, "%lld %lld %lld\n", (long long)rows, (long long)cols, (long long)row_ptr[rows]);
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t p = row_ptr[r]; p < row_ptr[r + 1]; ++p) {
+            if (esz == 8)
+                fprintf(f, "%lld %d %.17g\n", (long long)(r + 1), col[p] + 1, ((const double*)val)[p]);
+            else
+                fprintf(f, "%lld %d %.9g\n", (long long)(r + 1), col[p] + 1, (double)((const float*)val)[p]);
+        }
+    return fclose(f) == 0 ? 0 : -1;
 }
