@@ -364,6 +364,7 @@ struct cove_dist {
     ncclComm_t comm = nullptr;
     std::vector<cove_plan*> plans;
     int64_t global_rows = 0, row_begin = 0, row_end = 0, wb = 0, wl = 0;
+    cove::CgWorkspace cg_ws;  // CG work vectors, kept between solves
     int timeout_ms = 60000;
     struct Xfer {
         int peer;
@@ -597,6 +598,21 @@ int cg_vector_step(cove_dist* d, int64_t n, double* p, const double* ap, double*
     return 5;
 }
 
+// The workspace for n rows and a window of wl entries: the kept vectors when
+// the sizes match (a previous solve on the same handle), else new ones.
+CgWorkspace& cg_workspace(CgWorkspace& ws, int64_t n, int64_t wl) {
+    if (ws.n != n || ws.wl != wl) {
+        alloc_n<double>(ws.r, n);
+        alloc_n<double>(ws.pw, wl);
+        alloc_n<double>(ws.ap, n);
+        alloc_n<double>(ws.partial, kDotCtas);
+        alloc_n<double>(ws.scal, 8);
+        ws.n = n;
+        ws.wl = wl;
+    }
+    return ws;
+}
+
 void cg_run(cove_dist* d, const std::vector<cove_plan*>& plans, int64_t n_local,
             int64_t p_off, int64_t wl, const double* b, double* x, int iters,
             cove_cg_result* res, cudaStream_t s) {
@@ -608,12 +624,8 @@ void cg_run(cove_dist* d, const std::vector<cove_plan*>& plans, int64_t n_local,
         if (res) res->iterations = iters;
         return;
     }
-    DevBuf r, pw, ap, partial, scal;
-    alloc_n<double>(r, n_local);
-    alloc_n<double>(pw, wl);
-    alloc_n<double>(ap, n_local);
-    alloc_n<double>(partial, kDotCtas);
-    alloc_n<double>(scal, 8);
+    CgWorkspace& ws = cg_workspace(d ? d->cg_ws : plans[0]->cg_ws, n_local, wl);
+    DevBuf &r = ws.r, &pw = ws.pw, &ap = ws.ap, &partial = ws.partial, &scal = ws.scal;
     double* p = pw.as<double>() + p_off;
     CUDA_OK(cudaMemsetAsync(pw.p, 0, static_cast<size_t>(wl) * 8, s));
     CUDA_OK(cudaMemsetAsync(x, 0, static_cast<size_t>(n_local) * 8, s));

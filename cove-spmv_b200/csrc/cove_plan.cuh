@@ -35,6 +35,15 @@ void block_row_col_bounds(const cove_plan* P, std::vector<int32_t>* lo, std::vec
 
 }  // namespace cove
 
+namespace cove {
+// Work vectors of a CG solve (r, the p window, Ap, dot partials, scalars),
+// allocated by the first solve and reused while the sizes stay the same.
+struct CgWorkspace {
+    DevBuf r, pw, ap, partial, scal;
+    int64_t n = -1, wl = -1;
+};
+}  // namespace cove
+
 struct cove_plan {
     cove_plan_opts opts{};
     int dtype = COVE_F64;
@@ -77,6 +86,8 @@ struct cove_plan {
 
     // host-call staging of x and y (cove_spmv_host)
     cove::DevBuf x_stage, y_stage;
+    // CG work vectors, kept between solves on this plan (cove_cg_solve)
+    mutable cove::CgWorkspace cg_ws;
     std::unique_ptr<cove::HostPipeline> pipe;
 
     cove::KernelShape shape() const;

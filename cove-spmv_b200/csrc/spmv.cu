@@ -563,8 +563,9 @@ bfp8_block_lane_kernel(const KernelShape k, Bfp8Dec<T> dec, const T* __restrict_
         const int total = __shfl_sync(0xffffffffu, incl, 31);
         const int base = vb & ~15;
         const int nch = (vb + total - base + 15) >> 4;
+        // (a plain load: the read-only form makes ptxas keep 16 more registers)
         for (int c = lane; c < nch; c += 32)
-            reinterpret_cast<uint4*>(stage[wp])[c] = __ldg(reinterpret_cast<const uint4*>(dec.kept + base) + c);
+            reinterpret_cast<uint4*>(stage[wp])[c] = reinterpret_cast<const uint4*>(dec.kept + base)[c];
         __syncwarp();
         if (bm) {
             const float sc = dec.block_ctx(j);

@@ -399,6 +399,9 @@ typedef struct {
  * {Ap = A p; alpha = rs / (p.Ap); x += alpha p; r -= alpha Ap;
  *  rs' = r.r; beta = rs'/rs; p = r + beta p}.  alpha and beta stay on the
  * device.  Single GPU; b, x device vectors of length rows (rows == cols).
+ * The work vectors (r, p, Ap: three n-vectors) are allocated by the first
+ * solve on a plan and kept in the plan for the next ones (freed with it), so
+ * solves on one plan must not overlap on the GPU.
  */
 COVE_API cove_status cove_cg_solve(const cove_plan* plan, const void* b, void* x, int32_t iters,
                           cove_cg_result* result, void* stream);
@@ -502,7 +505,8 @@ COVE_API int32_t cove_dist_halo_plan(int32_t rank, int32_t world, const int64_t*
 COVE_API cove_status cove_dist_halo(cove_dist* d, void* x_window, void* stream);
 
 /* Distributed CG over the partition; b and x are the local row blocks.
- * result->ms_spmv times the distributed SpMV (halo exchange included). */
+ * result->ms_spmv times the distributed SpMV (halo exchange included).  The
+ * work vectors are kept in the handle between solves (freed with it). */
 COVE_API cove_status cove_dist_cg_solve(cove_dist* d, const void* b_local, void* x_local, int32_t iters,
                                cove_cg_result* result, void* stream);
 
