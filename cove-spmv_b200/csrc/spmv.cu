@@ -5,15 +5,20 @@
 // (structural/src/main_gpu_csr_bitbsr_spmv.cu:517-634 lossless,
 // :755-860 joint/quantized) and the outlier correction (:967-979).
 //
-// Work split: one group of 8*SLOTS lanes owns one block row.  The group
-// loads G block words with one coalesced load, scans their popcounts for the
-// value bases and hands the blocks to the slots by shuffle; lane (s, r)
-// handles local row r of every SLOTS-th block: the four cells of a row
-// segment are contiguous in the value stream (bit order is row-major) and
-// the four x values are contiguous (two 16-byte loads).  The SLOTS lanes of
-// a row then stride its residual entries, the slots are reduced with
-// xor-shuffles and each row is stored once: no atomics, no zero-fill,
-// deterministic.
+// Work split (the plan picks one main-pass kernel from the matrix's shape):
+//  - hybrid_main_kernel: one group of 8*SLOTS lanes owns one block row.  The
+//    group loads G block words with one coalesced load, scans their
+//    popcounts for the value bases and hands the blocks to the slots by
+//    shuffle; lane (s, r) handles local row r of every SLOTS-th block: the
+//    four cells of a row segment are contiguous in the value stream (bit
+//    order is row-major) and the four x values are contiguous (two 16-byte
+//    loads).  The SLOTS lanes of a row then stride its residual entries and
+//    the slots are reduced with xor-shuffles.
+//  - hybrid_row_kernel: a lane owns whole rows (two of them) for matrices
+//    with few kept blocks per block row and short residual rows.
+//  - bfp8_block_lane_kernel: a lane owns a block, for the BFP8 routes of
+//    block-dense matrices.
+// Each row is stored once: no atomics, no zero-fill, deterministic.
 //
 // Block rows with more than `heavy_limit` kept blocks and residual rows
 // longer than `long_tau` are finished by a second launch (one warp per
