@@ -310,7 +310,10 @@ struct Bfp4Dec {
 
 // ---- main pass -----------------------------------------------------------------
 
-template <typename T, typename Dec, int SLOTS>
+// XVEC: x is 16-byte aligned and cols % 4 == 0, so a block's four x values
+// are two 16-byte loads (a compile-time choice: with a run-time flag both
+// paths stay in the loop and the kernel measured 6 % slower on FEM)
+template <typename T, typename Dec, int SLOTS, bool XVEC>
 __global__ void __launch_bounds__(kThreads)
 hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y) {
     dec.prepare(g_smem);
@@ -337,7 +340,6 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
             dec.prefetch_values(vb, k.kept_brvp[br + 1]);
         }
     }
-    const bool vec_x = k.x_vec_ok;
     const uint32_t lowmask = (1u << (4 * r)) - 1u;
     Acc sum = Acc(0);
 
@@ -394,7 +396,7 @@ hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __r
                 const Acc ctx = dec.block_ctx(batch + j);
                 int v0 = vblk + __popc(bm & lowmask);
                 Acc xs[4];
-                load_x4<Acc, T>(x, c4, vec_x, nib, xs);
+                load_x4<Acc, T>(x, c4, XVEC, nib, xs);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if (nib & (1u << c)) {
@@ -745,7 +747,11 @@ void launch_main(const KernelShape& k, const Dec& dec, int smem, const T* x, T* 
     } else {
         constexpr int G = 8 * SLOTS;
         const int grid = grid_for(static_cast<int64_t>(k.nbr) - k.br_begin, kThreads / G);
-        hybrid_main_kernel<T, Dec, SLOTS><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+        if (k.x_vec_ok) {
+            hybrid_main_kernel<T, Dec, SLOTS, true><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+        } else {
+            hybrid_main_kernel<T, Dec, SLOTS, false><<<grid, kThreads, smem, s>>>(k, dec, x, y);
+        }
     }
     CUDA_LAUNCH_OK();
 }
