@@ -40,6 +40,7 @@ struct KernelShape {
     int long_tau = 0;                     // residual rows longer than this go to chunks
     bool x_vec_ok = false;                // set per launch: x 16-byte aligned, cols % 4 == 0
     bool l2_prefetch = false;             // plan buffers: aligned with tail slack, bulk L2 prefetch allowed
+    int32_t kb_avg = 0;                   // kept blocks per block row (whole plan, rounded down)
     // overflow tasks (second launch)
     int64_t num_heavy = 0;
     const int32_t* heavy_br = nullptr;

@@ -303,6 +303,7 @@ cove::KernelShape cove_plan::shape() const {
     k.res_col = sp.res_col.as<int32_t>();
     k.slots = slots;
     k.l2_prefetch = true;  // DevBuf: cudaMalloc alignment and kTailSlack
+    k.kb_avg = nbr > 0 ? static_cast<int32_t>(sp.kept_blocks / nbr) : 0;
     k.heavy_limit = heavy_limit;
     k.long_tau = long_tau;
     k.num_heavy = num_heavy;

@@ -311,6 +311,36 @@ def test_blocksparse_outlier_config_scaled(codec):
     assert O.compare_vectors(ref, y)[2] <= bound
 
 
+@pytest.mark.parametrize("dtype", ["f64", "f32"])
+@pytest.mark.parametrize("codec", ["bfp8", "bfp8_outlier"])
+def test_bfp8_long_block_rows(codec, dtype):
+    """Block rows of more than 64 kept blocks (several 32-block batches each)
+    take the segment-decoding BFP8 kernel: its output equals the oracle's
+    emulation of the same codes within fp32 summation noise, for x read as
+    32-byte, 16-byte and element loads (three alignments of the same x)."""
+    import torch
+
+    rows, cols, rp, ci, v = cb.synth_blocksparse(1 << 14, p_block=0.03, outlier_fraction=0.002, seed=5)
+    if dtype == "f32":
+        v = v.astype(np.float32)
+    p = plan_for(rows, cols, rp, ci, v, value_codec=codec, long_row_split=256)
+    assert p.info.kept_blocks >= 64 * ((rows + 7) // 8)  # the segment kernel's rule
+    frac = 0.005 if codec == "bfp8_outlier" else None
+    x = cb.synth_vector("normal", cols, seed=3).astype(v.dtype)
+    ye = _joint_oracle(rows, cols, rp, ci, v, x, frac)
+    scale = max(np.abs(ye).max(), 1e-30)
+    tdt = torch.float64 if v.dtype == np.float64 else torch.float32
+    for off in (0, 1, 2, 4):  # elements past a 512-byte aligned allocation
+        buf = torch.zeros(cols + 8, dtype=tdt, device="cuda")
+        xd = buf[off:off + cols]
+        xd.copy_(torch.from_numpy(x))
+        yd = torch.full((rows,), float("nan"), dtype=tdt, device="cuda")
+        p.spmv(xd, yd, route=p.info.joint_route)
+        torch.cuda.synchronize()
+        y = yd.cpu().numpy().astype(np.float64)
+        assert np.abs(ye - y).max() / scale <= 2e-6, off
+
+
 def test_auto_route_choice_matches_reference_rule():
     # uniq <= 256 -> dict_u8; > 256 -> bfp8 (main_gpu_csr_bitbsr_spmv.cu:1244-1245)
     rows, cols, rp, ci, v = cb.synth_lapl2d(64, 64)
