@@ -924,6 +924,8 @@ def run_blocksparse(args):
         hbm, peak_kind = peaks()
         alg = int(alg_total / world)  # per GPU
         achieved = alg / (ms_all * 1e-3) / 1e9
+        tr = load_traffic("blocksparse", cb.ROUTE_NAMES[route])
+        traffic = int(round(tr["bytes"] * (nnz_total / world) / tr["nnz"])) if tr and tr.get("nnz") else None
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             # bounded sample: the first 32,768 rows (~8e7 nnz) through the reference's spmv_csr
@@ -948,7 +950,9 @@ def run_blocksparse(args):
                        "parity_rel_sampled_rows": rel_all},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "algorithmic_bytes": alg,
-                         "traffic": None},
+                         "traffic": traffic,
+                         "traffic_source": (f"ncu DRAM bytes of one main-pass launch on {tr['case']}, scaled by "
+                                            f"nnz to a rank's plans (profiles/traffic.json)") if traffic else None},
             "cpu_baseline": cpu,
             "e2e": {"value": round(2.0 * nnz_total / (e2e_all * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
                     "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": (re - rb) * 8},
