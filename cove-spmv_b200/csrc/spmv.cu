@@ -89,6 +89,21 @@ __device__ __forceinline__ void load_x4(const T* __restrict__ x, int64_t c4, boo
     for (int c = 0; c < 4; ++c) out[c] = (nib & (1u << c)) ? static_cast<Acc>(__ldg(x + c4 + c)) : Acc(0);
 }
 
+// The four fp64 x values of a block column as one 32-byte read-only load
+// (x 32-byte aligned, cols a multiple of 4).
+template <typename Acc, typename T>
+__device__ __forceinline__ void load_x4_32(const T* __restrict__ x, int64_t c4, Acc* out) {
+    static_assert(sizeof(T) == 8, "32-byte x loads are for fp64 x");
+    double d0, d1, d2, d3;
+    asm("ld.global.nc.v4.f64 {%0, %1, %2, %3}, [%4];"
+        : "=d"(d0), "=d"(d1), "=d"(d2), "=d"(d3)
+        : "l"(x + c4));
+    out[0] = static_cast<Acc>(d0);
+    out[1] = static_cast<Acc>(d1);
+    out[2] = static_cast<Acc>(d2);
+    out[3] = static_cast<Acc>(d3);
+}
+
 // Hint: start pulling [p, p + bytes) into L2 before the dependent loads ask
 // for it.  The range is widened to 16-byte bounds; plan buffers are
 // 256-byte aligned and carry tail slack, so it stays inside the allocation.
@@ -315,7 +330,8 @@ struct Bfp4Dec {
 
 // XVEC: x is 16-byte aligned and cols % 4 == 0, so a block's four x values
 // are two 16-byte loads (a compile-time choice: with a run-time flag both
-// paths stay in the loop and the kernel measured 6 % slower on FEM)
+// paths stay in the loop and the kernel measured 6 % slower on FEM; one
+// 32-byte load instead: 0.131 -> 0.134-0.136 ms on FEM at 32-40 registers)
 template <typename T, typename Dec, int SLOTS, bool XVEC>
 __global__ void __launch_bounds__(kThreads)
 hybrid_main_kernel(const KernelShape k, Dec dec, const T* __restrict__ x, T* __restrict__ y) {
@@ -739,14 +755,7 @@ bfp8_segment_kernel(const KernelShape k, Bfp8Dec<T> dec, const T* __restrict__ x
             const int64_t c4 = static_cast<int64_t>(w & 0x7fffffffULL) * 4;
             float xq[4];
             if constexpr (XM == 2) {
-                double d0, d1, d2, d3;
-                asm volatile("ld.global.nc.v4.f64 {%0, %1, %2, %3}, [%4];"
-                             : "=d"(d0), "=d"(d1), "=d"(d2), "=d"(d3)
-                             : "l"(x + c4));
-                xq[0] = static_cast<float>(d0);
-                xq[1] = static_cast<float>(d1);
-                xq[2] = static_cast<float>(d2);
-                xq[3] = static_cast<float>(d3);
+                load_x4_32<float, T>(x, c4, xq);
             } else if constexpr (XM == 1) {
                 load_x4<float, T>(x, c4, true, 0xFu, xq);
             } else {  // only the columns a present cell reads (the last block may pass cols)
