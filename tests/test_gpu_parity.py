@@ -341,6 +341,43 @@ def test_bfp8_long_block_rows(codec, dtype):
         assert np.abs(ye - y).max() / scale <= 2e-6, off
 
 
+@pytest.mark.parametrize("codec", ["bfp8", "bfp8_outlier"])
+def test_bfp8_long_block_rows_heavy_and_ragged(codec):
+    """The segment-decoding BFP8 kernel with a ragged last block row (n not a
+    multiple of 8) and one block row of 3000 kept blocks, beyond the heavy
+    limit, whose tail the overflow launch finishes: output equals the
+    oracle's emulation of the same codes within fp32 summation noise."""
+    rng = np.random.default_rng(7)
+    rows, cols, rp, ci, v = cb.synth_blocksparse(16387, p_block=0.03, outlier_fraction=0.002, seed=7)
+    heavy = range(800, 808)  # block row 100
+    blocks = np.sort(rng.choice((cols + 3) // 4, 3000, replace=False))
+    cells = (blocks[:, None] * 4 + np.arange(4)[None, :]).ravel()
+    cells = cells[cells < cols]
+    new_rp, new_ci, new_v = [0], [], []
+    for r in range(rows):
+        if r in heavy:
+            c = np.sort(cells[rng.random(cells.size) < 0.6]).astype(np.int32)
+            val = rng.integers(1, 64, c.size) * rng.choice([-0.125, 0.125], c.size)  # bf16-exact, nonzero
+        else:
+            c, val = ci[rp[r]:rp[r + 1]], v[rp[r]:rp[r + 1]]
+        new_ci.append(c)
+        new_v.append(val)
+        new_rp.append(new_rp[-1] + c.size)
+    rp = np.array(new_rp, np.int64)
+    ci = np.concatenate(new_ci).astype(np.int32)
+    v = np.concatenate(new_v).astype(np.float64)
+    x = cb.synth_vector("normal", cols, seed=3)
+    frac = 0.005 if codec == "bfp8_outlier" else None
+    for dt in (np.float64, np.float32):
+        vv, xx = v.astype(dt), x.astype(dt)
+        p = plan_for(rows, cols, rp, ci, vv, value_codec=codec, long_row_split=256, gate_enable=0)
+        assert p.info.kept_blocks >= 64 * ((rows + 7) // 8)  # the segment kernel's rule
+        assert p.info.kernel_overflow_tasks > 0  # the heavy block row's tail
+        ye = _joint_oracle(rows, cols, rp, ci, vv, xx, frac)
+        y = gpu_spmv(p, xx, route=p.info.joint_route).astype(np.float64)
+        assert np.abs(ye - y).max() / max(np.abs(ye).max(), 1e-30) <= 2e-6, dt
+
+
 def test_auto_route_choice_matches_reference_rule():
     # uniq <= 256 -> dict_u8; > 256 -> bfp8 (main_gpu_csr_bitbsr_spmv.cu:1244-1245)
     rows, cols, rp, ci, v = cb.synth_lapl2d(64, 64)
