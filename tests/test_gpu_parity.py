@@ -707,6 +707,24 @@ def test_spmv_host_sliced_overlap_matches_device(long_row):
     assert np.array_equal(p.spmv_host(x), yd) or long_row  # pageable buffers: one-shot path
 
 
+def test_spmv_host_sliced_segment_kernel_matches_device():
+    """The host path's block-row slices run the segment-decoding BFP8 kernel
+    from each slice's first block row: the same rows, bit for bit."""
+    rows, cols, rp, ci, v = cb.synth_blocksparse(1 << 18, outlier_fraction=0.0)  # 131 kept blocks a block row
+    p = plan_for(rows, cols, rp, ci, v, value_codec="bfp8", long_row_split=256, gate_enable=0)
+    assert p.info.kept_blocks >= 64 * ((rows + 7) // 8)
+    assert p.info.dispatched_route == cb.ROUTE_BFP8 and p.launches() == 1
+    x = cb.synth_vector("normal", cols, seed=3)
+    yd = gpu_spmv(p, x)
+    xh = _pinned(cols)
+    xh[:] = x
+    for _ in range(2):
+        yh = _pinned(rows)
+        yh[:] = np.nan
+        p.spmv_host(xh, yh)
+        assert np.array_equal(yh, yd)
+
+
 @pytest.mark.parametrize("cfg", ["lapl2d_512", "fem27_64", "rmat_22"])
 def test_full_size_configs(cfg):
     """2D Laplacian 512^2, FEM 27-point 64^3 and R-MAT 2^22 at full size:
