@@ -208,17 +208,16 @@ def reference_sample(args):
         rp, ci, v = O.lapl2d(512, 512)
         x = O.vector("uniform_pm1", 0, 7, 0, 512 * 512)
         return 512 * 512, 512 * 512, rp, ci, v, x, "the whole matrix"
-    # R-MAT and block-sparse inputs come from the library's host generators
-    import cove_b200 as cb
-
     if args.workload == "rmat_22":
-        rows, n, rp, ci, v, x = cb.workload("rmat_22")
-        return rows, n, rp, ci, v, x, "the whole matrix"
+        rp, ci, v = O.rmat(22, 16, seed=2)
+        n = 1 << 22
+        x = O.vector("uniform01", 2, 7, 0, n).astype(np.float32)
+        return n, n, rp, ci, v, x, "the whole matrix"
     bs = BLOCKSPARSE
     n = args.bs_n or bs["n"]
-    rp, ci, v = cb.synth_blocksparse_rows(n, 0, min(n, 32768), bs["p_block"], bs["p_entry"],
-                                          bs["outlier_fraction"], bs["seed"])
-    x = cb.synth_vector("normal", n, seed=bs["seed"])
+    rp, ci, v = O.blocksparse_rows(n, 0, min(n, 32768), bs["p_block"], bs["p_entry"],
+                                   bs["outlier_fraction"], bs["seed"])
+    x = O.vector("normal", bs["seed"], 7, 0, n)
     return len(rp) - 1, n, rp, ci, v, x, f"rows [0, {len(rp) - 1}) ({ci.size} nnz)"
 
 
@@ -929,7 +928,7 @@ def run_blocksparse(args):
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             # bounded sample: the first 32,768 rows (~8e7 nnz) through the reference's spmv_csr
-            srp, sci, sv = cb.synth_blocksparse_rows(n, 0, min(n, 32768), *gen)
+            srp, sci, sv = _oracle().blocksparse_rows(n, 0, min(n, 32768), *gen)
             cms, cores, kind = cpu_reference_time(len(srp) - 1, n, srp, sci, sv, x_host, 5)
             cpu = {"value": round(2.0 * len(sv) / (cms * 1e-3) / 1e9, 3), "unit": "GFLOP/s", "cores": cores,
                    "kind": kind, "sample": f"best of 5 SpMVs of rows [0, {len(srp) - 1}) ({len(sv)} nnz)"}

@@ -118,6 +118,10 @@ def _setup(L):
     L.oc_write_mtx.restype = C.c_int
     L.oc_write_mtx.argtypes = [C.c_char_p, i64, i64, vp, vp, vp, i32]
     L.oc_fem27_rows.argtypes = [i32, i32, i32, i32, u64, i64, i64, i64, vp, vp, vp]
+    L.oc_blocksparse_rows.restype = i64
+    L.oc_blocksparse_rows.argtypes = [i32, f64, f64, f64, u64, i64, i64, vp, vp, vp]
+    L.oc_rmat.restype = i64
+    L.oc_rmat.argtypes = [i32, i32, f64, f64, f64, u64, vp, vp, vp]
 
 
 def _setup_ref(R):
@@ -609,6 +613,35 @@ def fem27_rows(nx, ny, nz, dof, seed, row_begin, row_end, col_shift=0):
                     lambda a, b, c: L.oc_fem27_rows(nx, ny, nz, dof, seed, row_begin, row_end, col_shift,
                                                     a, b, c),
                     row_end - row_begin)
+
+
+def blocksparse_rows(n, row_begin, row_end, p_block=2e-3, p_entry=0.6, outlier_fraction=1e-3, seed=3):
+    """Rows [row_begin, row_end) of the random 8x4 block-sparse n x n matrix
+    (row_ptr relative to row_begin, global columns): (rp, ci, v)."""
+    L = _lib()
+    args = (n, p_block, p_entry, outlier_fraction, seed, row_begin, row_end)
+    nnz = L.oc_blocksparse_rows(*args, None, None, None)
+    if nnz < 0:
+        raise ValueError("block-sparse rows must start and end on whole 8-row block rows")
+    rp = np.zeros(row_end - row_begin + 1, np.int64)
+    ci = np.empty(nnz, np.int32)
+    v = np.empty(nnz, np.float64)
+    L.oc_blocksparse_rows(*args, _p(rp), _p(ci), _p(v))
+    return rp, ci, v
+
+
+def rmat(scale, edge_factor=16, a=0.57, b=0.19, c=0.19, seed=2):
+    """The R-MAT graph with 2^scale rows and float values: (rp, ci, v)."""
+    L = _lib()
+    n = 1 << scale
+    nnz = L.oc_rmat(scale, edge_factor, a, b, c, seed, None, None, None)
+    if nnz < 0:
+        raise MemoryError("R-MAT generation failed")
+    rp = np.zeros(n + 1, np.int64)
+    ci = np.empty(nnz, np.int32)
+    v = np.empty(nnz, np.float32)
+    L.oc_rmat(scale, edge_factor, a, b, c, seed, _p(rp), _p(ci), _p(v))
+    return rp, ci, v
 
 
 def write_mtx(path, rows, cols, row_ptr, col_idx, values):

@@ -39,3 +39,18 @@ def test_vectors_match():
         ref = cb.synth_vector(kind, 5000, seed=seed)
         assert np.array_equal(O.vector(kind, seed, 7, 0, 5000), ref)
         assert np.array_equal(O.vector(kind, seed, 7, 1234, 100), ref[1234:1334])
+
+
+def test_blocksparse_rows_match():
+    g = dict(p_block=0.05, p_entry=0.6, outlier_fraction=0.01, seed=11)
+    for (n, rb, re) in ((4099, 0, 4099), (4099, 1024, 2048), (4099, 4096, 4099), (1 << 14, 8, 4000)):
+        rp, ci, v = cb.synth_blocksparse_rows(n, rb, re, **g)
+        _same(O.blocksparse_rows(n, rb, re, **g), (rp, ci, v))
+    rows, _, rp, ci, v = cb.synth_blocksparse(1 << 14)  # the bench's default densities, scaled
+    _same(O.blocksparse_rows(1 << 14, 0, 1 << 14), (rp, ci, v))
+
+
+def test_rmat_matches():
+    for scale, ef in ((10, 16), (14, 8)):
+        _, _, rp, ci, v = cb.synth_rmat(scale, ef, seed=2)
+        _same(O.rmat(scale, ef, seed=2), (rp, ci, v))
