@@ -38,6 +38,7 @@ import subprocess
 import sys
 import threading
 import time
+import warnings
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "cove-spmv_b200"))
@@ -426,8 +427,11 @@ def run_fem(args):
     # vendor library context: cuSPARSE CSR SpMV (through torch) of the same matrix
     vendor_ms = None
     try:
-        A_csr = torch.sparse_csr_tensor(torch.from_numpy(rp.astype(np.int64)), torch.from_numpy(ci.astype(np.int64)),
-                                        torch.from_numpy(v), size=(rows, wl), device=dev)
+        with warnings.catch_warnings():  # torch's beta-state notes on sparse CSR tensors
+            warnings.simplefilter("ignore", UserWarning)
+            A_csr = torch.sparse_csr_tensor(torch.from_numpy(rp.astype(np.int64)),
+                                            torch.from_numpy(ci.astype(np.int64)),
+                                            torch.from_numpy(v), size=(rows, wl), device=dev)
         xv = xw.view(-1, 1)
         for _ in range(3):
             A_csr.matmul(xv)
